@@ -1,0 +1,416 @@
+#!/usr/bin/env python
+"""Benchmark of the persistent micro-op runtime on the reference's headline workload.
+
+Workload (one step = one flush): 4096 independent fp32 requests of 4096 contiguous
+elements each, a, b ~ U(-1, 1) from a fixed seed, op 50/50 add/mul, a separate output
+buffer per request, submitted with submit_add / submit_mul and one flush(sync=True).
+Inputs + outputs are 201 MB per step (> 126 MB L2), so every step streams from HBM.
+
+Printed JSON line (rank 0):
+  value     micro-ops/s of the whole job, inputs resident in HBM, timed with CUDA events
+            on the current stream around K steps (submit calls included), max over ranks,
+            summed over ranks (weak scaling: every rank runs the full workload on its GPU)
+  e2e       the same through the public API with host (pinned) buffers: H2D of a and b and
+            D2H of out inside every step
+  roofline  the worker kernel: algorithmic bytes (12 B per element) / launch duration,
+            launches timed with CUDA events on the worker's stream in drain mode (one launch
+            per flush), against MEASURED_PEAKS.json hbm_gbs
+  baselines GPU per-op torch eager (same stream of requests as individual launches) and
+            the CPU path (PyTorch CPU eager over the same requests on the host cores)
+  latency   p50/p99 submit->done of single 4096-element requests (sync flush each)
+
+--impl reference runs the reference's CPU path (PyTorch CPU eager over the identical
+request stream, all host threads) and prints the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "aggregated micro-ops/s"
+UNIT = "micro-ops/s"
+WORKLOAD = "4096 fp32 requests x 4096 contiguous elements, add/mul 50/50, one flush per step"
+BYTES_PER_ELEM = 12  # read a, read b, write out (fp32)
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--requests", type=int, default=4096)
+    p.add_argument("--numel", type=int, default=4096)
+    p.add_argument("--worker-mode", choices=["persistent", "drain"], default="persistent")
+    p.add_argument("--no-extras", action="store_true", help="skip baselines, latency, e2e (profiling runs)")
+    p.add_argument("--cpu-seconds", type=float, default=10.0)
+    p.add_argument("--latency-samples", type=int, default=2000)
+    return p.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def workload(rank: int, R: int, N: int):
+    g = torch.Generator().manual_seed(1234 + 1 + rank)
+    A = torch.rand(R, N, generator=g) * 2 - 1
+    B = torch.rand(R, N, generator=g) * 2 - 1
+    ops = torch.randint(0, 2, (R,), generator=g)
+    return A, B, ops
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                self.samples.append(parts)
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for s in self.samples for k in range(4) if s[5 + k].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+_CPU = {}
+
+
+def _cpu_init(A, B, out, ops):
+    torch.set_num_threads(1)
+    _CPU.update(A=A, B=B, out=out, ops=ops)
+
+
+def _cpu_slice(bounds):
+    lo, hi = bounds
+    A, B, out, ops = _CPU["A"], _CPU["B"], _CPU["out"], _CPU["ops"]
+    for i in range(lo, hi):
+        if ops[i] == 0:
+            torch.add(A[i], B[i], out=out[i])
+        else:
+            torch.mul(A[i], B[i], out=out[i])
+    return hi - lo
+
+
+class CpuPath:
+    """The request stream in PyTorch CPU eager, split over `procs` host processes (spawned,
+    tensors in shared memory; Python threads would serialise on the GIL)."""
+
+    def __init__(self, A, B, out, ops, procs: int):
+        self.procs = procs
+        R = A.shape[0]
+        self.chunks = [(k * R // procs, (k + 1) * R // procs) for k in range(procs)]
+        if procs > 1:
+            for t in (A, B, out):
+                t.share_memory_()
+            ctx = torch.multiprocessing.get_context("spawn")
+            self.pool = ctx.Pool(procs, initializer=_cpu_init, initargs=(A, B, out, ops))
+        else:
+            _cpu_init(A, B, out, ops)
+            self.pool = None
+
+    def run(self):
+        if self.pool is None:
+            _cpu_slice(self.chunks[0])
+        else:
+            self.pool.map(_cpu_slice, self.chunks)
+
+    def close(self):
+        if self.pool is not None:
+            self.pool.close()
+            self.pool.join()
+
+
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def run_reference(args, rank, world):
+    """The reference's CPU path: PyTorch CPU eager over the identical request stream."""
+    if rank != 0:
+        return None
+    import oracle.reference_semantics  # noqa: F401  (CPU path lives with the oracle)
+    threads = cpu_threads()
+    A, B, ops = workload(0, args.requests, args.numel)
+    out = torch.empty_like(A)
+    cpu = CpuPath(A, B, out, ops.tolist(), threads)
+    for _ in range(args.warmup):
+        cpu.run()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu.run()
+    dt = time.perf_counter() - t0
+    cpu.close()
+    ok = torch.equal(out, torch.where(ops[:, None] == 0, A + B, A * B))
+    v = args.requests * args.steps / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded U(-1,1))",
+        "config": {"workload": WORKLOAD, "requests": args.requests, "numel": args.numel, "l2": "inputs > L2"},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} steps x {args.requests} requests (full workload)"},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "correct": bool(ok),
+    }
+    return line
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.cuda.current_device()
+    from gpuos_b200 import gpuos_ext as g
+
+    R, N = args.requests, args.numel
+    A, B, ops = workload(rank, R, N)
+    a, b = A.cuda(), B.cuda()
+    out = torch.empty_like(a)
+    a_rows, b_rows, o_rows = list(a.unbind(0)), list(b.unbind(0)), list(out.unbind(0))
+    subs = [g.submit_add if int(o) == 0 else g.submit_mul for o in ops]
+    torch.cuda.synchronize()
+
+    g.init(capacity=8192, threads_per_block=256)
+    if args.worker_mode == "drain":
+        g.set_idle_quiesce_ms(0)
+
+    def step():
+        for i in range(R):
+            subs[i](a_rows[i], b_rows[i], o_rows[i])
+        return g.flush(sync=True)
+
+    def barrier():
+        if dist is not None:
+            g.quiesce()
+            torch.cuda.synchronize()
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        g.quiesce()
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    ref = torch.where(ops[:, None] == 0, A + B, A * B)
+    correct = bool(torch.equal(out.cpu(), ref))
+
+    # ---- value: whole job, inputs resident in HBM ----
+    g.quiesce()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = Clocks(dev)
+    clocks.start()
+    n_launch0 = g.launches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    seqs = [step() for _ in range(args.steps)]
+    e1.record()
+    e1.synchronize()
+    clk = clocks.stop()
+    launches = g.launches() - n_launch0
+    elapsed_ms = max_over_ranks(e0.elapsed_time(e1))
+    value = R * args.steps * world / (elapsed_ms / 1e3)
+    dev_ns = []
+    for s in seqs:
+        try:
+            t0, t1 = g.flush_times(s)
+            dev_ns.append(t1 - t0)
+        except Exception:
+            pass
+    flush_dev_ms = statistics.median(dev_ns) / 1e6 if dev_ns else None
+    peak, peak_kind = peaks()
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded U(-1,1))",
+        "config": {"workload": WORKLOAD, "requests": R, "numel": N, "worker_mode": args.worker_mode,
+                   "l2": "inputs larger than L2 (201 MB per step)", "parallelism": f"dp{world} (independent request streams)"},
+        "gpu_launches": launches, "clocks": clk, "correct": correct,
+        "persistent_flush_device_ms": flush_dev_ms,
+        "persistent_flush_hbm_gbs": (R * N * BYTES_PER_ELEM / (flush_dev_ms * 1e-3) / 1e9) if flush_dev_ms else None,
+    }
+
+    if not args.no_extras:
+        # ---- roofline: worker launches timed with CUDA events on the worker's stream ----
+        g.set_idle_quiesce_ms(0)
+        g.quiesce()
+        ks = torch.cuda.ExternalStream(g.kernel_stream())
+        durs = []
+        for k in range(max(5, args.steps // 2)):
+            for i in range(R):
+                subs[i](a_rows[i], b_rows[i], o_rows[i])
+            ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ea.record(ks)
+            g.flush(sync=True)
+            eb.record(ks)
+            eb.synchronize()
+            if k > 0:
+                durs.append(ea.elapsed_time(eb))
+        g.set_idle_quiesce_ms(200 if args.worker_mode == "persistent" else 0)
+        kms = statistics.mean(durs)
+        achieved = R * N * BYTES_PER_ELEM / (kms * 1e-3) / 1e9
+        line["roofline"] = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                            "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
+                            "kernel": "gpuos_batch_worker", "launch_ms": kms,
+                            "algorithmic_bytes_per_launch": R * N * BYTES_PER_ELEM}
+
+        # ---- e2e: host buffers, H2D + D2H inside every step ----
+        hA, hB = A.pin_memory(), B.pin_memory()
+        hO = torch.empty_like(hA).pin_memory()
+        g.quiesce()
+        barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        for _ in range(args.steps):
+            a.copy_(hA, non_blocking=True)
+            b.copy_(hB, non_blocking=True)
+            for i in range(R):
+                subs[i](a_rows[i], b_rows[i], o_rows[i])
+            g.flush(sync=True)
+            hO.copy_(out, non_blocking=True)
+        f1.record()
+        f1.synchronize()
+        e2e_ms = max_over_ranks(f0.elapsed_time(f1))
+        line["e2e"] = {"value": R * args.steps * world / (e2e_ms / 1e3), "unit": UNIT,
+                       "h2d_bytes_per_step": 2 * R * N * 4, "d2h_bytes_per_step": R * N * 4,
+                       "correct": bool(torch.equal(hO, ref))}
+
+        # ---- latency: single 4096-element requests, sync flush each ----
+        g.set_idle_quiesce_ms(200)
+        lat = []
+        x1, y1, z1 = a_rows[0], b_rows[0], o_rows[0]
+        for k in range(args.latency_samples + 50):
+            t0 = time.perf_counter_ns()
+            g.submit_add(x1, y1, z1)
+            g.flush(sync=True)
+            t1 = time.perf_counter_ns()
+            if k >= 50:
+                lat.append((t1 - t0) / 1e3)
+        lat.sort()
+        line["latency_us"] = {"p50": lat[len(lat) // 2], "p99": lat[int(len(lat) * 0.99)],
+                              "load": "one 4096-element request per sync flush, back to back"}
+
+        # ---- baseline (b): GPU per-op torch eager ----
+        g.quiesce()
+        torch.cuda.synchronize()
+        ops_l = ops.tolist()
+        for _ in range(2):
+            for i in range(R):
+                (torch.add if ops_l[i] == 0 else torch.mul)(a_rows[i], b_rows[i], out=o_rows[i])
+        h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ke = max(3, args.steps // 2)
+        h0.record()
+        for _ in range(ke):
+            for i in range(R):
+                (torch.add if ops_l[i] == 0 else torch.mul)(a_rows[i], b_rows[i], out=o_rows[i])
+        h1.record()
+        h1.synchronize()
+        eager = R * ke / (h0.elapsed_time(h1) / 1e3)
+        line["baseline_gpu_eager"] = {"value": eager * world, "unit": UNIT,
+                                      "what": "same requests as individual torch.add/mul(out=) launches"}
+        line["speedup_vs_gpu_eager"] = value / (eager * world)
+
+        # ---- CPU path (rank 0, single GPU run only) ----
+        if rank == 0 and world == 1:
+            threads = cpu_threads()
+            cpu = CpuPath(A.clone(), B.clone(), torch.empty_like(A), ops_l, threads)
+            cpu.run()
+            steps = 0
+            t0 = time.perf_counter()
+            while True:
+                cpu.run()
+                steps += 1
+                if time.perf_counter() - t0 >= args.cpu_seconds:
+                    break
+            dt = time.perf_counter() - t0
+            cpu.close()
+            line["cpu_baseline"] = {"value": R * steps / dt, "unit": UNIT, "cores": threads, "kind": "port",
+                                    "sample": f"{steps} steps x {R} requests in {dt:.1f} s (PyTorch CPU eager)"}
+    g.shutdown()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

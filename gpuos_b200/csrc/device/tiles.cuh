@@ -1,0 +1,278 @@
+// tiles.cuh — per-item compute bodies of the batched path.
+//
+// The reference aggregates sub-tasks in one device function that one CTA walks
+// serially, decoding every element with three int64 stride walks
+// (src/persistent_kernel.cu:20-31, 81-112).  Here each work item is one tile; the
+// dequeue warp has staged its contiguous operands in shared memory with a TMA bulk
+// copy, and the compute warps run one tile function reached through a device
+// function-pointer table (one indirect call per tile, not per element).
+#pragma once
+#include "ptx.cuh"
+#include "ops.cuh"
+
+namespace gpuos {
+
+struct TileCtx {
+  const StageMeta* m;
+  const unsigned char* sa;  // stage buffer for operand a (shared memory)
+  const unsigned char* sb;  // stage buffer for operand b (shared memory)
+  uint32_t tid;             // compute-thread index
+  uint32_t nt;              // compute-thread count (multiple of 32)
+};
+typedef void (*TileFn)(const TileCtx&);
+
+__device__ __forceinline__ float item_p0(const WorkItem& it) { return __uint_as_float((uint32_t)it.x); }
+__device__ __forceinline__ float item_p1(const WorkItem& it) { return __uint_as_float((uint32_t)(it.x >> 32)); }
+
+template <int OP>
+__device__ __forceinline__ float4 ew_apply4(float4 a, float4 b, float p0, float p1) {
+  return make_float4(ew_apply<OP>(a.x, b.x, p0, p1), ew_apply<OP>(a.y, b.y, p0, p1),
+                     ew_apply<OP>(a.z, b.z, p0, p1), ew_apply<OP>(a.w, b.w, p0, p1));
+}
+
+// ---- 16-bit vector helpers: 8 elements per 16 bytes ----------------------------------
+__device__ __forceinline__ void unpack8(uint4 raw, int dt, float* f) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    if (dt == kF16) {
+      __half2 h = *reinterpret_cast<const __half2*>(&w[k]);
+      float2 v = __half22float2(h);
+      f[2 * k] = v.x;
+      f[2 * k + 1] = v.y;
+    } else {
+      f[2 * k] = __uint_as_float(w[k] << 16);
+      f[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
+    }
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float* f, int dt) {
+  uint32_t w[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    if (dt == kF16) {
+      __half2 h = __floats2half2_rn(f[2 * k], f[2 * k + 1]);
+      w[k] = *reinterpret_cast<uint32_t*>(&h);
+    } else {
+      __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * k], f[2 * k + 1]);
+      w[k] = *reinterpret_cast<uint32_t*>(&h);
+    }
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Load 8 consecutive elements starting at element i (16-byte aligned for 16-bit
+// types, 32-byte span for fp32) as floats.
+__device__ __forceinline__ void load8(const unsigned char* base, int dt, uint32_t i, float* f) {
+  if (dt == kF32) {
+    const float4* p = reinterpret_cast<const float4*>(base) + 2 * (i >> 3);
+    float4 v0 = p[0], v1 = p[1];
+    f[0] = v0.x; f[1] = v0.y; f[2] = v0.z; f[3] = v0.w;
+    f[4] = v1.x; f[5] = v1.y; f[6] = v1.z; f[7] = v1.w;
+  } else {
+    uint4 raw = reinterpret_cast<const uint4*>(base)[i >> 3];
+    unpack8(raw, dt, f);
+  }
+}
+
+__device__ __forceinline__ void store8(unsigned char* base, int dt, uint32_t i, const float* f) {
+  if (dt == kF32) {
+    float4* p = reinterpret_cast<float4*>(base) + 2 * (i >> 3);
+    ptx::st_cs_v4(p, make_float4(f[0], f[1], f[2], f[3]));
+    ptx::st_cs_v4(p + 1, make_float4(f[4], f[5], f[6], f[7]));
+  } else {
+    uint4 v = pack8(f, dt);
+    asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(reinterpret_cast<uint4*>(base) + (i >> 3)),
+                 "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+  }
+}
+
+// ---- EW_CONTIG -------------------------------------------------------------------------
+template <int OP>
+__device__ __noinline__ void ew_contig(const TileCtx& c) {
+  const WorkItem& it = c.m->item;
+  const uint32_t n = it.count;
+  const float p0 = item_p0(it), p1 = item_p1(it);
+  const int dta = it.dt_a, dtb = it.dt_b, dto = it.dt_o;
+  const bool has_b = (it.flags & IF_B_PRESENT) != 0;
+  const bool b_imm = (it.flags & IF_B_SCALAR) != 0;
+  const bool a_bc = (it.flags & IF_A_BCAST) != 0;
+  const bool b_bc = (it.flags & IF_B_BCAST) != 0;
+  const unsigned char* A = (c.m->staged & 1) ? c.sa + c.m->a_off : reinterpret_cast<const unsigned char*>(it.a);
+  const unsigned char* B = (c.m->staged & 2) ? c.sb + c.m->b_off : reinterpret_cast<const unsigned char*>(it.b);
+  unsigned char* O = reinterpret_cast<unsigned char*>(it.o);
+
+  float bscal = 0.f;
+  if (has_b) {
+    if (b_imm) bscal = __uint_as_float((uint32_t)it.b);
+    else if (b_bc) bscal = ld_elem(B, dtb, 0);
+  }
+  const bool b_vec = has_b && !b_imm && !b_bc;
+  float ascal = a_bc ? ld_elem(A, dta, 0) : 0.f;
+
+  // Vector body: 8 elements per step when every vector operand is 16-byte aligned.
+  const bool a_al = a_bc || ((reinterpret_cast<uintptr_t>(A) & 15) == 0);
+  const bool b_al = !b_vec || ((reinterpret_cast<uintptr_t>(B) & 15) == 0);
+  const bool o_al = (reinterpret_cast<uintptr_t>(O) & 15) == 0;
+  uint32_t done = 0;
+  if (a_al && b_al && o_al) {
+    const uint32_t n8 = n >> 3;
+    if (dta == kF32 && dto == kF32 && (!b_vec || dtb == kF32) && !a_bc) {
+      // fp32 fast path: two float4 per step.
+      const float4* A4 = reinterpret_cast<const float4*>(A);
+      const float4* B4 = reinterpret_cast<const float4*>(B);
+      float4* O4 = reinterpret_cast<float4*>(O);
+      const float4 bsv = make_float4(bscal, bscal, bscal, bscal);
+      const uint32_t n4 = n >> 2;
+      for (uint32_t i = c.tid; i < n4; i += c.nt) {
+        float4 av = A4[i];
+        float4 bv = b_vec ? B4[i] : bsv;
+        ptx::st_cs_v4(O4 + i, ew_apply4<OP>(av, bv, p0, p1));
+      }
+      done = n4 << 2;
+    } else {
+      for (uint32_t v = c.tid; v < n8; v += c.nt) {
+        float fa[8], fb[8], fo[8];
+        if (a_bc) {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) fa[k] = ascal;
+        } else {
+          load8(A, dta, v << 3, fa);
+        }
+        if (b_vec) {
+          load8(B, dtb, v << 3, fb);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) fb[k] = bscal;
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) fo[k] = ew_apply<OP>(fa[k], fb[k], p0, p1);
+        store8(O, dto, v << 3, fo);
+      }
+      done = n8 << 3;
+    }
+  }
+  for (uint32_t i = done + c.tid; i < n; i += c.nt) {
+    float av = a_bc ? ascal : ld_elem(A, dta, i);
+    float bv = b_vec ? ld_elem(B, dtb, i) : bscal;
+    st_elem(O, dto, i, ew_apply<OP>(av, bv, p0, p1));
+  }
+}
+
+// ---- EW_GENERIC: strided / broadcast operands -----------------------------------------
+__device__ __noinline__ void ew_generic(const TileCtx& c) {
+  const int OP = c.m->item.op;
+  const WorkItem& it = c.m->item;
+  const Layout& L = c.m->ext.layout;
+  const int nd = L.ndim;
+  const bool has_b = (it.flags & IF_B_PRESENT) != 0;
+  const bool b_imm = (it.flags & IF_B_SCALAR) != 0;
+  const float bscal = b_imm ? __uint_as_float((uint32_t)it.b) : 0.f;
+  const float p0 = L.params[0], p1 = L.params[1];
+  const void* A = reinterpret_cast<const void*>(it.a);
+  const void* B = reinterpret_cast<const void*>(it.b);
+  void* O = reinterpret_cast<void*>(it.o);
+  const int64_t start = (int64_t)it.x;
+  const int64_t n = it.count;
+  for (int64_t k = c.tid; k < n; k += c.nt) {
+    int64_t rem = start + k;
+    int64_t oa = 0, ob = 0, oo = 0;
+    for (int d = nd - 1; d >= 0; --d) {
+      const int64_t sz = L.sizes[d];
+      const int64_t idx = rem % sz;
+      rem /= sz;
+      oa += idx * L.sa[d];
+      ob += idx * L.sb[d];
+      oo += idx * L.so[d];
+    }
+    const float av = ld_elem(A, it.dt_a, oa);
+    const float bv = has_b ? (b_imm ? bscal : ld_elem(B, it.dt_b, ob)) : 0.f;
+    st_elem(O, it.dt_o, oo, ew_apply_dyn(OP, av, bv, p0, p1));
+  }
+}
+
+template <int OP>
+__device__ void ew_tile(const TileCtx& c) {
+  if (c.m->item.kind == IK_EW_CONTIG) ew_contig<OP>(c);
+  else ew_generic(c);
+}
+
+// ---- reductions ------------------------------------------------------------------------
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Rows of one item: warp w reduces rows w, w + nwarps, ...  Each lane keeps four
+// partial sums in a fixed order, so the result is deterministic.
+__device__ __noinline__ void row_reduce_tile(const TileCtx& c) {
+  const WorkItem& it = c.m->item;
+  const uint32_t rows = it.count;
+  const int64_t C = it.aux;
+  const int64_t rs = (int64_t)it.x;
+  const int64_t is = (int64_t)it.b;
+  const int dta = it.dt_a;
+  const int es = dtype_size(dta);
+  const unsigned char* base =
+      (c.m->staged & 1) ? c.sa + c.m->a_off : reinterpret_cast<const unsigned char*>(it.a);
+  const uint32_t warp = c.tid >> 5, lane = c.tid & 31, nw = c.nt >> 5;
+  const bool mean = (it.flags & IF_MEAN) != 0;
+  for (uint32_t r = warp; r < rows; r += nw) {
+    const unsigned char* row = base + (int64_t)r * rs * es;
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    int64_t j = lane;
+    for (; j + 96 < C; j += 128) {
+      s0 = __fadd_rn(s0, ld_elem(row, dta, j * is));
+      s1 = __fadd_rn(s1, ld_elem(row, dta, (j + 32) * is));
+      s2 = __fadd_rn(s2, ld_elem(row, dta, (j + 64) * is));
+      s3 = __fadd_rn(s3, ld_elem(row, dta, (j + 96) * is));
+    }
+    for (; j < C; j += 32) s0 = __fadd_rn(s0, ld_elem(row, dta, j * is));
+    float s = warp_sum(__fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3)));
+    if (lane == 0) {
+      if (mean) s = __fdiv_rn(s, (float)C);
+      st_elem(reinterpret_cast<void*>(it.o), it.dt_o, r, s);
+    }
+  }
+}
+
+// Arbitrary reduced axes: one output element per thread, serial over the reduced extent.
+__device__ __noinline__ void red_generic_tile(const TileCtx& c) {
+  const WorkItem& it = c.m->item;
+  const Layout& L = c.m->ext.layout;
+  const void* A = reinterpret_cast<const void*>(it.a);
+  void* O = reinterpret_cast<void*>(it.o);
+  const bool mean = (it.flags & IF_MEAN) != 0;
+  const int64_t start = (int64_t)it.x;
+  for (int64_t k = c.tid; k < (int64_t)it.count; k += c.nt) {
+    int64_t rem = start + k, ia = 0, oo = 0;
+    for (int d = L.ndim - 1; d >= 0; --d) {
+      const int64_t idx = rem % L.sizes[d];
+      rem /= L.sizes[d];
+      ia += idx * L.sa[d];
+      oo += idx * L.so[d];
+    }
+    float acc = 0.f;
+    for (int64_t rv = 0; rv < L.rtotal; ++rv) {
+      int64_t t = rv, off = 0;
+      for (int d = L.rdim - 1; d >= 0; --d) {
+        const int64_t idx = t % L.rsizes[d];
+        t /= L.rsizes[d];
+        off += idx * L.rsa[d];
+      }
+      acc = __fadd_rn(acc, ld_elem(A, it.dt_a, ia + off));
+    }
+    if (mean) acc = __fdiv_rn(acc, (float)L.rtotal);
+    st_elem(O, it.dt_o, oo, acc);
+  }
+}
+
+__device__ void reduce_tile(const TileCtx& c) {
+  if (c.m->item.kind == IK_ROW_REDUCE) row_reduce_tile(c);
+  else red_generic_tile(c);
+}
+
+}  // namespace gpuos

@@ -1,0 +1,579 @@
+// worker.cuh — the persistent worker (one CTA per SM).
+//
+// Reference: src/persistent_kernel.cu:138-231.  There, thread 0 of each CTA CAS-claims
+// one 496-byte Task, the whole CTA runs it, and completion is a system atomic on a
+// mapped counter.  Here:
+//   * warp 0 is the dequeue warp: it takes item tickets from a device counter, reads
+//     the 64-byte item from the ring in mapped pinned memory, waits on the item's
+//     dependency barrier, and stages contiguous operands into shared memory with TMA
+//     bulk copies (mbarrier complete_tx), up to `stages` items ahead;
+//   * warps 1.. are compute warps: they run the tile function for the item through the
+//     device function-pointer table (one indirect call per tile), or, for a reference
+//     Task, resolve g_op_alias/g_op_table at dequeue time and run it with the whole CTA;
+//   * completion is counted per flush; the last item of a flush writes that flush's
+//     ticket into mapped memory (single writer, no host-memory atomics);
+//   * every wait is bounded by %globaltimer; a wait that runs out records an error in the
+//     mapped report and the grid exits;
+//   * exit is coordinated so no ticket is lost: the CTAs park, the leader (CTA 0)
+//     publishes EXITING, re-reads the host tail (Dekker-style with the host's publish) and
+//     either resumes or lets the grid exit with the exact drain point recorded for the
+//     next launch.
+#pragma once
+#include "tiles.cuh"
+
+namespace gpuos {
+
+constexpr uint64_t kNoTicket = ~0ull;
+constexpr uint32_t kBarTask = 2;                            // named barrier: whole CTA
+constexpr uint32_t kBarCompute = 1;                         // named barrier: compute warps
+
+struct WorkerShared {
+  SmemHeader* H;
+  unsigned char* bufs;
+  uint32_t stage_bytes;
+};
+
+__device__ __forceinline__ unsigned char* stage_buf(const WorkerShared& W, uint32_t s) {
+  return W.bufs + (size_t)s * W.stage_bytes;
+}
+
+__device__ __forceinline__ void report_error(const WorkerParams& P, uint32_t code, uint64_t item) {
+  if (atomicCAS(&P.dc->abort, 0u, 1u) == 0u) {
+    ptx::st_relaxed_sys(&P.rep->error_item, item);
+    ptx::fence_acq_rel_sys();
+    ptx::st_relaxed_sys(&P.rep->error, ((uint64_t)code << 32) | (uint32_t)blockIdx.x);
+  }
+}
+
+// Table lookup at dequeue time (persistent_kernel.cu:184-193).
+__device__ __forceinline__ OpFn resolve_op(const WorkerParams& P, int op) {
+  if (op < 0 || op >= GPUOS_MAX_OPS) return nullptr;
+  const int phys = *reinterpret_cast<volatile int*>(&P.op_alias[op]);
+  if (phys < 0 || phys >= GPUOS_MAX_OPS) return nullptr;
+  return reinterpret_cast<OpFn>(*reinterpret_cast<volatile unsigned long long*>(&P.op_table[phys]));
+}
+
+// Tile functions of the batched path: one per element-wise op, then the reductions.
+// One indirect call per work item dispatches through this table.
+__device__ TileFn g_tile_fns[GPUOS_EW_NUM_OPS + 1] = {
+    ew_tile<0>,  ew_tile<1>,  ew_tile<2>,  ew_tile<3>,  ew_tile<4>,  ew_tile<5>,  ew_tile<6>,
+    ew_tile<7>,  ew_tile<8>,  ew_tile<9>,  ew_tile<10>, ew_tile<11>, ew_tile<12>, ew_tile<13>,
+    ew_tile<14>, ew_tile<15>, ew_tile<16>, ew_tile<17>, ew_tile<18>, ew_tile<19>, ew_tile<20>,
+    ew_tile<21>, ew_tile<22>, ew_tile<23>, ew_tile<24>, ew_tile<25>, ew_tile<26>, ew_tile<27>,
+    ew_tile<28>, ew_tile<29>, reduce_tile};
+
+// ---- completion ----------------------------------------------------------------------
+__device__ __forceinline__ void complete_item(const WorkerParams& P, const WorkItem& it) {
+  ptx::fence_acq_rel_gpu();
+  atomicAdd(&P.dc->items_done, 1ull);
+  const unsigned int prev = atomicAdd(&P.dc->batch_done[it.batch], 1u);
+  if (prev + 1 == it.batch_items) {
+    ptx::fence_acq_rel_gpu();
+    P.dc->batch_done[it.batch] = 0u;
+    const unsigned long long t0 = atomicExch(&P.dc->batch_t0[it.batch], ~0ull);
+    Ticket& tk = P.tickets[it.batch];
+    ptx::st_relaxed_sys(&tk.t_start, t0);
+    ptx::st_relaxed_sys(&tk.t_end, ptx::now_ns());
+    ptx::fence_sc_sys();
+    ptx::st_relaxed_sys(&tk.seq, it.batch_seq);
+  }
+}
+
+// ---- compute warps ----------------------------------------------------------------------
+__device__ void compute_loop(const WorkerParams& P, const WorkerShared& W, uint32_t ctid, uint32_t nct) {
+  SmemHeader& H = *W.H;
+  const uint32_t S = P.stages;
+  for (uint64_t iter = 0;; ++iter) {
+    const uint32_t s = (uint32_t)(iter % S);
+    const uint32_t parity = (uint32_t)((iter / S) & 1);
+    const uint32_t full = ptx::smem_addr(&H.full[s]);
+    uint32_t spins = 0;
+    while (!ptx::mbar_try_wait(full, parity)) {
+      if ((++spins & 1023u) == 0) {
+        const uint64_t alive = *reinterpret_cast<volatile unsigned long long*>(&H.prod_alive);
+        if (ptx::now_ns() - alive > P.hc->wait_limit_ns + P.hc->safety_idle_ns) {
+          report_error(P, DE_WAIT_FULL, iter);
+          return;
+        }
+      }
+    }
+    const StageMeta& m = H.meta[s];
+    const uint8_t kind = m.item.kind;
+    if (kind == IK_EXIT) return;
+    if (kind == IK_TASK) {
+      ptx::named_bar_sync(kBarTask, nct + 32);
+      OpFn fn = reinterpret_cast<OpFn>(m.item.x);
+      fn(m.ext.task);
+      ptx::named_bar_sync(kBarTask, nct + 32);
+    } else {
+      TileCtx ctx;
+      ctx.m = &m;
+      ctx.sa = stage_buf(W, s);
+      ctx.sb = stage_buf(W, s) + (W.stage_bytes >> 1);
+      ctx.tid = ctid;
+      ctx.nt = nct;
+      const uint32_t fi = (kind == IK_EW_CONTIG || kind == IK_EW_GENERIC) ? m.item.op : GPUOS_EW_NUM_OPS;
+      TileFn fn = g_tile_fns[fi];
+      fn(ctx);
+    }
+    ptx::named_bar_sync(kBarCompute, nct);
+    if (ctid == 0) {
+      complete_item(P, m.item);
+      ptx::mbar_arrive(ptx::smem_addr(&H.empty[s]));
+    }
+  }
+}
+
+// ---- dequeue warp -------------------------------------------------------------------------
+struct ProdState {
+  uint64_t iter;        // items staged so far
+  uint64_t ticket;      // held ticket (kNoTicket if none)
+  uint64_t tail_cache;
+  uint64_t items_done_cache;
+  uint64_t seen_round;  // last closing round handled
+  uint64_t round;       // leader: current closing round
+  uint64_t beat_val;    // leader: last observed host beat
+  uint64_t beat_t;      // leader: when it changed
+  uint64_t polls;
+};
+
+// Wait (lane 0) until compute warps released stage use `use` (i.e. iteration use-1 done).
+__device__ bool wait_empty(const WorkerParams& P, SmemHeader& H, uint64_t iter, uint32_t S) {
+  if (iter < S) return true;
+  const uint32_t s = (uint32_t)(iter % S);
+  const uint32_t parity = (uint32_t)(((iter / S) - 1) & 1);
+  const uint32_t bar = ptx::smem_addr(&H.empty[s]);
+  const uint64_t t0 = ptx::now_ns();
+  uint32_t spins = 0;
+  while (!ptx::mbar_try_wait(bar, parity)) {
+    if ((++spins & 255u) == 0) {
+      const uint64_t t = ptx::now_ns();
+      *reinterpret_cast<volatile unsigned long long*>(&H.prod_alive) = t;
+      if (t - t0 > P.hc->wait_limit_ns) {
+        report_error(P, DE_WAIT_EMPTY, iter);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+// Wait (lane 0) until all `iter` staged items have been released by the compute warps.
+__device__ bool drain_own(const WorkerParams& P, SmemHeader& H, uint64_t iter, uint32_t S) {
+  const uint64_t lo = iter > S ? iter - S : 0;
+  for (uint64_t u = lo; u < iter; ++u) {
+    // use u was released when the empty barrier of its stage completed phase (u / S)
+    const uint32_t s = (uint32_t)(u % S);
+    const uint32_t parity = (uint32_t)((u / S) & 1);
+    const uint32_t bar = ptx::smem_addr(&H.empty[s]);
+    const uint64_t t0 = ptx::now_ns();
+    uint32_t spins = 0;
+    while (!ptx::mbar_try_wait(bar, parity)) {
+      if ((++spins & 255u) == 0 && ptx::now_ns() - t0 > P.hc->wait_limit_ns) {
+        report_error(P, DE_WAIT_EMPTY, u);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+enum ParkVerdict { PV_RESUME = 1, PV_EXIT = 2 };
+constexpr uint64_t kGatherNs = 200ull * 1000;  // leader gathers parked CTAs this long, then retries
+
+// Count this CTA as parked in `round` (no-op if that round is no longer open).
+__device__ __forceinline__ void park_count(DevCtl* dc, uint64_t round) {
+  while (true) {
+    const unsigned long long w = ptx::ld_acquire_gpu(&dc->park_word);
+    if ((w >> 32) != round) return;
+    if (atomicCAS(&dc->park_word, w, w + 1) == w) return;
+  }
+}
+
+// Park protocol (lane 0 of a dequeue warp that is idle and holds an unpublished ticket).
+// Returns PV_RESUME or PV_EXIT.
+__device__ int park(const WorkerParams& P, SmemHeader& H, ProdState& st, uint64_t round, uint32_t S) {
+  DevCtl* dc = P.dc;
+  st.seen_round = round;
+  const bool leader = blockIdx.x == 0;
+  if (!leader) {
+    const unsigned long long v = ptx::ld_acquire_gpu(&dc->verdict);
+    if ((v >> 2) == round) return (int)(v & 3);
+    if ((v >> 2) > round) return PV_RESUME;
+  }
+  if (!drain_own(P, H, st.iter, S)) return PV_EXIT;
+  atomicMin(&dc->park_min, (unsigned long long)st.ticket);
+  ptx::fence_acq_rel_gpu();
+  park_count(dc, round);
+  const uint64_t t0 = ptx::now_ns();
+  if (leader) {
+    uint32_t spins = 0;
+    bool gathered = false;
+    while (true) {
+      if ((ptx::ld_acquire_gpu(&dc->park_word) & 0xffffffffull) >= gridDim.x) {
+        gathered = true;
+        break;
+      }
+      if (*reinterpret_cast<volatile unsigned int*>(&dc->abort)) break;
+      const uint64_t t = ptx::ld_acquire_sys(&P.hc->tail);
+      if (t > *reinterpret_cast<volatile unsigned long long*>(&dc->park_min)) break;  // work for a parked CTA
+      if ((++spins & 15u) == 0) {
+        const uint64_t now = ptx::now_ns();
+        *reinterpret_cast<volatile unsigned long long*>(&H.prod_alive) = now;
+        if (now - t0 > kGatherNs) break;  // someone is still busy: retry later
+      }
+      ptx::nanosleep(128);
+    }
+    const bool aborted = *reinterpret_cast<volatile unsigned int*>(&dc->abort) != 0;
+    if (!gathered && !aborted) {
+      ptx::st_release_gpu(&dc->tail_mirror, ptx::ld_acquire_sys(&P.hc->tail));
+      ptx::st_release_gpu(&dc->verdict, (round << 2) | PV_RESUME);
+      return PV_RESUME;
+    }
+    // Publish EXITING, then re-read the host tail: the host stores tail, fences, then
+    // reads the state, so at least one side sees the other's write.
+    ptx::st_relaxed_sys(&P.rep->state, (P.epoch << 8) | WS_EXITING);
+    ptx::fence_sc_sys();
+    const uint64_t T = ptx::ld_acquire_sys(&P.hc->tail);
+    const uint64_t pm = *reinterpret_cast<volatile unsigned long long*>(&dc->park_min);
+    if (!aborted && T > pm) {
+      ptx::st_relaxed_sys(&P.rep->state, (P.epoch << 8) | WS_RUNNING);
+      ptx::st_release_gpu(&dc->tail_mirror, T);
+      ptx::st_release_gpu(&dc->verdict, (round << 2) | PV_RESUME);
+      return PV_RESUME;
+    }
+    dc->exit_tail = pm;
+    ptx::st_release_gpu(&dc->verdict, (round << 2) | PV_EXIT);
+    return PV_EXIT;
+  }
+  uint32_t spins = 0;
+  while (true) {
+    const unsigned long long v = ptx::ld_acquire_gpu(&dc->verdict);
+    if ((v >> 2) == round) return (int)(v & 3);
+    if ((v >> 2) > round) return PV_RESUME;
+    if (*reinterpret_cast<volatile unsigned int*>(&dc->abort)) return PV_EXIT;
+    if ((++spins & 63u) == 0) {
+      const uint64_t now = ptx::now_ns();
+      *reinterpret_cast<volatile unsigned long long*>(&H.prod_alive) = now;
+      if (now - t0 > P.hc->wait_limit_ns) {
+        report_error(P, DE_WAIT_PARK, st.ticket);
+        return PV_EXIT;
+      }
+    }
+    ptx::nanosleep(256);
+  }
+}
+
+// Copy `bytes` (multiple of 16) from mapped/global memory into shared memory with the warp.
+__device__ __forceinline__ void warp_copy16(void* dst, const void* src, uint32_t bytes, uint32_t lane) {
+  for (uint32_t off = lane * 16; off < bytes; off += 32 * 16) {
+    const uint4 v = ptx::ld_volatile_v4(reinterpret_cast<const unsigned char*>(src) + off);
+    *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(dst) + off) = v;
+  }
+}
+
+// Arm stage s as the exit sentinel (lane 0).
+__device__ __forceinline__ void arm_exit(SmemHeader& H, uint32_t s) {
+  H.meta[s].item.kind = IK_EXIT;
+  ptx::mbar_arrive(ptx::smem_addr(&H.full[s]));
+}
+
+// Stage one item (whole dequeue warp; stage `st.iter % S` is free).  On an error the
+// stage is armed as the exit sentinel and false is returned.
+__device__ bool stage_item(const WorkerParams& P, const WorkerShared& W, ProdState& st, uint32_t lane) {
+  SmemHeader& H = *W.H;
+  const uint32_t S = P.stages;
+  const uint32_t s = (uint32_t)(st.iter % S);
+  StageMeta& m = H.meta[s];
+  const WorkItem* src = P.items + (st.ticket & P.item_mask);
+  warp_copy16(&m.item, src, sizeof(WorkItem), lane);
+  __syncwarp();
+  const WorkItem it = m.item;
+  int ok = 1;
+  if (lane == 0) {
+    if (it.kind == IK_NONE || it.kind > IK_TASK || it.batch >= kNumBatchSlots ||
+        (it.kind != IK_TASK && it.kind != IK_ROW_REDUCE && it.kind != IK_RED_GENERIC && it.op >= GPUOS_EW_NUM_OPS)) {
+      report_error(P, DE_BAD_ITEM, st.ticket);
+      ok = 0;
+    }
+    // dependency barrier: every item before the segment start must be complete
+    if (ok && it.wait_items > st.items_done_cache) {
+      const uint64_t t0 = ptx::now_ns();
+      uint32_t spins = 0;
+      while (true) {
+        st.items_done_cache = ptx::ld_acquire_gpu(&P.dc->items_done);
+        if (st.items_done_cache >= it.wait_items) break;
+        if (*reinterpret_cast<volatile unsigned int*>(&P.dc->abort)) { ok = 0; break; }
+        if ((++spins & 63u) == 0) {
+          const uint64_t now = ptx::now_ns();
+          *reinterpret_cast<volatile unsigned long long*>(&H.prod_alive) = now;
+          if (now - t0 > P.hc->wait_limit_ns) {
+            report_error(P, DE_WAIT_BARRIER, st.ticket);
+            ok = 0;
+            break;
+          }
+        }
+        ptx::nanosleep(64);
+      }
+    }
+    if (ok) atomicMin(&P.dc->batch_t0[it.batch], (unsigned long long)ptx::now_ns());
+    else arm_exit(H, s);
+  }
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (!ok) return false;
+
+  m.staged = 0;
+  if (it.kind == IK_EW_GENERIC || it.kind == IK_RED_GENERIC) {
+    warp_copy16(&m.ext.layout, P.layouts + (it.aux & P.layout_mask), sizeof(Layout), lane);
+  } else if (it.kind == IK_TASK) {
+    warp_copy16(&m.ext.task, P.tasks + (it.aux & P.task_mask), sizeof(Task), lane);
+  }
+  __syncwarp();
+  if (lane == 0) {
+    const uint32_t full = ptx::smem_addr(&H.full[s]);
+    unsigned char* buf = stage_buf(W, s);
+    if (it.kind == IK_EW_CONTIG) {
+      uint32_t tx = 0;
+      uint64_t a0 = 0, a1 = 0, b0 = 0, b1 = 0;
+      const uint32_t half = W.stage_bytes >> 1;
+      if (!(it.flags & IF_A_BCAST)) {
+        const uint64_t bytes = (uint64_t)it.count * dtype_size(it.dt_a);
+        a0 = it.a & ~15ull;
+        a1 = (it.a + bytes + 15) & ~15ull;
+        if (a1 - a0 <= half) {
+          m.a_off = (uint32_t)(it.a - a0);
+          m.staged |= 1;
+          tx += (uint32_t)(a1 - a0);
+        }
+      }
+      if ((it.flags & IF_B_PRESENT) && !(it.flags & (IF_B_SCALAR | IF_B_BCAST))) {
+        const uint64_t bytes = (uint64_t)it.count * dtype_size(it.dt_b);
+        b0 = it.b & ~15ull;
+        b1 = (it.b + bytes + 15) & ~15ull;
+        if (b1 - b0 <= half) {
+          m.b_off = (uint32_t)(it.b - b0);
+          m.staged |= 2;
+          tx += (uint32_t)(b1 - b0);
+        }
+      }
+      if (tx) {
+        ptx::mbar_arrive_expect_tx(full, tx);
+        if (m.staged & 1) ptx::bulk_g2s(ptx::smem_addr(buf), reinterpret_cast<const void*>(a0), (uint32_t)(a1 - a0), full);
+        if (m.staged & 2)
+          ptx::bulk_g2s(ptx::smem_addr(buf + half), reinterpret_cast<const void*>(b0), (uint32_t)(b1 - b0), full);
+      } else {
+        ptx::mbar_arrive(full);
+      }
+    } else if (it.kind == IK_ROW_REDUCE && !(it.flags & IF_UNSTAGED)) {
+      const int es = dtype_size(it.dt_a);
+      const int64_t rows = it.count, C = it.aux, rs = (int64_t)it.x, is = (int64_t)it.b;
+      const uint64_t span = (uint64_t)(((rows - 1) * rs + (C - 1) * is + 1) * es);
+      const uint64_t a0 = it.a & ~15ull;
+      const uint64_t a1 = (it.a + span + 15) & ~15ull;
+      if (a1 - a0 <= W.stage_bytes) {
+        m.a_off = (uint32_t)(it.a - a0);
+        m.staged = 1;
+        ptx::mbar_arrive_expect_tx(full, (uint32_t)(a1 - a0));
+        ptx::bulk_g2s(ptx::smem_addr(buf), reinterpret_cast<const void*>(a0), (uint32_t)(a1 - a0), full);
+      } else {
+        ptx::mbar_arrive(full);
+      }
+    } else if (it.kind == IK_TASK) {
+      const OpFn fn = resolve_op(P, m.ext.task.op);
+      if (fn == nullptr) {
+        report_error(P, DE_NULL_OP, st.ticket);
+        ok = 0;
+        arm_exit(H, s);
+      } else {
+        m.item.x = reinterpret_cast<uint64_t>(fn);
+        ptx::mbar_arrive(full);
+      }
+    } else {
+      ptx::mbar_arrive(full);
+    }
+  }
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (!ok) return false;
+  if (it.kind == IK_TASK) {
+    // run the reference-ABI operator with the whole CTA
+    ptx::named_bar_sync(kBarTask, blockDim.x);
+    OpFn fn = reinterpret_cast<OpFn>(m.item.x);
+    fn(m.ext.task);
+    ptx::named_bar_sync(kBarTask, blockDim.x);
+  }
+  return true;
+}
+
+__device__ void push_exit(const WorkerParams& P, SmemHeader& H, ProdState& st, uint32_t lane) {
+  const uint32_t S = P.stages;
+  if (lane == 0) {
+    wait_empty(P, H, st.iter, S);
+    arm_exit(H, (uint32_t)(st.iter % S));
+  }
+  __syncwarp();
+}
+
+__device__ void producer_loop(const WorkerParams& P, const WorkerShared& W, uint32_t lane) {
+  SmemHeader& H = *W.H;
+  DevCtl* dc = P.dc;
+  const uint32_t S = P.stages;
+  const bool leader = blockIdx.x == 0;
+  ProdState st;
+  st.iter = 0;
+  st.ticket = kNoTicket;
+  st.tail_cache = ptx::ld_acquire_gpu(&dc->tail_mirror);
+  st.items_done_cache = 0;
+  st.seen_round = 0;
+  st.round = 0;
+  st.beat_val = P.hc->host_beat;
+  st.beat_t = ptx::now_ns();
+  st.polls = 0;
+
+  while (true) {
+    int action = 0;  // 0: stage ticket, 1: exit
+    if (lane == 0) {
+      if (st.ticket == kNoTicket) {
+        if (!wait_empty(P, H, st.iter, S)) action = 1;
+        else st.ticket = atomicAdd(&dc->head, 1ull);
+      }
+      while (action == 0 && st.ticket >= st.tail_cache) {
+        // idle: poll for publication, watch for exit conditions
+        ++st.polls;
+        uint64_t t;
+        if (leader || (st.polls & 15u) == 0) {
+          t = ptx::ld_acquire_sys(&P.hc->tail);
+          if (t > *reinterpret_cast<volatile unsigned long long*>(&dc->tail_mirror)) ptx::st_release_gpu(&dc->tail_mirror, t);
+        } else {
+          t = ptx::ld_acquire_gpu(&dc->tail_mirror);
+        }
+        if (st.ticket < t) {
+          st.tail_cache = t;
+          break;
+        }
+        const uint64_t now = ptx::now_ns();
+        *reinterpret_cast<volatile unsigned long long*>(&H.prod_alive) = now;
+        if (*reinterpret_cast<volatile unsigned int*>(&dc->abort)) {
+          action = 1;
+          break;
+        }
+        if (leader && (st.polls & 7u) == 0) {
+          if ((st.polls & 63u) == 0) {
+            ptx::st_relaxed_sys(&P.rep->heartbeat, st.polls);
+            ptx::st_relaxed_sys(&P.rep->head_mirror, *reinterpret_cast<volatile unsigned long long*>(&dc->head));
+            ptx::st_relaxed_sys(&P.rep->items_done, *reinterpret_cast<volatile unsigned long long*>(&dc->items_done));
+          }
+          const uint64_t beat = P.hc->host_beat;
+          if (beat != st.beat_val) {
+            st.beat_val = beat;
+            st.beat_t = now;
+          }
+          bool want_exit = P.hc->quit_epoch >= P.epoch;
+          const uint64_t ye = P.hc->yield_every;
+          if (ye && ptx::ld_acquire_gpu(&dc->items_done) - dc->yield_base >= ye) want_exit = true;
+          if (now - st.beat_t > P.hc->safety_idle_ns) want_exit = true;
+          if (want_exit) {
+            st.round = (st.round > st.seen_round ? st.round : st.seen_round) + 1;
+            dc->park_min = ~0ull;
+            atomicExch(&dc->park_word, (unsigned long long)st.round << 32);
+            ptx::fence_acq_rel_gpu();
+            ptx::st_release_gpu(&dc->closing, st.round);
+          }
+        }
+        const unsigned long long cl = ptx::ld_acquire_gpu(&dc->closing);
+        if (cl > st.seen_round) {
+          const int v = park(P, H, st, cl, S);
+          if (v == PV_EXIT) {
+            action = 1;
+            break;
+          }
+          st.tail_cache = ptx::ld_acquire_gpu(&dc->tail_mirror);
+          continue;
+        }
+        ptx::nanosleep(leader ? P.hc->spin_ns : 256);
+      }
+    }
+    action = __shfl_sync(0xffffffffu, action, 0);
+    if (action == 1) {
+      push_exit(P, H, st, lane);
+      return;
+    }
+    st.ticket = __shfl_sync(0xffffffffu, st.ticket, 0);
+    if (!stage_item(P, W, st, lane)) return;
+    st.iter = __shfl_sync(0xffffffffu, st.iter, 0) + 1;
+    st.ticket = kNoTicket;
+  }
+}
+
+// ---- the kernel ---------------------------------------------------------------------------
+__device__ void batch_worker_body(const WorkerParams& P, unsigned char* smem_raw) {
+  SmemHeader* H = reinterpret_cast<SmemHeader*>(smem_raw);
+  WorkerShared W;
+  W.H = H;
+  W.bufs = smem_raw + ((sizeof(SmemHeader) + 127) & ~size_t(127));
+  W.stage_bytes = P.stage_bytes;
+  const uint32_t S = P.stages;
+  DevCtl* dc = P.dc;
+
+  if (threadIdx.x == 0) {
+    for (uint32_t s = 0; s < S; ++s) {
+      ptx::mbar_init(ptx::smem_addr(&H->full[s]), 1);
+      ptx::mbar_init(ptx::smem_addr(&H->empty[s]), 1);
+    }
+    ptx::fence_mbar_init();
+    H->prod_alive = ptx::now_ns();
+    H->exit_flag = 0;
+  }
+  __syncthreads();
+
+  // Launch initialisation: CTA 0 resets the dequeue position to where the previous
+  // launch stopped; the other CTAs wait for it (bounded).
+  __shared__ int start_ok;
+  if (threadIdx.x == 0) {
+    start_ok = 1;
+    if (blockIdx.x == 0) {
+      dc->head = dc->exit_tail;
+      dc->closing = 0;
+      dc->verdict = 0;
+      dc->park_word = 0;
+      dc->park_min = ~0ull;
+      dc->abort = 0;
+      dc->exited = 0;
+      dc->yield_base = dc->items_done;
+      dc->tail_mirror = ptx::ld_acquire_sys(&P.hc->tail);
+      ptx::fence_acq_rel_gpu();
+      ptx::st_release_gpu(&dc->launch_epoch, P.epoch);
+      ptx::st_relaxed_sys(&P.rep->state, (P.epoch << 8) | WS_RUNNING);
+      ptx::fence_acq_rel_sys();
+      ptx::st_relaxed_sys(&P.rep->ready_epoch, P.epoch);
+    } else {
+      const uint64_t t0 = ptx::now_ns();
+      while (ptx::ld_acquire_gpu(&dc->launch_epoch) != P.epoch) {
+        if (ptx::now_ns() - t0 > P.hc->wait_limit_ns) {
+          report_error(P, DE_WAIT_START, 0);
+          start_ok = 0;
+          break;
+        }
+        ptx::nanosleep(128);
+      }
+    }
+  }
+  __syncthreads();
+  if (start_ok) {
+    const uint32_t warp = threadIdx.x >> 5;
+    if (warp == 0) producer_loop(P, W, threadIdx.x & 31);
+    else compute_loop(P, W, threadIdx.x - 32, blockDim.x - 32);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    ptx::fence_acq_rel_gpu();
+    const unsigned int n = atomicAdd(&dc->exited, 1u) + 1;
+    if (n == gridDim.x) {
+      ptx::st_relaxed_sys(&P.rep->exit_tail, dc->exit_tail);
+      ptx::st_relaxed_sys(&P.rep->items_done, dc->items_done);
+      ptx::fence_sc_sys();
+      ptx::st_relaxed_sys(&P.rep->state, (P.epoch << 8) | WS_EXITED);
+    }
+  }
+}
+
+}  // namespace gpuos

@@ -1,0 +1,225 @@
+// internal.h — descriptors shared by the host runtime and the device worker.
+//
+// The reference publishes one 496-byte Task per ring slot and aggregates micro
+// requests into "batch" Tasks whose sub-tasks one CTA walks serially
+// (src/persistent_kernel.cu:81-112, pytorch_ext/gpuos_ext.cpp:755-778).  Here a flush is
+// split into 64-byte work items (a tile of one request, a group of reduction rows,
+// or one reference-layout Task) that every CTA of the persistent grid claims from a
+// ring in mapped pinned memory.  Items are self-contained for the contiguous case so
+// the dequeue warp needs a single 64-byte read per item.
+#pragma once
+#include <stdint.h>
+#include "gpuos_b200.h"
+
+#if defined(__CUDACC__) || defined(__CUDACC_RTC__)
+#define GPUOS_HD __host__ __device__
+#else
+#define GPUOS_HD
+#endif
+
+namespace gpuos {
+
+// ---- item kinds -----------------------------------------------------------------
+enum ItemKind : uint8_t {
+  IK_NONE = 0,
+  IK_EW_CONTIG = 1,   // 1-D contiguous element-wise tile (operands staged by TMA bulk copy)
+  IK_EW_GENERIC = 2,  // strided / broadcast element-wise tile (layout record)
+  IK_ROW_REDUCE = 3,  // group of rows reduced over the last (possibly strided) axis
+  IK_RED_GENERIC = 4, // arbitrary-axes reduction, one output element per thread
+  IK_TASK = 5,        // reference-layout Task dispatched through g_op_alias/g_op_table
+  IK_EXIT = 255       // in-CTA sentinel (never in the ring)
+};
+
+enum ItemFlags : uint8_t {
+  IF_B_PRESENT = 1,   // binary op: operand b exists
+  IF_B_SCALAR = 2,    // b is an immediate float held in the low 32 bits of WorkItem::b
+  IF_A_BCAST = 4,     // EW_CONTIG: a is one element broadcast over the tile
+  IF_B_BCAST = 8,     // EW_CONTIG: b is one element (in memory) broadcast over the tile
+  IF_UNSTAGED = 16,   // ROW_REDUCE: rows read directly from global memory
+  IF_MEAN = 32        // reductions: divide by the reduced extent
+};
+
+// One work item (64 bytes).  Field use per kind:
+//   EW_CONTIG   a,b,o = operand addresses of the tile's first element; count = elements;
+//               x = two float params (p0 low, p1 high); aux = layout index when the op
+//               needs more than two params (else 0xffffffff).
+//   EW_GENERIC  a,b,o = base addresses; x = first output linear index; count = elements;
+//               aux = layout index.
+//   ROW_REDUCE  a = first element of the first row; o = first output; count = rows;
+//               aux = row length C; x = row stride (elements); b = element stride.
+//   RED_GENERIC a,o = base addresses; x = first output linear index; count = outputs;
+//               aux = layout index.
+//   TASK        aux = task ring index; op = logical op id (low 8 bits of Task::op).
+struct alignas(64) WorkItem {
+  uint8_t kind;
+  uint8_t op;
+  uint8_t dt_a;
+  uint8_t dt_b;
+  uint8_t dt_o;
+  uint8_t flags;
+  uint16_t batch;        // ticket slot of the flush this item belongs to
+  uint32_t count;
+  uint32_t aux;
+  uint64_t a;
+  uint64_t b;
+  uint64_t o;
+  uint64_t x;
+  uint64_t wait_items;   // start only once items_done >= wait_items (dependency barrier)
+  uint32_t batch_items;  // number of items of this flush
+  uint32_t batch_seq;    // low 32 bits of the flush ticket
+};
+static_assert(sizeof(WorkItem) == 64, "WorkItem must be 64 bytes");
+
+// Strided layout for EW_GENERIC / RED_GENERIC (coalesced dims, in elements).
+struct alignas(16) Layout {
+  int32_t ndim;        // output dims
+  int32_t rdim;        // reduced dims (RED_GENERIC)
+  float params[4];
+  int64_t sizes[GPUOS_MAX_NDIM];
+  int64_t sa[GPUOS_MAX_NDIM];
+  int64_t sb[GPUOS_MAX_NDIM];
+  int64_t so[GPUOS_MAX_NDIM];
+  int64_t rsizes[GPUOS_MAX_NDIM];
+  int64_t rsa[GPUOS_MAX_NDIM];
+  int64_t rtotal;
+  int64_t _pad;
+};
+static_assert(sizeof(Layout) <= 512, "Layout must fit the stage extension area");
+
+// ---- control blocks ----------------------------------------------------------------
+// Host-written, device-read (mapped pinned memory).
+struct alignas(128) HostCtl {
+  volatile uint64_t tail;            // items published (global monotonic index)
+  volatile uint64_t quit_epoch;      // workers with epoch <= quit_epoch exit once drained
+  volatile uint64_t host_beat;       // incremented by the host keeper thread
+  volatile uint64_t safety_idle_ns;  // exit if idle and host_beat unchanged this long
+  volatile uint64_t yield_every;     // exit after this many completed items (0: never)
+  volatile uint32_t debug_level;
+  volatile uint32_t spin_ns;         // idle poll back-off of the leader
+  volatile uint64_t wait_limit_ns;   // bound of the worker's in-grid waits
+  uint64_t _pad[9];
+};
+
+// Device-written, host-read (mapped pinned memory).  Every field has one writer.
+enum WorkerState : uint64_t { WS_NONE = 0, WS_RUNNING = 1, WS_EXITING = 2, WS_EXITED = 3 };
+struct alignas(128) DevReport {
+  volatile uint64_t ready_epoch;     // epoch of the last worker that came up
+  volatile uint64_t heartbeat;       // leader idle-poll counter
+  volatile uint64_t state;           // (epoch << 8) | WorkerState
+  volatile uint64_t exit_tail;       // items < exit_tail were processed when it exited
+  volatile uint64_t error;           // (code << 32) | detail; 0 = no error
+  volatile uint64_t error_item;      // item index involved in the error
+  volatile uint64_t head_mirror;     // dequeue position (for peek_queue)
+  volatile uint64_t items_done;      // completed items (mirror)
+  uint64_t _pad[8];
+};
+
+enum DeviceError : uint32_t {
+  DE_NONE = 0,
+  DE_WAIT_EMPTY = 1,    // dequeue warp: compute warps did not release a stage in time
+  DE_WAIT_FULL = 2,     // compute warps: dequeue warp stopped feeding
+  DE_WAIT_BARRIER = 3,  // dependency barrier did not open in time
+  DE_WAIT_PARK = 4,     // grid exit coordination timed out
+  DE_WAIT_START = 5,    // grid start coordination timed out
+  DE_BAD_ITEM = 6,      // malformed item (kind / slot / ndim out of range)
+  DE_NULL_OP = 7,       // table slot resolved to a null function
+  DE_HOST_LOST = 8      // host heartbeat stopped while idle
+};
+
+// Completion ticket of one flush (mapped pinned memory, one writer).
+struct alignas(32) Ticket {
+  volatile uint64_t seq;       // flush ticket once complete
+  volatile uint64_t t_start;   // %globaltimer when its first item started
+  volatile uint64_t t_end;     // %globaltimer when its last item completed
+  volatile uint64_t _pad;
+};
+
+constexpr int kNumBatchSlots = 1024;
+
+// Device-memory control block (cudaMalloc, zeroed at init).
+struct alignas(128) DevCtl {
+  unsigned long long head;         // next item ticket
+  unsigned long long items_done;   // completed items (dependency barriers)
+  unsigned long long tail_mirror;  // leader's copy of HostCtl::tail
+  unsigned long long launch_epoch; // set by CTA 0 once the launch is initialised
+  unsigned long long exit_tail;    // head value for the next launch
+  unsigned long long closing;      // leader requests grid exit (round number)
+  unsigned long long verdict;      // (round << 2) | 1 resume | 2 exit
+  unsigned long long park_min;     // lowest held ticket among parked CTAs
+  unsigned long long park_word;    // (round << 32) | CTAs parked in that round
+  unsigned int abort;              // a CTA hit an error: everybody exits
+  unsigned int exited;             // CTAs that left the current launch
+  unsigned long long yield_base;   // items_done at launch (yield accounting)
+  unsigned long long _pad[5];
+  unsigned int batch_done[kNumBatchSlots];
+  unsigned long long batch_t0[kNumBatchSlots];
+};
+
+// ---- worker launch parameters ---------------------------------------------------------
+typedef void (*OpFn)(const Task&);
+
+struct WorkerParams {
+  HostCtl* hc;
+  DevReport* rep;
+  Ticket* tickets;
+  const WorkItem* items;
+  const Task* tasks;
+  const Layout* layouts;
+  DevCtl* dc;
+  OpFn* op_table;
+  int* op_alias;
+  uint64_t item_mask;     // item ring capacity - 1 (power of two)
+  uint32_t task_mask;
+  uint32_t layout_mask;
+  uint64_t epoch;
+  uint32_t stages;
+  uint32_t stage_bytes;   // operand buffer bytes per stage
+  uint32_t compute_threads;
+  uint32_t _pad;
+};
+
+// Per-stage bookkeeping in shared memory.
+struct alignas(16) StageMeta {
+  WorkItem item;
+  uint32_t a_off;       // byte offset of the first a element inside the staged buffer
+  uint32_t b_off;
+  uint32_t staged;      // bit0: a staged, bit1: b staged
+  uint32_t _pad;
+  union {
+    Task task;
+    Layout layout;
+    unsigned char raw[512];
+  } ext;
+};
+
+// Worker shared-memory header (stage buffers follow, 128-byte aligned).
+constexpr int kMaxStages = 8;
+struct alignas(128) SmemHeader {
+  unsigned long long full[kMaxStages];
+  unsigned long long empty[kMaxStages];
+  unsigned long long prod_alive;   // %globaltimer stamp of the dequeue warp
+  unsigned int exit_flag;
+  unsigned int _pad;
+  StageMeta meta[kMaxStages];
+};
+
+constexpr uint32_t kStageBytesDefault = 32768 + 128;  // two 16 KB operand halves + slack
+constexpr uint32_t kHalfBytes = 16384;                // one operand tile
+
+GPUOS_HD inline int dtype_size(int dt) {
+  return dt == kF32 ? 4 : (dt == kF16 || dt == kBF16) ? 2 : dt == kF64 ? 8 : 4;
+}
+
+// Number of tensor inputs an element-wise op reads (1 or 2).
+GPUOS_HD inline int ew_arity(int op) {
+  switch (op) {
+    case GPUOS_EW_ADD: case GPUOS_EW_MUL: case GPUOS_EW_SUB: case GPUOS_EW_DIV:
+    case GPUOS_EW_MAXIMUM: case GPUOS_EW_MINIMUM: case GPUOS_EW_POW:
+    case GPUOS_EW_ADD_ALPHA: case GPUOS_EW_SUB_ALPHA:
+      return 2;
+    default:
+      return 1;
+  }
+}
+
+}  // namespace gpuos

@@ -1,0 +1,1018 @@
+// pyext.cpp — CPython binding of libgpuos_b200.so with the reference module's API.
+//
+// Reference: the pybind11 module gpuos_ext (pytorch_ext/gpuos_ext.cpp:1093-1142).  Same
+// function names, defaults and argument meaning; differences:
+//   * tensors are kept alive until the flush that reads/writes them has completed (the
+//     reference borrows raw data_ptr values);
+//   * errors raise (RuntimeError / ValueError / TimeoutError) instead of exit();
+//   * a blocking wait releases the GIL;
+//   * requests go to the runtime of the tensors' device (the reference uses device 0);
+//   * extra entry points for the scheduler (submit_elementwise, submit_reduction) and for
+//     op-table control (set_slot, set_alias, ...).
+// The hot calls (submit_add/mul/sub/div) use METH_FASTCALL and read the tensors through
+// THPVariable_Unpack without creating intermediate objects.
+#include <Python.h>
+
+#include <ATen/core/Tensor.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/csrc/autograd/python_variable.h>
+
+#include <cmath>
+#include <cstring>
+#include <deque>
+#include <string>
+#include <utility>
+#include <vector>
+
+#include "gpuos_b200.h"
+
+namespace {
+
+constexpr int kMaxDev = 64;
+
+struct DevRefs {
+  std::vector<PyObject*> pending;
+  std::deque<std::pair<uint64_t, std::vector<PyObject*>>> inflight;
+};
+
+gpuos_rt* g_rt[kMaxDev] = {nullptr};
+DevRefs g_refs[kMaxDev];
+int g_verbose = 0;
+
+PyObject* raise_status(int st) {
+  const char* msg = gpuos_rt_last_error();
+  PyObject* exc = PyExc_RuntimeError;
+  if (st == GPUOS_ERR_INVALID) exc = PyExc_ValueError;
+  else if (st == GPUOS_ERR_TIMEOUT) exc = PyExc_TimeoutError;
+  else if (st == GPUOS_ERR_UNSUPPORTED) exc = PyExc_NotImplementedError;
+  PyErr_SetString(exc, (msg && *msg) ? msg : "gpuos error");
+  return nullptr;
+}
+
+void release_list(std::vector<PyObject*>& v) {
+  for (PyObject* o : v) Py_DECREF(o);
+  v.clear();
+}
+
+void release_completed(int dev) {
+  gpuos_rt* rt = g_rt[dev];
+  DevRefs& R = g_refs[dev];
+  if (R.inflight.empty()) return;
+  const uint64_t done = rt ? gpuos_rt_completed(rt) : ~0ull;
+  while (!R.inflight.empty() && R.inflight.front().first <= done) {
+    release_list(R.inflight.front().second);
+    R.inflight.pop_front();
+  }
+}
+
+void release_all(int dev) {
+  DevRefs& R = g_refs[dev];
+  release_list(R.pending);
+  while (!R.inflight.empty()) {
+    release_list(R.inflight.front().second);
+    R.inflight.pop_front();
+  }
+}
+
+int dtype_code(c10::ScalarType st) {
+  switch (st) {
+    case c10::ScalarType::Float: return kF32;
+    case c10::ScalarType::Half: return kF16;
+    case c10::ScalarType::BFloat16: return kBF16;
+    default: return -1;
+  }
+}
+
+// Fill a GpuosOperand from a CUDA tensor.  Returns the device index or -1 with an error set.
+int to_operand(PyObject* o, GpuosOperand* op, const char* name) {
+  if (!THPVariable_Check(o)) {
+    PyErr_Format(PyExc_TypeError, "%s must be a torch.Tensor", name);
+    return -1;
+  }
+  const at::Tensor& t = THPVariable_Unpack(o);
+  if (!t.is_cuda()) {
+    PyErr_SetString(PyExc_RuntimeError, "tensors must be CUDA");
+    return -1;
+  }
+  const int dt = dtype_code(t.scalar_type());
+  if (dt < 0) {
+    PyErr_Format(PyExc_ValueError, "%s: unsupported dtype (float32, float16, bfloat16 only)", name);
+    return -1;
+  }
+  const int nd = (int)t.dim();
+  if (nd > GPUOS_MAX_NDIM) {
+    PyErr_Format(PyExc_ValueError, "%s: more than %d dimensions", name, GPUOS_MAX_NDIM);
+    return -1;
+  }
+  op->data = t.data_ptr();
+  op->dtype = dt;
+  op->ndim = nd;
+  const auto sz = t.sizes();
+  const auto st = t.strides();
+  for (int d = 0; d < nd; ++d) {
+    op->sizes[d] = sz[d];
+    op->strides[d] = st[d];
+  }
+  const int dev = t.get_device();
+  if (dev < 0 || dev >= kMaxDev) {
+    PyErr_SetString(PyExc_RuntimeError, "device index out of range");
+    return -1;
+  }
+  return dev;
+}
+
+gpuos_rt* rt_for(int dev) {
+  gpuos_rt* rt = g_rt[dev];
+  if (!rt) PyErr_SetString(PyExc_RuntimeError, "gpuos not initialized");
+  return rt;
+}
+
+void keep(int dev, PyObject* o) {
+  Py_INCREF(o);
+  g_refs[dev].pending.push_back(o);
+}
+
+// After a publish with ticket seq: pending refs belong to flushes <= seq.
+void move_pending(int dev, uint64_t seq) {
+  DevRefs& R = g_refs[dev];
+  if (R.pending.empty()) return;
+  if (seq == 0) seq = ~0ull >> 1;
+  if (!R.inflight.empty() && R.inflight.back().first == seq) {
+    auto& v = R.inflight.back().second;
+    v.insert(v.end(), R.pending.begin(), R.pending.end());
+    R.pending.clear();
+  } else {
+    R.inflight.emplace_back(seq, std::move(R.pending));
+    R.pending = std::vector<PyObject*>();
+  }
+}
+
+// Second operand: CUDA tensor, Python number, 0-dim CPU tensor, or None.
+int parse_b(PyObject* o, GpuosOperand* op, int* is_scalar, double* val, bool* present) {
+  *is_scalar = 0;
+  *val = 0.0;
+  *present = false;
+  if (o == nullptr || o == Py_None) return 0;
+  *present = true;
+  if (PyFloat_Check(o) || PyLong_Check(o) || PyBool_Check(o)) {
+    *is_scalar = 1;
+    *val = PyFloat_AsDouble(o);
+    return PyErr_Occurred() ? -1 : 0;
+  }
+  if (THPVariable_Check(o)) {
+    const at::Tensor& t = THPVariable_Unpack(o);
+    if (!t.is_cuda() && t.dim() == 0) {
+      *is_scalar = 1;
+      *val = t.item<double>();
+      return 0;
+    }
+  }
+  return to_operand(o, op, "b") < 0 ? -1 : 1;
+}
+
+// ---- submit_add / mul / sub / div (gpuos_ext.cpp:638-672) -------------------------------
+PyObject* submit_binary_builtin(PyObject* const* args, Py_ssize_t nargs, int op) {
+  if (nargs != 3) {
+    PyErr_SetString(PyExc_TypeError, "expected (a, b, out)");
+    return nullptr;
+  }
+  GpuosOperand a, b, out;
+  const int da = to_operand(args[0], &a, "a");
+  if (da < 0) return nullptr;
+  const int db = to_operand(args[1], &b, "b");
+  if (db < 0) return nullptr;
+  const int dout = to_operand(args[2], &out, "out");
+  if (dout < 0) return nullptr;
+  if (da != dout || db != dout) {
+    PyErr_SetString(PyExc_RuntimeError, "device mismatch");
+    return nullptr;
+  }
+  gpuos_rt* rt = rt_for(dout);
+  if (!rt) return nullptr;
+  const int st = gpuos_rt_submit_ew(rt, op, &a, &b, 0, 0.0, &out, nullptr, 0);
+  if (st) return raise_status(st);
+  keep(dout, args[0]);
+  keep(dout, args[1]);
+  keep(dout, args[2]);
+  Py_RETURN_NONE;
+}
+
+PyObject* py_submit_add(PyObject*, PyObject* const* a, Py_ssize_t n) { return submit_binary_builtin(a, n, GPUOS_EW_ADD); }
+PyObject* py_submit_mul(PyObject*, PyObject* const* a, Py_ssize_t n) { return submit_binary_builtin(a, n, GPUOS_EW_MUL); }
+PyObject* py_submit_sub(PyObject*, PyObject* const* a, Py_ssize_t n) { return submit_binary_builtin(a, n, GPUOS_EW_SUB); }
+PyObject* py_submit_div(PyObject*, PyObject* const* a, Py_ssize_t n) { return submit_binary_builtin(a, n, GPUOS_EW_DIV); }
+
+// submit_elementwise(op, a, b, out, p0=0.0, p1=0.0) — any built-in element-wise op, b may be
+// a tensor, a number or None.
+PyObject* py_submit_elementwise(PyObject*, PyObject* const* args, Py_ssize_t nargs) {
+  if (nargs < 4 || nargs > 6) {
+    PyErr_SetString(PyExc_TypeError, "expected (op, a, b, out[, p0[, p1]])");
+    return nullptr;
+  }
+  const long op = PyLong_AsLong(args[0]);
+  if (op == -1 && PyErr_Occurred()) return nullptr;
+  GpuosOperand a, b, out;
+  const int da = to_operand(args[1], &a, "a");
+  if (da < 0) return nullptr;
+  int b_scalar = 0;
+  double b_val = 0.0;
+  bool b_present = false;
+  const int bt = parse_b(args[2], &b, &b_scalar, &b_val, &b_present);
+  if (bt < 0) return nullptr;
+  const int dout = to_operand(args[3], &out, "out");
+  if (dout < 0) return nullptr;
+  if (da != dout) {
+    PyErr_SetString(PyExc_RuntimeError, "device mismatch");
+    return nullptr;
+  }
+  float params[2] = {0.f, 0.f};
+  for (int i = 0; i < 2 && 4 + i < nargs; ++i) {
+    params[i] = (float)PyFloat_AsDouble(args[4 + i]);
+    if (PyErr_Occurred()) return nullptr;
+  }
+  gpuos_rt* rt = rt_for(dout);
+  if (!rt) return nullptr;
+  const int st = gpuos_rt_submit_ew(rt, (int)op, &a, bt == 1 ? &b : nullptr, b_scalar, b_val, &out, params, 2);
+  if (st) return raise_status(st);
+  keep(dout, args[1]);
+  if (bt == 1) keep(dout, args[2]);
+  keep(dout, args[3]);
+  Py_RETURN_NONE;
+}
+
+bool parse_axes(PyObject* seq, std::vector<int>* axes) {
+  axes->clear();
+  if (PyLong_Check(seq)) {
+    axes->push_back((int)PyLong_AsLong(seq));
+    return !PyErr_Occurred();
+  }
+  PyObject* fast = PySequence_Fast(seq, "axes must be a sequence of ints");
+  if (!fast) return false;
+  const Py_ssize_t n = PySequence_Fast_GET_SIZE(fast);
+  for (Py_ssize_t i = 0; i < n; ++i) {
+    const long v = PyLong_AsLong(PySequence_Fast_GET_ITEM(fast, i));
+    if (v == -1 && PyErr_Occurred()) {
+      Py_DECREF(fast);
+      return false;
+    }
+    axes->push_back((int)v);
+  }
+  Py_DECREF(fast);
+  return true;
+}
+
+// submit_reduction(op, x, out, axes, keepdim) — batched sum/mean.
+PyObject* py_submit_reduction(PyObject*, PyObject* const* args, Py_ssize_t nargs) {
+  if (nargs != 5) {
+    PyErr_SetString(PyExc_TypeError, "expected (op, x, out, axes, keepdim)");
+    return nullptr;
+  }
+  const long op = PyLong_AsLong(args[0]);
+  if (op == -1 && PyErr_Occurred()) return nullptr;
+  GpuosOperand x, out;
+  const int dx = to_operand(args[1], &x, "x");
+  if (dx < 0) return nullptr;
+  const int dout = to_operand(args[2], &out, "out");
+  if (dout < 0) return nullptr;
+  if (dx != dout) {
+    PyErr_SetString(PyExc_RuntimeError, "device mismatch");
+    return nullptr;
+  }
+  std::vector<int> axes;
+  if (!parse_axes(args[3], &axes)) return nullptr;
+  const int keepdim = PyObject_IsTrue(args[4]);
+  if (keepdim < 0) return nullptr;
+  gpuos_rt* rt = rt_for(dout);
+  if (!rt) return nullptr;
+  const int st = gpuos_rt_submit_reduce(rt, (int)op, &x, &out, axes.data(), (int)axes.size(), keepdim);
+  if (st) return raise_status(st);
+  keep(dout, args[1]);
+  keep(dout, args[2]);
+  Py_RETURN_NONE;
+}
+
+// ---- flush (gpuos_ext.cpp:675-811) ------------------------------------------------------
+int flush_device(int dev, bool sync, uint64_t* seq_out) {
+  gpuos_rt* rt = g_rt[dev];
+  if (!rt) return 0;
+  cudaStream_t dep = c10::cuda::getCurrentCUDAStream((c10::DeviceIndex)dev).stream();
+  uint64_t seq = 0;
+  int st = gpuos_rt_flush(rt, GPUOS_FLUSH_DEP, dep, &seq);
+  if (st) return st;
+  move_pending(dev, seq);
+  if (sync && seq) {
+    Py_BEGIN_ALLOW_THREADS st = gpuos_rt_wait(rt, seq, 30000);
+    Py_END_ALLOW_THREADS
+  }
+  if (seq_out) *seq_out = seq;
+  release_completed(dev);
+  return st;
+}
+
+PyObject* py_flush(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"sync", "device", nullptr};
+  int sync = 0;
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "|pO", const_cast<char**>(kwlist), &sync, &devobj)) return nullptr;
+  uint64_t last = 0;
+  if (devobj != Py_None) {
+    const long d = PyLong_AsLong(devobj);
+    if (d < 0 || d >= kMaxDev) return PyErr_Format(PyExc_ValueError, "bad device %ld", d);
+    const int st = flush_device((int)d, sync != 0, &last);
+    if (st) return raise_status(st);
+    return PyLong_FromUnsignedLongLong(last);
+  }
+  for (int d = 0; d < kMaxDev; ++d) {
+    if (!g_rt[d]) continue;
+    uint64_t s = 0;
+    const int st = flush_device(d, sync != 0, &s);
+    if (st) return raise_status(st);
+    if (s) last = s;
+  }
+  return PyLong_FromUnsignedLongLong(last);
+}
+
+// ---- lifecycle ----------------------------------------------------------------------------
+int current_device() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return dev;
+}
+
+int parse_device(PyObject* devobj, int* dev) {
+  if (devobj == nullptr || devobj == Py_None) {
+    *dev = current_device();
+    return 0;
+  }
+  if (PyLong_Check(devobj)) {
+    *dev = (int)PyLong_AsLong(devobj);
+  } else {
+    PyObject* idx = PyObject_GetAttrString(devobj, "index");
+    if (!idx) return -1;
+    *dev = idx == Py_None ? current_device() : (int)PyLong_AsLong(idx);
+    Py_DECREF(idx);
+  }
+  if (*dev < 0 || *dev >= kMaxDev) {
+    PyErr_SetString(PyExc_ValueError, "device index out of range");
+    return -1;
+  }
+  return 0;
+}
+
+PyObject* py_init(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"capacity", "threads_per_block", "device", nullptr};
+  int capacity = 4096, tpb = 256;
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "|iiO", const_cast<char**>(kwlist), &capacity, &tpb, &devobj))
+    return nullptr;
+  int dev;
+  if (parse_device(devobj, &dev)) return nullptr;
+  if (g_rt[dev]) Py_RETURN_NONE;
+  gpuos_rt* rt = nullptr;
+  int st;
+  Py_BEGIN_ALLOW_THREADS st = gpuos_rt_init(dev, capacity, tpb, &rt);
+  Py_END_ALLOW_THREADS
+  if (st) return raise_status(st);
+  g_rt[dev] = rt;
+  Py_RETURN_NONE;
+}
+
+int shutdown_device(int dev) {
+  gpuos_rt* rt = g_rt[dev];
+  if (!rt) return 0;
+  move_pending(dev, 0);
+  int st;
+  Py_BEGIN_ALLOW_THREADS st = gpuos_rt_shutdown(rt);
+  Py_END_ALLOW_THREADS
+  g_rt[dev] = nullptr;
+  release_all(dev);
+  return st;
+}
+
+PyObject* py_shutdown(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"device", nullptr};
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "|O", const_cast<char**>(kwlist), &devobj)) return nullptr;
+  int first_err = 0;
+  if (devobj != Py_None) {
+    int dev;
+    if (parse_device(devobj, &dev)) return nullptr;
+    first_err = shutdown_device(dev);
+  } else {
+    for (int d = 0; d < kMaxDev; ++d) {
+      const int st = shutdown_device(d);
+      if (st && !first_err) first_err = st;
+    }
+  }
+  if (first_err) return raise_status(first_err);
+  Py_RETURN_NONE;
+}
+
+// Runtime selected by an optional device argument (default: first initialised runtime).
+gpuos_rt* rt_arg(PyObject* devobj, int* dev_out) {
+  if (devobj && devobj != Py_None) {
+    int dev;
+    if (parse_device(devobj, &dev)) return nullptr;
+    if (dev_out) *dev_out = dev;
+    return rt_for(dev);
+  }
+  const int cur = current_device();
+  if (g_rt[cur]) {
+    if (dev_out) *dev_out = cur;
+    return g_rt[cur];
+  }
+  for (int d = 0; d < kMaxDev; ++d)
+    if (g_rt[d]) {
+      if (dev_out) *dev_out = d;
+      return g_rt[d];
+    }
+  PyErr_SetString(PyExc_RuntimeError, "gpuos not initialized");
+  return nullptr;
+}
+
+PyObject* py_abi_version(PyObject*, PyObject*) { return PyLong_FromLong(1); }
+
+PyObject* py_set_debug_level(PyObject*, PyObject* args) {
+  int lvl;
+  if (!PyArg_ParseTuple(args, "i", &lvl)) return nullptr;
+  for (int d = 0; d < kMaxDev; ++d)
+    if (g_rt[d]) {
+      const int st = gpuos_rt_set_debug_level(g_rt[d], lvl);
+      if (st) return raise_status(st);
+    }
+  Py_RETURN_NONE;
+}
+
+PyObject* py_set_verbose_level(PyObject*, PyObject* args) {
+  if (!PyArg_ParseTuple(args, "i", &g_verbose)) return nullptr;
+  Py_RETURN_NONE;
+}
+
+PyObject* py_set_yield_every(PyObject*, PyObject* args) {
+  unsigned long long every;
+  if (!PyArg_ParseTuple(args, "K", &every)) return nullptr;
+  for (int d = 0; d < kMaxDev; ++d)
+    if (g_rt[d]) {
+      const int st = gpuos_rt_set_yield_every(g_rt[d], every);
+      if (st) return raise_status(st);
+    }
+  Py_RETURN_NONE;
+}
+
+PyObject* py_set_idle_quiesce_ms(PyObject*, PyObject* args) {
+  int ms;
+  if (!PyArg_ParseTuple(args, "i", &ms)) return nullptr;
+  for (int d = 0; d < kMaxDev; ++d)
+    if (g_rt[d]) {
+      const int st = gpuos_rt_set_idle_quiesce_ms(g_rt[d], ms);
+      if (st) return raise_status(st);
+    }
+  Py_RETURN_NONE;
+}
+
+PyObject* py_worker_alive(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"device", nullptr};
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "|O", const_cast<char**>(kwlist), &devobj)) return nullptr;
+  if (devobj == Py_None) {
+    bool any = false;
+    for (int d = 0; d < kMaxDev; ++d) any |= (g_rt[d] && gpuos_rt_worker_alive(g_rt[d]));
+    return PyBool_FromLong(any);
+  }
+  gpuos_rt* rt = rt_arg(devobj, nullptr);
+  if (!rt) return nullptr;
+  return PyBool_FromLong(gpuos_rt_worker_alive(rt));
+}
+
+PyObject* py_quiesce(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"timeout_ms", "device", nullptr};
+  int timeout_ms = 30000;
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "|iO", const_cast<char**>(kwlist), &timeout_ms, &devobj)) return nullptr;
+  for (int d = 0; d < kMaxDev; ++d) {
+    if (!g_rt[d]) continue;
+    if (devobj != Py_None) {
+      int dev;
+      if (parse_device(devobj, &dev)) return nullptr;
+      if (dev != d) continue;
+    }
+    int st;
+    Py_BEGIN_ALLOW_THREADS st = gpuos_rt_quiesce(g_rt[d], timeout_ms);
+    Py_END_ALLOW_THREADS
+    if (st) return raise_status(st);
+  }
+  Py_RETURN_NONE;
+}
+
+PyObject* py_peek_queue(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"device", nullptr};
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "|O", const_cast<char**>(kwlist), &devobj)) return nullptr;
+  int dev = 0;
+  gpuos_rt* rt = rt_arg(devobj, &dev);
+  if (!rt) return nullptr;
+  int64_t v[32];
+  const int st = gpuos_rt_stats(rt, v, 32);
+  if (st) return raise_status(st);
+  PyObject* d = PyDict_New();
+  std::string names = gpuos_rt_stat_names();
+  size_t pos = 0;
+  int i = 0;
+  while (pos <= names.size() && i < 32) {
+    size_t c = names.find(',', pos);
+    if (c == std::string::npos) c = names.size();
+    const std::string key = names.substr(pos, c - pos);
+    PyObject* val = PyLong_FromLongLong(v[i++]);
+    PyDict_SetItemString(d, key.c_str(), val);
+    Py_DECREF(val);
+    pos = c + 1;
+  }
+  PyObject* t = Py_True;
+  PyDict_SetItemString(d, "sync_enabled", t);
+  PyObject* sv = PyUnicode_FromString("mapped");
+  PyDict_SetItemString(d, "staging", sv);
+  Py_DECREF(sv);
+  PyObject* dv = PyLong_FromLong(dev);
+  PyDict_SetItemString(d, "device", dv);
+  Py_DECREF(dv);
+  return d;
+}
+
+// ---- zero-copy sync API (gpuos_ext.cpp:1125-1141) ---------------------------------------
+PyObject* py_sync_poll_processed(PyObject*, PyObject*) {
+  uint64_t total = 0;
+  bool any = false;
+  for (int d = 0; d < kMaxDev; ++d)
+    if (g_rt[d]) {
+      total += gpuos_rt_poll_processed(g_rt[d]);
+      release_completed(d);
+      any = true;
+    }
+  if (!any) {
+    PyErr_SetString(PyExc_RuntimeError, "gpuos not initialized");
+    return nullptr;
+  }
+  return PyLong_FromUnsignedLongLong(total);
+}
+
+PyObject* py_sync_poll_heartbeat(PyObject*, PyObject*) {
+  gpuos_rt* rt = rt_arg(nullptr, nullptr);
+  if (!rt) return nullptr;
+  return PyLong_FromUnsignedLongLong(gpuos_rt_poll_heartbeat(rt));
+}
+
+PyObject* py_sync_poll_ready(PyObject*, PyObject*) {
+  gpuos_rt* rt = rt_arg(nullptr, nullptr);
+  if (!rt) return nullptr;
+  return PyBool_FromLong(gpuos_rt_poll_ready(rt));
+}
+
+PyObject* py_sync_enabled(PyObject*, PyObject*) {
+  for (int d = 0; d < kMaxDev; ++d)
+    if (g_rt[d]) Py_RETURN_TRUE;
+  Py_RETURN_FALSE;
+}
+
+PyObject* py_sync_wait(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"target", "timeout_ms", nullptr};
+  unsigned long long target;
+  int timeout_ms = 30000;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "K|i", const_cast<char**>(kwlist), &target, &timeout_ms)) return nullptr;
+  gpuos_rt* rt = rt_arg(nullptr, nullptr);
+  if (!rt) return nullptr;
+  int st;
+  Py_BEGIN_ALLOW_THREADS st = gpuos_rt_sync_wait(rt, target, timeout_ms);
+  Py_END_ALLOW_THREADS
+  if (st) return raise_status(st);
+  Py_RETURN_NONE;
+}
+
+PyObject* py_wait(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"seq", "timeout_ms", "device", nullptr};
+  unsigned long long seq;
+  int timeout_ms = 30000;
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "K|iO", const_cast<char**>(kwlist), &seq, &timeout_ms, &devobj))
+    return nullptr;
+  int dev = 0;
+  gpuos_rt* rt = rt_arg(devobj, &dev);
+  if (!rt) return nullptr;
+  int st;
+  Py_BEGIN_ALLOW_THREADS st = gpuos_rt_wait(rt, seq, timeout_ms);
+  Py_END_ALLOW_THREADS
+  if (st) return raise_status(st);
+  release_completed(dev);
+  Py_RETURN_NONE;
+}
+
+PyObject* py_completed(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"device", nullptr};
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "|O", const_cast<char**>(kwlist), &devobj)) return nullptr;
+  int dev = 0;
+  gpuos_rt* rt = rt_arg(devobj, &dev);
+  if (!rt) return nullptr;
+  const uint64_t c = gpuos_rt_completed(rt);
+  release_completed(dev);
+  return PyLong_FromUnsignedLongLong(c);
+}
+
+PyObject* py_flush_times(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"seq", "device", nullptr};
+  unsigned long long seq;
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "K|O", const_cast<char**>(kwlist), &seq, &devobj)) return nullptr;
+  gpuos_rt* rt = rt_arg(devobj, nullptr);
+  if (!rt) return nullptr;
+  uint64_t t0 = 0, t1 = 0;
+  const int st = gpuos_rt_flush_times(rt, seq, &t0, &t1);
+  if (st) return raise_status(st);
+  return Py_BuildValue("(KK)", (unsigned long long)t0, (unsigned long long)t1);
+}
+
+PyObject* py_kernel_stream(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"device", nullptr};
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "|O", const_cast<char**>(kwlist), &devobj)) return nullptr;
+  gpuos_rt* rt = rt_arg(devobj, nullptr);
+  if (!rt) return nullptr;
+  return PyLong_FromVoidPtr(reinterpret_cast<void*>(gpuos_rt_kernel_stream(rt)));
+}
+
+PyObject* py_set_device_wait_ms(PyObject*, PyObject* args) {
+  int ms;
+  if (!PyArg_ParseTuple(args, "i", &ms)) return nullptr;
+  for (int d = 0; d < kMaxDev; ++d)
+    if (g_rt[d]) {
+      const int st = gpuos_rt_set_device_wait_ms(g_rt[d], ms);
+      if (st) return raise_status(st);
+    }
+  Py_RETURN_NONE;
+}
+
+PyObject* py_debug_inject_stall(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"device", nullptr};
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "|O", const_cast<char**>(kwlist), &devobj)) return nullptr;
+  gpuos_rt* rt = rt_arg(devobj, nullptr);
+  if (!rt) return nullptr;
+  const int st = gpuos_rt_debug_inject_stall(rt);
+  if (st) return raise_status(st);
+  Py_RETURN_NONE;
+}
+
+PyObject* py_launches(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"device", nullptr};
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "|O", const_cast<char**>(kwlist), &devobj)) return nullptr;
+  gpuos_rt* rt = rt_arg(devobj, nullptr);
+  if (!rt) return nullptr;
+  return PyLong_FromUnsignedLongLong(gpuos_rt_launches(rt));
+}
+
+// ---- op table: slots, aliases, built-in registrations -------------------------------------
+PyObject* py_set_slot(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"slot", "fn", "device", nullptr};
+  int slot;
+  unsigned long long fn;
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "iK|O", const_cast<char**>(kwlist), &slot, &fn, &devobj)) return nullptr;
+  gpuos_rt* rt = rt_arg(devobj, nullptr);
+  if (!rt) return nullptr;
+  const int st = gpuos_rt_set_slot(rt, slot, fn);
+  if (st) return raise_status(st);
+  Py_RETURN_NONE;
+}
+
+PyObject* py_get_slot(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"slot", "device", nullptr};
+  int slot;
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "i|O", const_cast<char**>(kwlist), &slot, &devobj)) return nullptr;
+  gpuos_rt* rt = rt_arg(devobj, nullptr);
+  if (!rt) return nullptr;
+  OpPtrInt fn = 0;
+  const int st = gpuos_rt_get_slot(rt, slot, &fn);
+  if (st) return raise_status(st);
+  return PyLong_FromUnsignedLongLong(fn);
+}
+
+PyObject* py_set_alias(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"logical", "physical", "device", nullptr};
+  int lg, ph;
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "ii|O", const_cast<char**>(kwlist), &lg, &ph, &devobj)) return nullptr;
+  gpuos_rt* rt = rt_arg(devobj, nullptr);
+  if (!rt) return nullptr;
+  const int st = gpuos_rt_set_alias(rt, lg, ph);
+  if (st) return raise_status(st);
+  Py_RETURN_NONE;
+}
+
+PyObject* py_get_alias(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"logical", "device", nullptr};
+  int lg;
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "i|O", const_cast<char**>(kwlist), &lg, &devobj)) return nullptr;
+  gpuos_rt* rt = rt_arg(devobj, nullptr);
+  if (!rt) return nullptr;
+  int ph = -1;
+  const int st = gpuos_rt_get_alias(rt, lg, &ph);
+  if (st) return raise_status(st);
+  return PyLong_FromLong(ph);
+}
+
+PyObject* py_builtin_op_address(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"code", "device", nullptr};
+  int code;
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "i|O", const_cast<char**>(kwlist), &code, &devobj)) return nullptr;
+  int dev = 0;
+  gpuos_rt* rt = rt_arg(devobj, &dev);
+  if (!rt) return nullptr;
+  OpPtrInt addr = 0;
+  cudaSetDevice(dev);
+  cudaStream_t s = c10::cuda::getCurrentCUDAStream((c10::DeviceIndex)dev).stream();
+  cudaError_t e = gpu_get_builtin_op_async(code, &addr, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return PyErr_Format(PyExc_RuntimeError, "builtin_op_address: %s", cudaGetErrorString(e));
+  return PyLong_FromUnsignedLongLong(addr);
+}
+
+PyObject* py_register_builtin(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"kind", "op", "device", nullptr};
+  const char* kind;
+  int op;
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "si|O", const_cast<char**>(kwlist), &kind, &op, &devobj)) return nullptr;
+  gpuos_rt* rt = rt_arg(devobj, nullptr);
+  if (!rt) return nullptr;
+  int slot = -1;
+  int st;
+  if (std::strcmp(kind, "reduce") == 0) st = gpuos_rt_register_builtin_reduce(rt, op, &slot);
+  else if (std::strcmp(kind, "elementwise") == 0) st = gpuos_rt_register_builtin_ew(rt, op, &slot);
+  else return PyErr_Format(PyExc_ValueError, "kind must be 'reduce' or 'elementwise'");
+  if (st) return raise_status(st);
+  return PyLong_FromLong(slot);
+}
+
+PyObject* py_register_expr(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"key", "expr", "arity", "slot", "device", nullptr};
+  const char *key, *expr;
+  int arity, slot = -1;
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "ssi|iO", const_cast<char**>(kwlist), &key, &expr, &arity, &slot, &devobj))
+    return nullptr;
+  gpuos_rt* rt = rt_arg(devobj, nullptr);
+  if (!rt) return nullptr;
+  int out = -1, st;
+  Py_BEGIN_ALLOW_THREADS st = gpuos_rt_register_expr(rt, key, expr, arity, slot, &out);
+  Py_END_ALLOW_THREADS
+  if (st) return raise_status(st);
+  return PyLong_FromLong(out);
+}
+
+// ---- reference-layout Tasks (gpuos_ext.cpp:280-314, 884-896, 1016-1045) --------------------
+void fill_ref(TensorRef& tr, const GpuosOperand& t) {
+  std::memset(&tr, 0, sizeof(tr));
+  tr.data = t.data;
+  tr.dtype = t.dtype;
+  tr.ndim = t.ndim;
+  for (int d = 0; d < t.ndim; ++d) {
+    tr.sizes[d] = t.sizes[d];
+    tr.strides[d] = t.strides[d];
+  }
+}
+
+// Input aligned to the output dims: broadcast dims carry the output size and stride 0, so
+// decoding an output index with the input's own sizes gives the right coordinates.
+bool fill_ref_bcast(TensorRef& tr, const GpuosOperand& in, const GpuosOperand& out) {
+  std::memset(&tr, 0, sizeof(tr));
+  tr.data = in.data;
+  tr.dtype = in.dtype;
+  tr.ndim = out.ndim;
+  for (int d = 0; d < out.ndim; ++d) {
+    const int id = in.ndim - out.ndim + d;
+    const int64_t sz = id >= 0 ? in.sizes[id] : 1;
+    tr.sizes[d] = out.sizes[d];
+    if (sz == out.sizes[d]) tr.strides[d] = out.sizes[d] == 1 ? 0 : in.strides[id];
+    else if (sz == 1) tr.strides[d] = 0;
+    else return false;
+  }
+  return true;
+}
+
+PyObject* submit_task_common(int dev, const Task& t, PyObject* const* keep_objs, int nkeep) {
+  gpuos_rt* rt = rt_for(dev);
+  if (!rt) return nullptr;
+  int st = gpuos_rt_submit_task(rt, &t);
+  if (st) return raise_status(st);
+  for (int i = 0; i < nkeep; ++i) keep(dev, keep_objs[i]);
+  // The reference enqueues these Tasks directly (no flush needed): publish now.
+  uint64_t seq = 0;
+  st = flush_device(dev, false, &seq);
+  if (st) return raise_status(st);
+  Py_RETURN_NONE;
+}
+
+PyObject* py_submit_unary(PyObject*, PyObject* const* args, Py_ssize_t nargs) {
+  if (nargs != 3) {
+    PyErr_SetString(PyExc_TypeError, "expected (slot, a, out)");
+    return nullptr;
+  }
+  const long slot = PyLong_AsLong(args[0]);
+  if (slot == -1 && PyErr_Occurred()) return nullptr;
+  GpuosOperand a, out;
+  const int da = to_operand(args[1], &a, "a");
+  if (da < 0) return nullptr;
+  const int dout = to_operand(args[2], &out, "out");
+  if (dout < 0) return nullptr;
+  if (da != dout) {
+    PyErr_SetString(PyExc_RuntimeError, "device mismatch");
+    return nullptr;
+  }
+  Task t;
+  std::memset(&t, 0, sizeof(t));
+  t.op = (int)slot;
+  t.ndim = out.ndim;
+  t.numel = 1;
+  for (int d = 0; d < out.ndim; ++d) t.numel *= out.sizes[d];
+  fill_ref(t.out0, out);
+  if (!fill_ref_bcast(t.in0, a, out)) return PyErr_Format(PyExc_ValueError, "a does not broadcast to out");
+  t.in1.data = nullptr;
+  t.in1.dtype = t.in0.dtype;
+  t.in1.ndim = out.ndim;
+  for (int d = 0; d < out.ndim; ++d) t.in1.sizes[d] = 1;
+  PyObject* ks[2] = {args[1], args[2]};
+  return submit_task_common(dout, t, ks, 2);
+}
+
+PyObject* py_submit_binary(PyObject*, PyObject* const* args, Py_ssize_t nargs) {
+  if (nargs != 4) {
+    PyErr_SetString(PyExc_TypeError, "expected (slot, a, b, out)");
+    return nullptr;
+  }
+  const long slot = PyLong_AsLong(args[0]);
+  if (slot == -1 && PyErr_Occurred()) return nullptr;
+  GpuosOperand a, b, out;
+  const int da = to_operand(args[1], &a, "a");
+  if (da < 0) return nullptr;
+  const int db = to_operand(args[2], &b, "b");
+  if (db < 0) return nullptr;
+  const int dout = to_operand(args[3], &out, "out");
+  if (dout < 0) return nullptr;
+  if (da != dout || db != dout) {
+    PyErr_SetString(PyExc_RuntimeError, "device mismatch");
+    return nullptr;
+  }
+  Task t;
+  std::memset(&t, 0, sizeof(t));
+  t.op = (int)slot;
+  t.ndim = out.ndim;
+  t.numel = 1;
+  for (int d = 0; d < out.ndim; ++d) t.numel *= out.sizes[d];
+  fill_ref(t.out0, out);
+  if (!fill_ref_bcast(t.in0, a, out) || !fill_ref_bcast(t.in1, b, out))
+    return PyErr_Format(PyExc_ValueError, "operands do not broadcast to out");
+  PyObject* ks[3] = {args[1], args[2], args[3]};
+  return submit_task_common(dout, t, ks, 3);
+}
+
+PyObject* py_submit_reduce(PyObject*, PyObject* args) {
+  int slot, keepdim;
+  PyObject *xo, *oo, *axes_obj;
+  if (!PyArg_ParseTuple(args, "iOOOp", &slot, &xo, &oo, &axes_obj, &keepdim)) return nullptr;
+  GpuosOperand x, out;
+  const int dx = to_operand(xo, &x, "x");
+  if (dx < 0) return nullptr;
+  const int dout = to_operand(oo, &out, "out");
+  if (dout < 0) return nullptr;
+  if (dx != dout) {
+    PyErr_SetString(PyExc_RuntimeError, "device mismatch");
+    return nullptr;
+  }
+  std::vector<int> axes;
+  if (!parse_axes(axes_obj, &axes)) return nullptr;
+  if ((int)axes.size() > GPUOS_MAX_NDIM) return PyErr_Format(PyExc_ValueError, "too many axes");
+  Task t;
+  std::memset(&t, 0, sizeof(t));
+  t.op = slot;
+  t.ndim = out.ndim;
+  t.numel = 1;
+  for (int d = 0; d < out.ndim; ++d) t.numel *= out.sizes[d];
+  t.rrank = (int)axes.size();
+  for (size_t i = 0; i < axes.size(); ++i) {
+    int ax = axes[i] < 0 ? axes[i] + x.ndim : axes[i];
+    if (ax < 0 || ax >= x.ndim) return PyErr_Format(PyExc_ValueError, "axis %d out of range", axes[i]);
+    t.r_axes[i] = ax;
+  }
+  t.r_keepdim = keepdim;
+  fill_ref(t.in0, x);
+  fill_ref(t.out0, out);
+  t.in1.data = nullptr;
+  t.in1.ndim = out.ndim;
+  for (int d = 0; d < out.ndim; ++d) t.in1.sizes[d] = 1;
+  PyObject* ks[2] = {xo, oo};
+  return submit_task_common(dout, t, ks, 2);
+}
+
+PyMethodDef kMethods[] = {
+    {"init", (PyCFunction)(void (*)(void))py_init, METH_VARARGS | METH_KEYWORDS,
+     "init(capacity=4096, threads_per_block=256, device=None)"},
+    {"shutdown", (PyCFunction)(void (*)(void))py_shutdown, METH_VARARGS | METH_KEYWORDS, "shutdown(device=None)"},
+    {"abi_version", py_abi_version, METH_NOARGS, "extension ABI version"},
+    {"set_debug_level", py_set_debug_level, METH_VARARGS, "device debug print level"},
+    {"set_verbose_level", py_set_verbose_level, METH_VARARGS, "host verbose level"},
+    {"peek_queue", (PyCFunction)(void (*)(void))py_peek_queue, METH_VARARGS | METH_KEYWORDS, "queue state dict"},
+    {"set_yield_every", py_set_yield_every, METH_VARARGS, "worker exits after every N items (0 = never)"},
+    {"set_idle_quiesce_ms", py_set_idle_quiesce_ms, METH_VARARGS, "stop an idle worker after ms (0 = after every drain, -1 = never)"},
+    {"worker_alive", (PyCFunction)(void (*)(void))py_worker_alive, METH_VARARGS | METH_KEYWORDS, "worker kernel running"},
+    {"quiesce", (PyCFunction)(void (*)(void))py_quiesce, METH_VARARGS | METH_KEYWORDS, "drain and stop the worker"},
+    {"submit_add", (PyCFunction)(void (*)(void))py_submit_add, METH_FASTCALL, "out = a + b (pending until flush)"},
+    {"submit_mul", (PyCFunction)(void (*)(void))py_submit_mul, METH_FASTCALL, "out = a * b (pending until flush)"},
+    {"submit_sub", (PyCFunction)(void (*)(void))py_submit_sub, METH_FASTCALL, "out = a - b (pending until flush)"},
+    {"submit_div", (PyCFunction)(void (*)(void))py_submit_div, METH_FASTCALL, "out = a / b (pending until flush)"},
+    {"submit_elementwise", (PyCFunction)(void (*)(void))py_submit_elementwise, METH_FASTCALL,
+     "submit_elementwise(op, a, b, out, p0=0.0, p1=0.0)"},
+    {"submit_reduction", (PyCFunction)(void (*)(void))py_submit_reduction, METH_FASTCALL,
+     "submit_reduction(op, x, out, axes, keepdim)"},
+    {"flush", (PyCFunction)(void (*)(void))py_flush, METH_VARARGS | METH_KEYWORDS, "flush(sync=False, device=None) -> ticket"},
+    {"wait", (PyCFunction)(void (*)(void))py_wait, METH_VARARGS | METH_KEYWORDS, "wait(seq, timeout_ms=30000, device=None)"},
+    {"completed", (PyCFunction)(void (*)(void))py_completed, METH_VARARGS | METH_KEYWORDS, "highest completed ticket"},
+    {"flush_times", (PyCFunction)(void (*)(void))py_flush_times, METH_VARARGS | METH_KEYWORDS,
+     "device (t_start_ns, t_end_ns) of a completed flush"},
+    {"kernel_stream", (PyCFunction)(void (*)(void))py_kernel_stream, METH_VARARGS | METH_KEYWORDS,
+     "raw handle of the worker kernel's stream"},
+    {"launches", (PyCFunction)(void (*)(void))py_launches, METH_VARARGS | METH_KEYWORDS, "worker launches so far"},
+    {"set_device_wait_ms", py_set_device_wait_ms, METH_VARARGS, "bound of the worker's in-grid waits"},
+    {"debug_inject_stall", (PyCFunction)(void (*)(void))py_debug_inject_stall, METH_VARARGS | METH_KEYWORDS,
+     "publish an item whose dependency barrier never opens (failure-path test)"},
+    {"submit_unary", (PyCFunction)(void (*)(void))py_submit_unary, METH_FASTCALL, "submit_unary(slot, a, out)"},
+    {"submit_binary", (PyCFunction)(void (*)(void))py_submit_binary, METH_FASTCALL, "submit_binary(slot, a, b, out)"},
+    {"submit_reduce", py_submit_reduce, METH_VARARGS, "submit_reduce(slot, x, out, axes, keepdim)"},
+    {"set_slot", (PyCFunction)(void (*)(void))py_set_slot, METH_VARARGS | METH_KEYWORDS, "write a device function address into a slot"},
+    {"get_slot", (PyCFunction)(void (*)(void))py_get_slot, METH_VARARGS | METH_KEYWORDS, "read a slot"},
+    {"set_alias", (PyCFunction)(void (*)(void))py_set_alias, METH_VARARGS | METH_KEYWORDS, "route logical op to a physical slot"},
+    {"get_alias", (PyCFunction)(void (*)(void))py_get_alias, METH_VARARGS | METH_KEYWORDS, "read an alias"},
+    {"builtin_op_address", (PyCFunction)(void (*)(void))py_builtin_op_address, METH_VARARGS | METH_KEYWORDS,
+     "device address of a built-in reference-ABI operator"},
+    {"register_builtin", (PyCFunction)(void (*)(void))py_register_builtin, METH_VARARGS | METH_KEYWORDS,
+     "register_builtin(kind, op) -> slot"},
+    {"register_expr", (PyCFunction)(void (*)(void))py_register_expr, METH_VARARGS | METH_KEYWORDS,
+     "NVRTC-compile an expression operator into a slot"},
+    {"sync_poll_processed", py_sync_poll_processed, METH_NOARGS, "completed requests (zero-copy)"},
+    {"sync_poll_heartbeat", py_sync_poll_heartbeat, METH_NOARGS, "worker heartbeat (zero-copy)"},
+    {"sync_poll_ready", py_sync_poll_ready, METH_NOARGS, "worker ready (zero-copy)"},
+    {"sync_wait", (PyCFunction)(void (*)(void))py_sync_wait, METH_VARARGS | METH_KEYWORDS,
+     "sync_wait(target, timeout_ms=30000)"},
+    {"sync_enabled", py_sync_enabled, METH_NOARGS, "zero-copy sync available"},
+    {nullptr, nullptr, 0, nullptr}};
+
+PyModuleDef kModule = {PyModuleDef_HEAD_INIT, "_gpuos_ext", "B200 persistent micro-op runtime binding", -1,
+                       kMethods};
+
+}  // namespace
+
+PyMODINIT_FUNC PyInit__gpuos_ext(void) {
+  PyObject* m = PyModule_Create(&kModule);
+  if (!m) return nullptr;
+  struct {
+    const char* n;
+    int v;
+  } consts[] = {{"EW_ADD", GPUOS_EW_ADD},
+                {"EW_MUL", GPUOS_EW_MUL},
+                {"EW_SUB", GPUOS_EW_SUB},
+                {"EW_DIV", GPUOS_EW_DIV},
+                {"EW_MAXIMUM", GPUOS_EW_MAXIMUM},
+                {"EW_MINIMUM", GPUOS_EW_MINIMUM},
+                {"EW_POW", GPUOS_EW_POW},
+                {"EW_COPY", GPUOS_EW_COPY},
+                {"EW_RELU", GPUOS_EW_RELU},
+                {"EW_SIGMOID", GPUOS_EW_SIGMOID},
+                {"EW_TANH", GPUOS_EW_TANH},
+                {"EW_EXP", GPUOS_EW_EXP},
+                {"EW_LOG", GPUOS_EW_LOG},
+                {"EW_SQRT", GPUOS_EW_SQRT},
+                {"EW_ABS", GPUOS_EW_ABS},
+                {"EW_HARDSIGMOID", GPUOS_EW_HARDSIGMOID},
+                {"EW_HARDSWISH", GPUOS_EW_HARDSWISH},
+                {"EW_GELU", GPUOS_EW_GELU},
+                {"EW_GELU_TANH", GPUOS_EW_GELU_TANH},
+                {"EW_SIN", GPUOS_EW_SIN},
+                {"EW_COS", GPUOS_EW_COS},
+                {"EW_LEAKY_RELU", GPUOS_EW_LEAKY_RELU},
+                {"EW_CLAMP", GPUOS_EW_CLAMP},
+                {"EW_CLAMP_MIN", GPUOS_EW_CLAMP_MIN},
+                {"EW_CLAMP_MAX", GPUOS_EW_CLAMP_MAX},
+                {"EW_ELU", GPUOS_EW_ELU},
+                {"EW_SOFTPLUS", GPUOS_EW_SOFTPLUS},
+                {"EW_NEG", GPUOS_EW_NEG},
+                {"EW_ADD_ALPHA", GPUOS_EW_ADD_ALPHA},
+                {"EW_SUB_ALPHA", GPUOS_EW_SUB_ALPHA},
+                {"EW_NUM_OPS", GPUOS_EW_NUM_OPS},
+                {"RED_SUM", GPUOS_RED_SUM},
+                {"RED_MEAN", GPUOS_RED_MEAN},
+                {"GPUOS_MAX_OPS", GPUOS_MAX_OPS}};
+  for (auto& c : consts) PyModule_AddIntConstant(m, c.n, c.v);
+  return m;
+}

@@ -1,0 +1,1470 @@
+// runtime.cpp — host runtime of the persistent micro-op worker (C ABI: gpuos_rt_*).
+//
+// Reference: pytorch_ext/gpuos_ext.cpp.  The reference keeps one global queue on device 0,
+// appends 496-byte Tasks to a vector, and at flush copies them to the device with a
+// blocking cudaMemcpy, hashes them (FNV-1a over the whole array), enqueues 512-request
+// shards with ~3 CUDA calls each and waits until a global completion count reaches
+// "before + shards" (gpuos_ext.cpp:675-811).  This runtime:
+//   * keeps one instance per device (queue, control blocks, worker);
+//   * plans each request into 64-byte work items as it is submitted, written straight
+//     into a ring in mapped pinned memory, so a flush is a single store of the tail
+//     (no CUDA call unless the worker has to be (re)launched);
+//   * orders dependent requests inside and across flushes with segment barriers
+//     derived from the byte ranges the requests read and write;
+//   * tracks completion per flush with a ticket the device writes, so sync flushes wait
+//     for exactly their own work;
+//   * never calls exit(): every failure is a status code plus a message.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <deque>
+#include <map>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "internal.h"
+
+using namespace gpuos;
+
+extern "C" cudaError_t gpuos_internal_launch_batch_worker(const WorkerParams* p, int blocks, int threads,
+                                                          size_t smem, cudaStream_t s);
+extern "C" cudaError_t gpuos_internal_set_worker_smem(size_t smem);
+extern "C" cudaError_t gpuos_internal_table_ptrs(void** table, void** alias);
+extern "C" size_t gpuos_internal_smem_header_bytes();
+
+// ---- errors -----------------------------------------------------------------------------
+static thread_local std::string t_last_error;
+
+static int fail(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+#define CK(expr)                                                                              \
+  do {                                                                                        \
+    cudaError_t _e = (expr);                                                                  \
+    if (_e != cudaSuccess)                                                                    \
+      return fail(GPUOS_ERR_CUDA, "%s failed: %s (%s:%d)", #expr, cudaGetErrorString(_e), __FILE__, __LINE__); \
+  } while (0)
+
+extern "C" const char* gpuos_rt_last_error(void) { return t_last_error.c_str(); }
+
+static uint64_t mono_ns() {
+  return (uint64_t)std::chrono::duration_cast<std::chrono::nanoseconds>(
+             std::chrono::steady_clock::now().time_since_epoch())
+      .count();
+}
+
+static inline void cpu_relax() {
+#if defined(__x86_64__)
+  __builtin_ia32_pause();
+#else
+  std::this_thread::yield();
+#endif
+}
+
+static uint64_t pow2_at_least(uint64_t v) {
+  uint64_t p = 1;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+static int env_int(const char* name, int dflt) {
+  const char* v = std::getenv(name);
+  if (!v || !*v) return dflt;
+  return std::atoi(v);
+}
+
+// =========================================================================================
+// Planner (no CUDA calls)
+// =========================================================================================
+namespace {
+
+struct Dims {
+  int nd = 0;
+  int64_t size[GPUOS_MAX_NDIM];
+  int64_t st[3][GPUOS_MAX_NDIM];
+};
+
+struct Range {
+  uint64_t lo = 0, hi = 0;
+  bool empty() const { return hi <= lo; }
+};
+
+bool dtype_ok(int dt) { return dt == kF32 || dt == kF16 || dt == kBF16; }
+
+Range operand_range(const void* data, int dtype, int ndim, const int64_t* sizes, const int64_t* strides) {
+  Range r;
+  int64_t lo = 0, hi = 0;
+  for (int d = 0; d < ndim; ++d) {
+    if (sizes[d] == 0) return r;
+    const int64_t ext = (sizes[d] - 1) * strides[d];
+    if (ext < 0) lo += ext;
+    else hi += ext;
+  }
+  const int es = dtype_size(dtype);
+  r.lo = (uint64_t)((int64_t)(uintptr_t)data + lo * es);
+  r.hi = (uint64_t)((int64_t)(uintptr_t)data + (hi + 1) * es);
+  return r;
+}
+
+Range operand_range(const GpuosOperand& t) { return operand_range(t.data, t.dtype, t.ndim, t.sizes, t.strides); }
+
+int64_t numel_of(int ndim, const int64_t* sizes) {
+  int64_t n = 1;
+  for (int d = 0; d < ndim; ++d) n *= sizes[d];
+  return n;
+}
+
+// Right-aligned broadcast of `in` against the output dims (gpuos_ext.cpp:260-278).
+bool align_operand(const GpuosOperand& in, const GpuosOperand& out, int64_t* st, std::string* err) {
+  const int nd = out.ndim;
+  if (in.ndim > nd) {
+    for (int d = 0; d < in.ndim - nd; ++d)
+      if (in.sizes[d] != 1) {
+        *err = "operand has more dimensions than the output";
+        return false;
+      }
+  }
+  for (int d = 0; d < nd; ++d) {
+    const int id = in.ndim - nd + d;
+    if (id < 0) {
+      st[d] = 0;
+      continue;
+    }
+    if (in.sizes[id] == out.sizes[d]) {
+      st[d] = out.sizes[d] == 1 ? 0 : in.strides[id];
+    } else if (in.sizes[id] == 1) {
+      st[d] = 0;
+    } else {
+      *err = "operand shape does not broadcast to the output shape";
+      return false;
+    }
+  }
+  return true;
+}
+
+void coalesce(Dims* d, int nops) {
+  Dims r;
+  r.nd = 0;
+  for (int i = 0; i < d->nd; ++i) {
+    if (d->size[i] == 1) continue;
+    r.size[r.nd] = d->size[i];
+    for (int k = 0; k < nops; ++k) r.st[k][r.nd] = d->st[k][i];
+    ++r.nd;
+  }
+  // merge right to left
+  Dims m;
+  m.nd = 0;
+  for (int i = 0; i < r.nd; ++i) {
+    if (m.nd > 0) {
+      bool ok = true;
+      // previous (outer) dim m.nd-1 merges with inner dim i when outer stride == inner stride * inner size
+      for (int k = 0; k < nops; ++k)
+        if (m.st[k][m.nd - 1] != r.st[k][i] * r.size[i]) ok = false;
+      if (ok) {
+        m.size[m.nd - 1] *= r.size[i];
+        for (int k = 0; k < nops; ++k) m.st[k][m.nd - 1] = r.st[k][i];
+        continue;
+      }
+    }
+    m.size[m.nd] = r.size[i];
+    for (int k = 0; k < nops; ++k) m.st[k][m.nd] = r.st[k][i];
+    ++m.nd;
+  }
+  *d = m;
+}
+
+struct EwReq {
+  int op;
+  const GpuosOperand* a;
+  const GpuosOperand* b;  // tensor operand or null
+  bool b_imm;
+  float b_val;
+  const GpuosOperand* out;
+  float params[4];
+};
+
+struct Plan {
+  std::vector<WorkItem> items;
+  bool has_layout = false;
+  Layout layout;
+  Range reads[2];
+  int nreads = 0;
+  Range write;
+};
+
+constexpr uint32_t kGenericTile = 8192;
+
+int plan_ew(const EwReq& r, uint32_t half_bytes, Plan* p) {
+  std::string err;
+  if (r.op < 0 || r.op >= GPUOS_EW_NUM_OPS) return fail(GPUOS_ERR_INVALID, "unknown element-wise op %d", r.op);
+  const GpuosOperand& out = *r.out;
+  if (!r.a || !dtype_ok(r.a->dtype) || !dtype_ok(out.dtype))
+    return fail(GPUOS_ERR_INVALID, "unsupported dtype (only float32, float16 and bfloat16 are computed)");
+  const bool binary = ew_arity(r.op) == 2;
+  if (binary && !r.b && !r.b_imm) return fail(GPUOS_ERR_INVALID, "binary op without a second operand");
+  const GpuosOperand* b = binary ? r.b : nullptr;
+  if (b && !dtype_ok(b->dtype)) return fail(GPUOS_ERR_INVALID, "unsupported dtype for the second operand");
+  if (out.ndim < 0 || out.ndim > GPUOS_MAX_NDIM || r.a->ndim < 0 || r.a->ndim > GPUOS_MAX_NDIM ||
+      (b && (b->ndim < 0 || b->ndim > GPUOS_MAX_NDIM)))
+    return fail(GPUOS_ERR_INVALID, "at most %d dimensions are supported", GPUOS_MAX_NDIM);
+  for (int d = 0; d < out.ndim; ++d)
+    if (out.sizes[d] < 0 || out.strides[d] < 0) return fail(GPUOS_ERR_INVALID, "negative size or stride");
+  const int64_t n = numel_of(out.ndim, out.sizes);
+  p->items.clear();
+  p->has_layout = false;
+  p->nreads = 0;
+  if (n == 0) return GPUOS_OK;
+  if (!out.data || !r.a->data || (b && !b->data)) return fail(GPUOS_ERR_INVALID, "null data pointer");
+
+  Dims d;
+  d.nd = out.ndim;
+  for (int i = 0; i < out.ndim; ++i) {
+    d.size[i] = out.sizes[i];
+    d.st[2][i] = out.sizes[i] == 1 ? 0 : out.strides[i];
+  }
+  if (!align_operand(*r.a, out, d.st[0], &err)) return fail(GPUOS_ERR_INVALID, "%s", err.c_str());
+  if (b) {
+    if (!align_operand(*b, out, d.st[1], &err)) return fail(GPUOS_ERR_INVALID, "%s", err.c_str());
+  } else {
+    for (int i = 0; i < out.ndim; ++i) d.st[1][i] = 0;
+  }
+  // output must not overlap itself (a broadcast output cannot be written element-wise)
+  for (int i = 0; i < out.ndim; ++i)
+    if (out.sizes[i] > 1 && out.strides[i] == 0) return fail(GPUOS_ERR_INVALID, "output has a zero stride");
+  coalesce(&d, 3);
+  if (d.nd == 0) {
+    d.nd = 1;
+    d.size[0] = 1;
+    d.st[0][0] = 0;
+    d.st[1][0] = 0;
+    d.st[2][0] = 1;
+  }
+  p->reads[p->nreads++] = operand_range(*r.a);
+  if (b) p->reads[p->nreads++] = operand_range(*b);
+  p->write = operand_range(out);
+
+  const int esa = dtype_size(r.a->dtype), eso = dtype_size(out.dtype);
+  const int esb = b ? dtype_size(b->dtype) : 4;
+  uint8_t base_flags = 0;
+  if (binary) base_flags |= IF_B_PRESENT;
+  if (binary && r.b_imm && !b) base_flags |= IF_B_SCALAR;
+  const uint64_t bimm_bits = [&] {
+    uint32_t u;
+    std::memcpy(&u, &r.b_val, 4);
+    return (uint64_t)u;
+  }();
+
+  const bool contig = d.nd == 1 && d.st[2][0] == 1 && (d.st[0][0] == 1 || d.st[0][0] == 0) &&
+                      (!b || d.st[1][0] == 1 || d.st[1][0] == 0);
+  WorkItem proto;
+  std::memset(&proto, 0, sizeof(proto));
+  proto.op = (uint8_t)r.op;
+  proto.dt_a = (uint8_t)r.a->dtype;
+  proto.dt_b = (uint8_t)(b ? b->dtype : kF32);
+  proto.dt_o = (uint8_t)out.dtype;
+  proto.aux = 0xffffffffu;
+  if (contig) {
+    const bool a_vec = d.st[0][0] == 1;
+    const bool b_vec = b && d.st[1][0] == 1;
+    int es_max = 1;
+    if (a_vec) es_max = std::max(es_max, esa);
+    if (b_vec) es_max = std::max(es_max, esb);
+    if (!a_vec && !b_vec) es_max = 4;
+    const uint32_t tile = half_bytes / (uint32_t)es_max;
+    uint32_t p0u, p1u;
+    std::memcpy(&p0u, &r.params[0], 4);
+    std::memcpy(&p1u, &r.params[1], 4);
+    proto.kind = IK_EW_CONTIG;
+    proto.x = (uint64_t)p0u | ((uint64_t)p1u << 32);
+    proto.flags = base_flags | (a_vec ? 0 : IF_A_BCAST) | ((b && !b_vec) ? IF_B_BCAST : 0);
+    const uint64_t A = (uint64_t)(uintptr_t)r.a->data, B = b ? (uint64_t)(uintptr_t)b->data : bimm_bits,
+                   O = (uint64_t)(uintptr_t)out.data;
+    for (int64_t s = 0; s < n; s += tile) {
+      WorkItem it = proto;
+      it.count = (uint32_t)std::min<int64_t>(tile, n - s);
+      it.a = A + (a_vec ? (uint64_t)s * esa : 0);
+      it.b = b ? (B + (b_vec ? (uint64_t)s * esb : 0)) : (r.b_imm ? bimm_bits : 0);
+      it.o = O + (uint64_t)s * eso;
+      p->items.push_back(it);
+    }
+    return GPUOS_OK;
+  }
+  // strided / broadcast: layout record shared by the request's tiles
+  p->has_layout = true;
+  Layout& L = p->layout;
+  std::memset(&L, 0, sizeof(L));
+  L.ndim = d.nd;
+  for (int i = 0; i < d.nd; ++i) {
+    L.sizes[i] = d.size[i];
+    L.sa[i] = d.st[0][i];
+    L.sb[i] = d.st[1][i];
+    L.so[i] = d.st[2][i];
+  }
+  for (int i = 0; i < 4; ++i) L.params[i] = r.params[i];
+  proto.kind = IK_EW_GENERIC;
+  proto.flags = base_flags;
+  for (int64_t s = 0; s < n; s += kGenericTile) {
+    WorkItem it = proto;
+    it.count = (uint32_t)std::min<int64_t>(kGenericTile, n - s);
+    it.a = (uint64_t)(uintptr_t)r.a->data;
+    it.b = b ? (uint64_t)(uintptr_t)b->data : (r.b_imm ? bimm_bits : 0);
+    it.o = (uint64_t)(uintptr_t)out.data;
+    it.x = (uint64_t)s;
+    p->items.push_back(it);
+  }
+  return GPUOS_OK;
+}
+
+int plan_reduce(int rop, const GpuosOperand& x, const GpuosOperand& out, const int* axes, int naxes, int keepdim,
+                uint32_t stage_bytes, Plan* p) {
+  if (rop != GPUOS_RED_SUM && rop != GPUOS_RED_MEAN) return fail(GPUOS_ERR_INVALID, "unknown reduction %d", rop);
+  if (!dtype_ok(x.dtype) || !dtype_ok(out.dtype))
+    return fail(GPUOS_ERR_INVALID, "unsupported dtype (only float32, float16 and bfloat16 are computed)");
+  if (x.ndim < 0 || x.ndim > GPUOS_MAX_NDIM || out.ndim < 0 || out.ndim > GPUOS_MAX_NDIM)
+    return fail(GPUOS_ERR_INVALID, "at most %d dimensions are supported", GPUOS_MAX_NDIM);
+  bool red[GPUOS_MAX_NDIM] = {false};
+  if (naxes == 0) {
+    for (int d = 0; d < x.ndim; ++d) red[d] = true;
+  }
+  for (int i = 0; i < naxes; ++i) {
+    int a = axes[i];
+    if (a < 0) a += x.ndim;
+    if (a < 0 || a >= x.ndim) return fail(GPUOS_ERR_INVALID, "reduction axis %d out of range", axes[i]);
+    if (red[a]) return fail(GPUOS_ERR_INVALID, "duplicate reduction axis %d", axes[i]);
+    red[a] = true;
+  }
+  // expected output shape
+  int64_t exp_sizes[GPUOS_MAX_NDIM];
+  int exp_nd = 0;
+  for (int d = 0; d < x.ndim; ++d) {
+    if (red[d]) {
+      if (keepdim) exp_sizes[exp_nd++] = 1;
+    } else {
+      exp_sizes[exp_nd++] = x.sizes[d];
+    }
+  }
+  if (exp_nd != out.ndim) return fail(GPUOS_ERR_INVALID, "output rank %d does not match reduction result rank %d", out.ndim, exp_nd);
+  for (int d = 0; d < exp_nd; ++d)
+    if (exp_sizes[d] != out.sizes[d]) return fail(GPUOS_ERR_INVALID, "output shape does not match the reduction result");
+  p->items.clear();
+  p->has_layout = false;
+  p->nreads = 0;
+  const int64_t nout = numel_of(out.ndim, out.sizes);
+  if (nout == 0) return GPUOS_OK;
+  if (!x.data || !out.data) return fail(GPUOS_ERR_INVALID, "null data pointer");
+
+  Dims kept, rd;
+  kept.nd = 0;
+  rd.nd = 0;
+  int od = 0;
+  for (int d = 0; d < x.ndim; ++d) {
+    if (red[d]) {
+      rd.size[rd.nd] = x.sizes[d];
+      rd.st[0][rd.nd] = x.strides[d];
+      ++rd.nd;
+      if (keepdim) ++od;
+    } else {
+      kept.size[kept.nd] = x.sizes[d];
+      kept.st[0][kept.nd] = x.strides[d];
+      kept.st[1][kept.nd] = out.strides[od];
+      ++kept.nd;
+      ++od;
+    }
+  }
+  coalesce(&kept, 2);
+  coalesce(&rd, 1);
+  int64_t rtotal = 1;
+  for (int i = 0; i < rd.nd; ++i) rtotal *= rd.size[i];
+  p->reads[p->nreads++] = operand_range(x);
+  p->write = operand_range(out);
+  const int es = dtype_size(x.dtype);
+
+  WorkItem proto;
+  std::memset(&proto, 0, sizeof(proto));
+  proto.op = (uint8_t)rop;
+  proto.dt_a = (uint8_t)x.dtype;
+  proto.dt_o = (uint8_t)out.dtype;
+  proto.flags = rop == GPUOS_RED_MEAN ? IF_MEAN : 0;
+  proto.aux = 0xffffffffu;
+
+  // Row case: one reduced dim, at most one kept dim with a contiguous output, and rows that
+  // do not interleave.
+  if (rd.nd == 1 && kept.nd <= 1 && (kept.nd == 0 || kept.st[1][0] == 1)) {
+    const int64_t C = rd.size[0], is = rd.st[0][0];
+    const int64_t rows = kept.nd ? kept.size[0] : 1;
+    const int64_t rs = kept.nd ? kept.st[0][0] : 0;
+    if (is >= 1 && (rows == 1 || C * is <= rs) && C <= 0x7fffffff) {
+      const int64_t row_span = ((C - 1) * is + 1) * es;
+      int64_t rows_per;
+      uint8_t fl = proto.flags;
+      const bool gaps = rows > 1 && rs * es > 2 * row_span;
+      if (row_span + 32 <= (int64_t)stage_bytes && !gaps) {
+        rows_per = rows > 1 ? 1 + ((int64_t)stage_bytes - 32 - row_span) / (rs * es) : 1;
+      } else {
+        fl |= IF_UNSTAGED;
+        rows_per = std::max<int64_t>(1, 16384 / C);
+      }
+      rows_per = std::max<int64_t>(1, std::min<int64_t>(rows_per, 1 << 16));
+      proto.kind = IK_ROW_REDUCE;
+      proto.flags = fl;
+      proto.aux = (uint32_t)C;
+      const int eso = dtype_size(out.dtype);
+      for (int64_t r0 = 0; r0 < rows; r0 += rows_per) {
+        WorkItem it = proto;
+        it.count = (uint32_t)std::min<int64_t>(rows_per, rows - r0);
+        it.a = (uint64_t)(uintptr_t)x.data + (uint64_t)(r0 * rs * es);
+        it.o = (uint64_t)(uintptr_t)out.data + (uint64_t)(r0 * eso);
+        it.x = (uint64_t)rs;
+        it.b = (uint64_t)is;
+        p->items.push_back(it);
+      }
+      return GPUOS_OK;
+    }
+  }
+  p->has_layout = true;
+  Layout& L = p->layout;
+  std::memset(&L, 0, sizeof(L));
+  L.ndim = kept.nd;
+  for (int i = 0; i < kept.nd; ++i) {
+    L.sizes[i] = kept.size[i];
+    L.sa[i] = kept.st[0][i];
+    L.so[i] = kept.st[1][i];
+  }
+  L.rdim = rd.nd;
+  for (int i = 0; i < rd.nd; ++i) {
+    L.rsizes[i] = rd.size[i];
+    L.rsa[i] = rd.st[0][i];
+  }
+  L.rtotal = rtotal;
+  proto.kind = IK_RED_GENERIC;
+  const int64_t per = std::max<int64_t>(1, std::min<int64_t>(8192, 262144 / std::max<int64_t>(rtotal, 1)));
+  for (int64_t s = 0; s < nout; s += per) {
+    WorkItem it = proto;
+    it.count = (uint32_t)std::min<int64_t>(per, nout - s);
+    it.a = (uint64_t)(uintptr_t)x.data;
+    it.o = (uint64_t)(uintptr_t)out.data;
+    it.x = (uint64_t)s;
+    p->items.push_back(it);
+  }
+  return GPUOS_OK;
+}
+
+// ---- hazard tracking --------------------------------------------------------------------
+// Byte ranges read and written by the requests of the current segment, bucketed by
+// 64 KiB block.  A request that reads a range written in the segment, or writes a range
+// read or written in the segment, starts a new segment whose items wait for every
+// earlier item (WorkItem::wait_items).
+class HazardMap {
+ public:
+  HazardMap() : table_(1 << 16) {}
+
+  void clear() {
+    ++gen_;
+    pool_.clear();
+    large_.clear();
+  }
+  size_t size() const { return pool_.size() + large_.size(); }
+
+  // true if r (read when !write) conflicts with the segment
+  bool conflicts(const Range& r, bool write) const {
+    if (r.empty()) return false;
+    for (const Ent& e : large_)
+      if ((write || e.write) && overlap(e, r)) return true;
+    const uint64_t b0 = r.lo >> kShift, b1 = (r.hi - 1) >> kShift;
+    if (b1 - b0 > kMaxBlocks) {
+      // scan everything for a huge range
+      for (const Ent& e : pool_)
+        if ((write || e.write) && overlap(e, r)) return true;
+      return false;
+    }
+    for (uint64_t blk = b0; blk <= b1; ++blk) {
+      const Slot* s = find(blk);
+      if (!s) continue;
+      for (int32_t i = s->head; i >= 0; i = pool_[i].next)
+        if ((write || pool_[i].write) && overlap(pool_[i], r)) return true;
+    }
+    return false;
+  }
+
+  void insert(const Range& r, bool write) {
+    if (r.empty()) return;
+    const uint64_t b0 = r.lo >> kShift, b1 = (r.hi - 1) >> kShift;
+    if (b1 - b0 > kMaxBlocks) {
+      large_.push_back(Ent{r.lo, r.hi, write, -1});
+      return;
+    }
+    for (uint64_t blk = b0; blk <= b1; ++blk) {
+      Slot* s = find_or_add(blk);
+      pool_.push_back(Ent{r.lo, r.hi, write, s->head});
+      s->head = (int32_t)pool_.size() - 1;
+    }
+  }
+
+ private:
+  static constexpr int kShift = 16;
+  static constexpr uint64_t kMaxBlocks = 64;
+  struct Ent {
+    uint64_t lo, hi;
+    bool write;
+    int32_t next;
+  };
+  struct Slot {
+    uint64_t key = 0;
+    uint32_t gen = 0;
+    int32_t head = -1;
+  };
+  static bool overlap(const Ent& e, const Range& r) { return e.lo < r.hi && r.lo < e.hi; }
+  static uint64_t hash(uint64_t k) {
+    k ^= k >> 33;
+    k *= 0xff51afd7ed558ccdull;
+    k ^= k >> 33;
+    return k;
+  }
+  const Slot* find(uint64_t key) const {
+    const size_t mask = table_.size() - 1;
+    for (size_t i = hash(key) & mask;; i = (i + 1) & mask) {
+      const Slot& s = table_[i];
+      if (s.gen != gen_) return nullptr;
+      if (s.key == key) return &s;
+    }
+  }
+  Slot* find_or_add(uint64_t key) {
+    if (used_gen_ != gen_) {
+      used_ = 0;
+      used_gen_ = gen_;
+    }
+    if (used_ * 2 >= table_.size()) grow();
+    const size_t mask = table_.size() - 1;
+    for (size_t i = hash(key) & mask;; i = (i + 1) & mask) {
+      Slot& s = table_[i];
+      if (s.gen != gen_) {
+        s.gen = gen_;
+        s.key = key;
+        s.head = -1;
+        ++used_;
+        return &s;
+      }
+      if (s.key == key) return &s;
+    }
+  }
+  void grow() {
+    std::vector<Slot> old;
+    old.swap(table_);
+    table_.assign(old.size() * 2, Slot());
+    const size_t mask = table_.size() - 1;
+    for (const Slot& s : old) {
+      if (s.gen != gen_) continue;
+      for (size_t i = hash(s.key) & mask;; i = (i + 1) & mask)
+        if (table_[i].gen != gen_) {
+          table_[i] = s;
+          break;
+        }
+    }
+  }
+  std::vector<Slot> table_;
+  std::vector<Ent> pool_;
+  std::vector<Ent> large_;
+  uint32_t gen_ = 1;
+  uint32_t used_gen_ = 0;
+  size_t used_ = 0;
+};
+
+}  // namespace
+
+// =========================================================================================
+// Runtime
+// =========================================================================================
+struct BatchInfo {
+  uint64_t seq;
+  uint64_t first_item, n_items;
+  uint64_t n_reqs;
+  uint64_t task_end, layout_end;
+  bool done;
+};
+
+struct gpuos_rt {
+  int device = 0;
+  int capacity = 0;
+  int tpb = 0;
+  int sm_count = 0;
+  uint32_t stages = 4;
+  uint32_t stage_bytes = kStageBytesDefault;
+  size_t smem = 0;
+  cudaStream_t kstream = nullptr, cstream = nullptr;
+
+  // mapped pinned block
+  void* host_block = nullptr;
+  HostCtl* hc = nullptr;
+  DevReport* rep = nullptr;
+  SyncState* sync = nullptr;
+  Ticket* tickets = nullptr;
+  WorkItem* items = nullptr;
+  Task* tasks = nullptr;
+  Layout* layouts = nullptr;
+  uint64_t item_cap = 0, task_cap = 0, layout_cap = 0;
+  DevCtl* dc = nullptr;
+  void* op_table = nullptr;
+  void* op_alias = nullptr;
+
+  std::mutex mu;
+  // producer cursors
+  uint64_t item_w = 0;    // next item index to write
+  uint64_t item_pub = 0;  // items published (tail)
+  uint64_t task_w = 0, layout_w = 0;
+  uint64_t pend_reqs = 0;
+  uint64_t seg_wait = 0;  // wait_items of new items
+  HazardMap hz;
+  // batches
+  uint64_t last_seq = 0;
+  std::deque<BatchInfo> inflight;
+  uint64_t completed_seq = 0;  // every seq <= completed_seq done
+  uint64_t processed = 0;      // completed requests
+  uint64_t submitted = 0;      // submitted requests
+  uint64_t oldest_item = 0, oldest_task = 0, oldest_layout = 0;
+  // worker
+  uint64_t epoch = 0;
+  bool launched = false;
+  int idle_quiesce_ms = 200;
+  uint64_t last_activity_ns = 0;
+  bool failed = false;
+  std::string fail_msg;
+  // keeper
+  std::thread keeper;
+  std::atomic<bool> stop{false};
+  int next_slot = 20;
+  int verbose = 0;
+};
+
+static std::mutex g_rt_mu;
+static std::map<int, gpuos_rt*> g_rts;
+
+extern "C" gpuos_rt* gpuos_rt_get(int device) {
+  std::lock_guard<std::mutex> lk(g_rt_mu);
+  auto it = g_rts.find(device);
+  return it == g_rts.end() ? nullptr : it->second;
+}
+
+// ---- completion reaping -------------------------------------------------------------------
+static void reap_locked(gpuos_rt* rt) {
+  for (BatchInfo& b : rt->inflight) {
+    if (!b.done) {
+      const Ticket& tk = rt->tickets[b.seq % kNumBatchSlots];
+      if (tk.seq == (uint32_t)b.seq) b.done = true;
+    }
+  }
+  while (!rt->inflight.empty() && rt->inflight.front().done) {
+    const BatchInfo& b = rt->inflight.front();
+    rt->completed_seq = b.seq;
+    rt->processed += b.n_reqs;
+    rt->oldest_item = b.first_item + b.n_items;
+    rt->oldest_task = b.task_end;
+    rt->oldest_layout = b.layout_end;
+    rt->inflight.pop_front();
+  }
+  if (rt->inflight.empty()) {
+    rt->oldest_item = rt->item_pub;
+    if (rt->pend_reqs == 0 && rt->item_w == rt->item_pub) {
+      // nothing outstanding: every earlier range is complete
+      rt->hz.clear();
+      rt->oldest_task = rt->task_w;
+      rt->oldest_layout = rt->layout_w;
+    }
+  }
+  if (rt->sync) rt->sync->processed = rt->processed;
+}
+
+static int check_device_error_locked(gpuos_rt* rt) {
+  const uint64_t e = rt->rep->error;
+  if (e == 0) return GPUOS_OK;
+  static const char* names[] = {"none",
+                                "dequeue warp: stage release wait expired",
+                                "compute warps: stage fill wait expired",
+                                "dependency barrier wait expired",
+                                "exit coordination wait expired",
+                                "start coordination wait expired",
+                                "malformed work item",
+                                "task dispatched to an empty op-table slot",
+                                "host heartbeat lost"};
+  const uint32_t code = (uint32_t)(e >> 32);
+  rt->failed = true;
+  char buf[256];
+  snprintf(buf, sizeof(buf), "worker error: %s (block %u, item %llu)", code < 9 ? names[code] : "unknown",
+           (unsigned)(e & 0xffffffffu), (unsigned long long)rt->rep->error_item);
+  rt->fail_msg = buf;
+  return fail(GPUOS_ERR_DEVICE, "%s", buf);
+}
+
+// ---- worker launch --------------------------------------------------------------------------
+static int launch_worker_locked(gpuos_rt* rt) {
+  const uint64_t ep = ++rt->epoch;
+  if (rt->idle_quiesce_ms == 0) rt->hc->quit_epoch = ep;  // drain mode: exit once drained
+  WorkerParams P;
+  std::memset(&P, 0, sizeof(P));
+  P.hc = rt->hc;
+  P.rep = rt->rep;
+  P.tickets = rt->tickets;
+  P.items = rt->items;
+  P.tasks = rt->tasks;
+  P.layouts = rt->layouts;
+  P.dc = rt->dc;
+  P.op_table = reinterpret_cast<OpFn*>(rt->op_table);
+  P.op_alias = reinterpret_cast<int*>(rt->op_alias);
+  P.item_mask = rt->item_cap - 1;
+  P.task_mask = (uint32_t)(rt->task_cap - 1);
+  P.layout_mask = (uint32_t)(rt->layout_cap - 1);
+  P.epoch = ep;
+  P.stages = rt->stages;
+  P.stage_bytes = rt->stage_bytes;
+  P.compute_threads = (uint32_t)rt->tpb;
+  CK(cudaSetDevice(rt->device));
+  CK(gpuos_internal_launch_batch_worker(&P, rt->sm_count, rt->tpb + 32, rt->smem, rt->kstream));
+  rt->launched = true;
+  return GPUOS_OK;
+}
+
+// Make sure a worker will process the published tail (after the tail store + fence).
+static int ensure_worker_locked(gpuos_rt* rt) {
+  if (!rt->launched) return launch_worker_locked(rt);
+  const uint64_t st = rt->rep->state;
+  const uint64_t ep = st >> 8, code = st & 0xff;
+  if (ep == rt->epoch && (code == WS_EXITING || code == WS_EXITED)) return launch_worker_locked(rt);
+  if (ep < rt->epoch) return GPUOS_OK;  // current launch queued behind the previous one
+  return GPUOS_OK;
+}
+
+// Publish pending items as one flush.  *seq_out = its ticket (0 if nothing was pending).
+static int publish_locked(gpuos_rt* rt, uint64_t* seq_out) {
+  if (seq_out) *seq_out = 0;
+  if (rt->failed) return fail(GPUOS_ERR_DEVICE, "%s", rt->fail_msg.c_str());
+  const uint64_t n = rt->item_w - rt->item_pub;
+  if (n == 0 && rt->pend_reqs == 0) return GPUOS_OK;
+  const uint64_t seq = ++rt->last_seq;
+  // the ticket slot of seq - kNumBatchSlots must be free
+  if (!rt->inflight.empty() && rt->inflight.front().seq + kNumBatchSlots <= seq) {
+    const uint64_t t0 = mono_ns();
+    while (!rt->inflight.empty() && rt->inflight.front().seq + kNumBatchSlots <= seq) {
+      reap_locked(rt);
+      int e = check_device_error_locked(rt);
+      if (e) return e;
+      if (mono_ns() - t0 > 30ull * 1000 * 1000 * 1000) return fail(GPUOS_ERR_TIMEOUT, "ticket ring full");
+      cpu_relax();
+    }
+  }
+  const uint16_t slot = (uint16_t)(seq % kNumBatchSlots);
+  for (uint64_t i = rt->item_pub; i < rt->item_w; ++i) {
+    WorkItem& it = rt->items[i & (rt->item_cap - 1)];
+    it.batch = slot;
+    it.batch_items = (uint32_t)n;
+    it.batch_seq = (uint32_t)seq;
+  }
+  BatchInfo b;
+  b.seq = seq;
+  b.first_item = rt->item_pub;
+  b.n_items = n;
+  b.n_reqs = rt->pend_reqs;
+  b.task_end = rt->task_w;
+  b.layout_end = rt->layout_w;
+  b.done = (n == 0);
+  rt->inflight.push_back(b);
+  rt->submitted += rt->pend_reqs;
+  rt->pend_reqs = 0;
+  rt->last_activity_ns = mono_ns();
+  if (seq_out) *seq_out = seq;
+  if (n == 0) {
+    reap_locked(rt);
+    return GPUOS_OK;
+  }
+  if (rt->idle_quiesce_ms != 0 && rt->hc->quit_epoch >= rt->epoch && rt->epoch > 0) {
+    rt->hc->quit_epoch = rt->epoch - 1;  // withdraw an idle-quiesce request
+  }
+  std::atomic_thread_fence(std::memory_order_seq_cst);
+  rt->hc->tail = rt->item_w;
+  rt->item_pub = rt->item_w;
+  std::atomic_thread_fence(std::memory_order_seq_cst);
+  if (rt->sync) rt->sync->submitted = rt->submitted;
+  return ensure_worker_locked(rt);
+}
+
+// Make room for `items` more items (and tasks/layouts) in the rings.
+static int reserve_locked(gpuos_rt* rt, uint64_t items, uint64_t tasks, uint64_t layouts) {
+  if (items > rt->item_cap / 2 || tasks > rt->task_cap / 2 || layouts > rt->layout_cap / 2)
+    return fail(GPUOS_ERR_INVALID, "request too large for the ring (%llu items)", (unsigned long long)items);
+  const uint64_t t0 = mono_ns();
+  bool published = false;
+  while (true) {
+    reap_locked(rt);
+    const bool ok = rt->item_w + items - rt->oldest_item <= rt->item_cap &&
+                    rt->task_w + tasks - rt->oldest_task <= rt->task_cap &&
+                    rt->layout_w + layouts - rt->oldest_layout <= rt->layout_cap;
+    if (ok) return GPUOS_OK;
+    if (!published) {
+      // pending requests occupy the ring: publish them so the worker can drain
+      int e = publish_locked(rt, nullptr);
+      if (e) return e;
+      published = true;
+    }
+    int e = check_device_error_locked(rt);
+    if (e) return e;
+    if (mono_ns() - t0 > 30ull * 1000 * 1000 * 1000) return fail(GPUOS_ERR_TIMEOUT, "ring full: worker not draining");
+    std::this_thread::yield();
+  }
+}
+
+// Append a planned request.
+static int append_plan_locked(gpuos_rt* rt, const Plan& p, const Task* task) {
+  if (rt->failed) return fail(GPUOS_ERR_DEVICE, "%s", rt->fail_msg.c_str());
+  const uint64_t nitems = p.items.size();
+  int e = reserve_locked(rt, nitems, task ? 1 : 0, p.has_layout ? 1 : 0);
+  if (e) return e;
+  // hazards against the current segment
+  bool hazard = false;
+  for (int i = 0; i < p.nreads && !hazard; ++i) hazard = rt->hz.conflicts(p.reads[i], false);
+  if (!hazard) hazard = rt->hz.conflicts(p.write, true);
+  if (hazard || rt->hz.size() > (1u << 20)) {
+    rt->hz.clear();
+    rt->seg_wait = rt->item_w;
+  }
+  for (int i = 0; i < p.nreads; ++i) rt->hz.insert(p.reads[i], false);
+  rt->hz.insert(p.write, true);
+
+  uint32_t layout_idx = 0, task_idx = 0;
+  if (p.has_layout) {
+    layout_idx = (uint32_t)(rt->layout_w & (rt->layout_cap - 1));
+    rt->layouts[layout_idx] = p.layout;
+    ++rt->layout_w;
+  }
+  if (task) {
+    task_idx = (uint32_t)(rt->task_w & (rt->task_cap - 1));
+    std::memcpy(&rt->tasks[task_idx], task, sizeof(Task));
+    ++rt->task_w;
+  }
+  const uint64_t mask = rt->item_cap - 1;
+  for (uint64_t i = 0; i < nitems; ++i) {
+    WorkItem it = p.items[i];
+    it.wait_items = rt->seg_wait;
+    if (p.has_layout) it.aux = layout_idx;
+    if (task) it.aux = task_idx;
+    rt->items[(rt->item_w + i) & mask] = it;
+  }
+  rt->item_w += nitems;
+  rt->pend_reqs += 1;
+  return GPUOS_OK;
+}
+
+// ---- keeper thread: host heartbeat, completion reaping, idle quiesce ------------------------
+static void keeper_main(gpuos_rt* rt) {
+  while (!rt->stop.load(std::memory_order_relaxed)) {
+    std::this_thread::sleep_for(std::chrono::milliseconds(2));
+    std::lock_guard<std::mutex> lk(rt->mu);
+    rt->hc->host_beat = rt->hc->host_beat + 1;
+    reap_locked(rt);
+    if (rt->launched && rt->idle_quiesce_ms > 0 && rt->inflight.empty() && rt->pend_reqs == 0 &&
+        rt->item_w == rt->item_pub && rt->hc->quit_epoch < rt->epoch &&
+        mono_ns() - rt->last_activity_ns > (uint64_t)rt->idle_quiesce_ms * 1000000ull) {
+      rt->hc->quit_epoch = rt->epoch;
+    }
+  }
+}
+
+// =========================================================================================
+// C ABI
+// =========================================================================================
+extern "C" int gpuos_rt_init(int device, int capacity, int threads_per_block, gpuos_rt** out) {
+  if (out) *out = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_rt_mu);
+    auto it = g_rts.find(device);
+    if (it != g_rts.end()) {  // gpuos_ext.cpp:450: init is idempotent
+      if (out) *out = it->second;
+      return GPUOS_OK;
+    }
+  }
+  if (capacity <= 0) capacity = 4096;
+  if (threads_per_block <= 0) threads_per_block = 256;
+  if (threads_per_block % 32 != 0 || threads_per_block < 64 || threads_per_block > 992)
+    return fail(GPUOS_ERR_INVALID, "threads_per_block must be a multiple of 32 in [64, 992]");
+  int ndev = 0;
+  CK(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) return fail(GPUOS_ERR_INVALID, "device %d out of range (%d devices)", device, ndev);
+  CK(cudaSetDevice(device));
+  CK(cudaFree(0));
+  gpuos_rt* rt = new gpuos_rt();
+  rt->device = device;
+  rt->capacity = capacity;
+  rt->tpb = threads_per_block;
+  rt->verbose = env_int("GPUOS_VERBOSE", 0);
+  rt->idle_quiesce_ms = env_int("GPUOS_IDLE_QUIESCE_MS", 200);
+  rt->stages = (uint32_t)std::max(2, std::min(kMaxStages, env_int("GPUOS_STAGES", 4)));
+  auto cleanup = [&](int code) {
+    if (rt->host_block) cudaFreeHost(rt->host_block);
+    if (rt->dc) cudaFree(rt->dc);
+    if (rt->kstream) cudaStreamDestroy(rt->kstream);
+    if (rt->cstream) cudaStreamDestroy(rt->cstream);
+    delete rt;
+    return code;
+  };
+  cudaError_t e = cudaDeviceGetAttribute(&rt->sm_count, cudaDevAttrMultiProcessorCount, device);
+  if (e != cudaSuccess) return cleanup(fail(GPUOS_ERR_CUDA, "cudaDeviceGetAttribute: %s", cudaGetErrorString(e)));
+  int smem_optin = 0;
+  cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+  rt->smem = gpuos_internal_smem_header_bytes() + (size_t)rt->stages * rt->stage_bytes;
+  while (rt->smem > (size_t)smem_optin && rt->stages > 2) {
+    --rt->stages;
+    rt->smem = gpuos_internal_smem_header_bytes() + (size_t)rt->stages * rt->stage_bytes;
+  }
+  rt->item_cap = pow2_at_least(std::max<uint64_t>((uint64_t)capacity * 8, 1u << 16));
+  rt->task_cap = pow2_at_least(std::max<uint64_t>((uint64_t)capacity, 1024));
+  rt->layout_cap = pow2_at_least(std::max<uint64_t>((uint64_t)capacity, 1024));
+  const size_t off_hc = 0, off_rep = 128, off_sync = 256, off_tk = 512;
+  const size_t off_items = off_tk + sizeof(Ticket) * kNumBatchSlots;
+  const size_t off_tasks = off_items + sizeof(WorkItem) * rt->item_cap;
+  const size_t off_lay = off_tasks + ((sizeof(Task) * rt->task_cap + 127) & ~size_t(127));
+  const size_t total = off_lay + sizeof(Layout) * rt->layout_cap;
+  e = cudaHostAlloc(&rt->host_block, total, cudaHostAllocMapped | cudaHostAllocPortable);
+  if (e != cudaSuccess) return cleanup(fail(GPUOS_ERR_CUDA, "cudaHostAlloc(%zu): %s", total, cudaGetErrorString(e)));
+  std::memset(rt->host_block, 0, total);
+  void* dev_block = nullptr;
+  e = cudaHostGetDevicePointer(&dev_block, rt->host_block, 0);
+  if (e != cudaSuccess || dev_block != rt->host_block)
+    return cleanup(fail(GPUOS_ERR_CUDA, "mapped memory needs unified addressing (%s)", cudaGetErrorString(e)));
+  unsigned char* hb = static_cast<unsigned char*>(rt->host_block);
+  rt->hc = reinterpret_cast<HostCtl*>(hb + off_hc);
+  rt->rep = reinterpret_cast<DevReport*>(hb + off_rep);
+  rt->sync = reinterpret_cast<SyncState*>(hb + off_sync);
+  rt->tickets = reinterpret_cast<Ticket*>(hb + off_tk);
+  rt->items = reinterpret_cast<WorkItem*>(hb + off_items);
+  rt->tasks = reinterpret_cast<Task*>(hb + off_tasks);
+  rt->layouts = reinterpret_cast<Layout*>(hb + off_lay);
+  rt->hc->safety_idle_ns = (uint64_t)env_int("GPUOS_SAFETY_IDLE_MS", 10000) * 1000000ull;
+  rt->hc->spin_ns = (uint32_t)env_int("GPUOS_SPIN_NS", 32);
+  rt->hc->wait_limit_ns = (uint64_t)env_int("GPUOS_DEVICE_WAIT_MS", 5000) * 1000000ull;
+  rt->hc->debug_level = (uint32_t)env_int("GPUOS_DEBUG", 0);
+
+  e = cudaMalloc(&rt->dc, sizeof(DevCtl));
+  if (e == cudaSuccess) e = cudaMemset(rt->dc, 0, sizeof(DevCtl));
+  if (e == cudaSuccess) e = cudaMemset(rt->dc->batch_t0, 0xff, sizeof(rt->dc->batch_t0));
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&rt->kstream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&rt->cstream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = launch_init_builtin_ops(rt->cstream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(rt->cstream);
+  if (e == cudaSuccess) e = gpuos_internal_table_ptrs(&rt->op_table, &rt->op_alias);
+  if (e == cudaSuccess) e = gpuos_internal_set_worker_smem(rt->smem);
+  if (e != cudaSuccess) return cleanup(fail(GPUOS_ERR_CUDA, "runtime setup: %s", cudaGetErrorString(e)));
+  rt->last_activity_ns = mono_ns();
+  {
+    std::lock_guard<std::mutex> lk(rt->mu);
+    int st = launch_worker_locked(rt);
+    if (st) return cleanup(st);
+  }
+  // wait for the worker to come up (gpuos_ext.cpp:495-511: 1 s cap, then proceed)
+  const uint64_t t0 = mono_ns();
+  while (rt->rep->ready_epoch < rt->epoch && mono_ns() - t0 < 2000ull * 1000 * 1000) std::this_thread::yield();
+  rt->keeper = std::thread(keeper_main, rt);
+  {
+    std::lock_guard<std::mutex> lk(g_rt_mu);
+    g_rts[device] = rt;
+  }
+  if (out) *out = rt;
+  return GPUOS_OK;
+}
+
+static int wait_seq_locked(gpuos_rt* rt, std::unique_lock<std::mutex>& lk, uint64_t seq, int timeout_ms);
+
+extern "C" int gpuos_rt_shutdown(gpuos_rt* rt) {
+  if (!rt) return GPUOS_OK;
+  {
+    std::lock_guard<std::mutex> lk(g_rt_mu);
+    auto it = g_rts.find(rt->device);
+    if (it == g_rts.end() || it->second != rt) return fail(GPUOS_ERR_NOT_INIT, "runtime not registered");
+    g_rts.erase(it);
+  }
+  rt->stop.store(true);
+  if (rt->keeper.joinable()) rt->keeper.join();
+  int status = GPUOS_OK;
+  cudaSetDevice(rt->device);
+  {
+    std::unique_lock<std::mutex> lk(rt->mu);
+    if (!rt->failed) {
+      uint64_t seq = 0;
+      status = publish_locked(rt, &seq);
+      if (!status && rt->last_seq) status = wait_seq_locked(rt, lk, rt->last_seq, 30000);
+    }
+    rt->hc->quit_epoch = rt->epoch;
+  }
+  // The worker exits once drained; a bounded wait before the stream sync.
+  const uint64_t t0 = mono_ns();
+  while (rt->launched && mono_ns() - t0 < 20ull * 1000 * 1000 * 1000) {
+    const uint64_t st = rt->rep->state;
+    if ((st >> 8) == rt->epoch && (st & 0xff) == WS_EXITED) break;
+    if (cudaStreamQuery(rt->kstream) != cudaErrorNotReady) break;
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+  cudaError_t e = cudaStreamSynchronize(rt->kstream);
+  if (e != cudaSuccess && !status) status = fail(GPUOS_ERR_CUDA, "worker: %s", cudaGetErrorString(e));
+  cudaStreamSynchronize(rt->cstream);
+  cudaStreamDestroy(rt->kstream);
+  cudaStreamDestroy(rt->cstream);
+  cudaFree(rt->dc);
+  cudaFreeHost(rt->host_block);
+  delete rt;
+  return status;
+}
+
+extern "C" int gpuos_rt_submit_ew(gpuos_rt* rt, int op, const GpuosOperand* a, const GpuosOperand* b, int b_is_scalar,
+                                  double b_scalar, const GpuosOperand* out, const float* params, int nparams) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  if (!a || !out) return fail(GPUOS_ERR_INVALID, "null operand");
+  EwReq r;
+  r.op = op;
+  r.a = a;
+  r.b = b_is_scalar ? nullptr : b;
+  r.b_imm = b_is_scalar != 0;
+  r.b_val = (float)b_scalar;
+  r.out = out;
+  for (int i = 0; i < 4; ++i) r.params[i] = (params && i < nparams) ? params[i] : 0.f;
+  static thread_local Plan plan;
+  int e = plan_ew(r, kHalfBytes, &plan);
+  if (e) return e;
+  std::lock_guard<std::mutex> lk(rt->mu);
+  return append_plan_locked(rt, plan, nullptr);
+}
+
+extern "C" int gpuos_rt_submit_reduce(gpuos_rt* rt, int red_op, const GpuosOperand* x, const GpuosOperand* out,
+                                      const int* axes, int naxes, int keepdim) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  if (!x || !out) return fail(GPUOS_ERR_INVALID, "null operand");
+  static thread_local Plan plan;
+  int e = plan_reduce(red_op, *x, *out, axes, naxes, keepdim, rt->stage_bytes, &plan);
+  if (e) return e;
+  std::lock_guard<std::mutex> lk(rt->mu);
+  return append_plan_locked(rt, plan, nullptr);
+}
+
+static Range tensorref_range(const TensorRef& t) {
+  if (!t.data) return Range();
+  return operand_range(t.data, t.dtype, t.ndim, t.sizes, t.strides);
+}
+
+extern "C" int gpuos_rt_submit_task(gpuos_rt* rt, const Task* task) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  if (!task) return fail(GPUOS_ERR_INVALID, "null task");
+  if (task->op < 0 || task->op >= GPUOS_MAX_OPS) return fail(GPUOS_ERR_INVALID, "task op %d out of range", task->op);
+  if (task->in0.ndim > GPUOS_MAX_NDIM || task->in1.ndim > GPUOS_MAX_NDIM || task->out0.ndim > GPUOS_MAX_NDIM)
+    return fail(GPUOS_ERR_INVALID, "task rank above %d", GPUOS_MAX_NDIM);
+  Plan p;
+  WorkItem it;
+  std::memset(&it, 0, sizeof(it));
+  it.kind = IK_TASK;
+  it.op = (uint8_t)task->op;
+  p.items.push_back(it);
+  p.reads[p.nreads++] = tensorref_range(task->in0);
+  p.reads[p.nreads++] = tensorref_range(task->in1);
+  p.write = tensorref_range(task->out0);
+  std::lock_guard<std::mutex> lk(rt->mu);
+  return append_plan_locked(rt, p, task);
+}
+
+static int wait_seq_locked(gpuos_rt* rt, std::unique_lock<std::mutex>& lk, uint64_t seq, int timeout_ms) {
+  const uint64_t t0 = mono_ns();
+  const uint64_t limit = (uint64_t)(timeout_ms < 0 ? 30000 : timeout_ms) * 1000000ull;
+  uint32_t spins = 0;
+  while (true) {
+    reap_locked(rt);
+    if (rt->completed_seq >= seq) return GPUOS_OK;
+    bool seq_done = false;
+    for (const BatchInfo& b : rt->inflight)
+      if (b.seq == seq) {
+        seq_done = b.done;
+        break;
+      }
+    if (seq_done) return GPUOS_OK;
+    int e = check_device_error_locked(rt);
+    if (e) return e;
+    if ((++spins & 1023u) == 0) {
+      // a worker that exited (yield, idle) with work outstanding is relaunched
+      const uint64_t st = rt->rep->state;
+      if ((st >> 8) == rt->epoch && (st & 0xff) == WS_EXITED && rt->item_pub > rt->rep->exit_tail) {
+        e = launch_worker_locked(rt);
+        if (e) return e;
+      }
+    }
+    const uint64_t el = mono_ns() - t0;
+    if (el > limit) return fail(GPUOS_ERR_TIMEOUT, "timed out waiting for flush %llu", (unsigned long long)seq);
+    if (spins < 4096) {
+      cpu_relax();
+    } else {
+      lk.unlock();
+      std::this_thread::sleep_for(std::chrono::microseconds(spins < 16384 ? 5 : 100));
+      lk.lock();
+    }
+  }
+}
+
+extern "C" int gpuos_rt_flush(gpuos_rt* rt, int flags, cudaStream_t dep_stream, uint64_t* seq_out) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  if (seq_out) *seq_out = 0;
+  const bool sync = (flags & GPUOS_FLUSH_SYNC) != 0;
+  // Work already enqueued on dep_stream (e.g. the kernels that produced the inputs) must
+  // finish before the worker reads the inputs.
+  if (flags & GPUOS_FLUSH_DEP) {
+    CK(cudaSetDevice(rt->device));
+    cudaError_t q = cudaStreamQuery(dep_stream);
+    if (q == cudaErrorNotReady) {
+      const uint64_t t0 = mono_ns();
+      while ((q = cudaStreamQuery(dep_stream)) == cudaErrorNotReady) {
+        if (mono_ns() - t0 > 30ull * 1000 * 1000 * 1000) return fail(GPUOS_ERR_TIMEOUT, "dependency stream did not drain");
+        std::this_thread::yield();
+      }
+    }
+    if (q != cudaSuccess) return fail(GPUOS_ERR_CUDA, "dependency stream: %s", cudaGetErrorString(q));
+  }
+  std::unique_lock<std::mutex> lk(rt->mu);
+  uint64_t seq = 0;
+  int e = publish_locked(rt, &seq);
+  if (e) return e;
+  if (seq_out) *seq_out = seq ? seq : rt->last_seq;
+  if (sync) {
+    const uint64_t target = rt->last_seq;  // this flush and everything before it
+    if (target) return wait_seq_locked(rt, lk, target, 30000);
+  }
+  return GPUOS_OK;
+}
+
+extern "C" int gpuos_rt_wait(gpuos_rt* rt, uint64_t seq, int timeout_ms) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  std::unique_lock<std::mutex> lk(rt->mu);
+  if (seq > rt->last_seq) return fail(GPUOS_ERR_INVALID, "flush %llu was never issued", (unsigned long long)seq);
+  return wait_seq_locked(rt, lk, seq, timeout_ms);
+}
+
+extern "C" uint64_t gpuos_rt_completed(gpuos_rt* rt) {
+  if (!rt) return 0;
+  std::lock_guard<std::mutex> lk(rt->mu);
+  reap_locked(rt);
+  return rt->completed_seq;
+}
+
+extern "C" int gpuos_rt_flush_times(gpuos_rt* rt, uint64_t seq, uint64_t* t_start, uint64_t* t_end) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  std::lock_guard<std::mutex> lk(rt->mu);
+  reap_locked(rt);
+  const Ticket& tk = rt->tickets[seq % kNumBatchSlots];
+  if (seq == 0 || seq > rt->last_seq || seq + kNumBatchSlots <= rt->last_seq || tk.seq != (uint32_t)seq)
+    return fail(GPUOS_ERR_INVALID, "flush %llu not complete or recycled", (unsigned long long)seq);
+  if (t_start) *t_start = tk.t_start;
+  if (t_end) *t_end = tk.t_end;
+  return GPUOS_OK;
+}
+
+extern "C" cudaStream_t gpuos_rt_kernel_stream(gpuos_rt* rt) { return rt ? rt->kstream : nullptr; }
+
+extern "C" uint64_t gpuos_rt_launches(gpuos_rt* rt) {
+  if (!rt) return 0;
+  std::lock_guard<std::mutex> lk(rt->mu);
+  return rt->epoch;
+}
+
+extern "C" uint64_t gpuos_rt_poll_processed(gpuos_rt* rt) {
+  if (!rt) return 0;
+  std::lock_guard<std::mutex> lk(rt->mu);
+  reap_locked(rt);
+  return rt->processed;
+}
+
+extern "C" uint64_t gpuos_rt_poll_heartbeat(gpuos_rt* rt) { return rt ? rt->rep->heartbeat : 0; }
+
+extern "C" int gpuos_rt_poll_ready(gpuos_rt* rt) {
+  if (!rt) return 0;
+  const uint64_t st = rt->rep->state;
+  return (rt->rep->ready_epoch >= 1 && (st & 0xff) == WS_RUNNING) ? 1 : 0;
+}
+
+extern "C" int gpuos_rt_sync_wait(gpuos_rt* rt, uint64_t target, int timeout_ms) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  std::unique_lock<std::mutex> lk(rt->mu);
+  const uint64_t t0 = mono_ns();
+  const uint64_t limit = (uint64_t)(timeout_ms < 0 ? 30000 : timeout_ms) * 1000000ull;
+  while (true) {
+    reap_locked(rt);
+    if (rt->processed >= target) return GPUOS_OK;
+    int e = check_device_error_locked(rt);
+    if (e) return e;
+    if (mono_ns() - t0 > limit)
+      return fail(GPUOS_ERR_TIMEOUT, "sync_wait: processed=%llu target=%llu", (unsigned long long)rt->processed,
+                  (unsigned long long)target);
+    lk.unlock();
+    std::this_thread::sleep_for(std::chrono::microseconds(5));
+    lk.lock();
+  }
+}
+
+extern "C" int gpuos_rt_worker_alive(gpuos_rt* rt) {
+  if (!rt || !rt->launched) return 0;
+  return cudaStreamQuery(rt->kstream) == cudaErrorNotReady ? 1 : 0;
+}
+
+extern "C" int gpuos_rt_ensure_worker(gpuos_rt* rt) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  std::lock_guard<std::mutex> lk(rt->mu);
+  if (rt->failed) return fail(GPUOS_ERR_DEVICE, "%s", rt->fail_msg.c_str());
+  if (cudaStreamQuery(rt->kstream) == cudaSuccess) {
+    if (rt->idle_quiesce_ms != 0 && rt->hc->quit_epoch >= rt->epoch) rt->hc->quit_epoch = rt->epoch;
+    return launch_worker_locked(rt);
+  }
+  return GPUOS_OK;
+}
+
+extern "C" int gpuos_rt_quiesce(gpuos_rt* rt, int timeout_ms) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  uint64_t ep;
+  {
+    std::lock_guard<std::mutex> lk(rt->mu);
+    if (!rt->launched) return GPUOS_OK;
+    rt->hc->quit_epoch = rt->epoch;
+    ep = rt->epoch;
+  }
+  const uint64_t t0 = mono_ns();
+  const uint64_t limit = (uint64_t)(timeout_ms < 0 ? 30000 : timeout_ms) * 1000000ull;
+  while (true) {
+    const uint64_t st = rt->rep->state;
+    if ((st >> 8) == ep && (st & 0xff) == WS_EXITED) break;
+    if (rt->rep->error) {
+      std::lock_guard<std::mutex> lk(rt->mu);
+      return check_device_error_locked(rt);
+    }
+    if (mono_ns() - t0 > limit) return fail(GPUOS_ERR_TIMEOUT, "worker did not exit");
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+  CK(cudaStreamSynchronize(rt->kstream));
+  return GPUOS_OK;
+}
+
+extern "C" int gpuos_rt_set_debug_level(gpuos_rt* rt, int level) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  rt->hc->debug_level = (uint32_t)level;
+  CK(cudaSetDevice(rt->device));
+  CK(gpu_set_debug_level_async(level, rt->cstream));
+  CK(cudaStreamSynchronize(rt->cstream));
+  return GPUOS_OK;
+}
+
+extern "C" int gpuos_rt_set_yield_every(gpuos_rt* rt, uint64_t every) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  rt->hc->yield_every = every;
+  return GPUOS_OK;
+}
+
+extern "C" int gpuos_rt_set_device_wait_ms(gpuos_rt* rt, int ms) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  if (ms <= 0) return fail(GPUOS_ERR_INVALID, "device wait bound must be positive");
+  rt->hc->wait_limit_ns = (uint64_t)ms * 1000000ull;
+  return GPUOS_OK;
+}
+
+// Publish one item whose dependency barrier never opens: the dequeue warp's bounded wait
+// expires, the worker records DE_WAIT_BARRIER and exits.  The item is never executed.
+extern "C" int gpuos_rt_debug_inject_stall(gpuos_rt* rt) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  std::lock_guard<std::mutex> lk(rt->mu);
+  int e = reserve_locked(rt, 1, 0, 0);
+  if (e) return e;
+  WorkItem it;
+  std::memset(&it, 0, sizeof(it));
+  it.kind = IK_EW_CONTIG;
+  it.op = GPUOS_EW_COPY;
+  it.count = 0;
+  it.aux = 0xffffffffu;
+  it.wait_items = ~0ull >> 1;
+  rt->items[rt->item_w & (rt->item_cap - 1)] = it;
+  rt->item_w += 1;
+  rt->pend_reqs += 1;
+  return publish_locked(rt, nullptr);
+}
+
+extern "C" int gpuos_rt_set_idle_quiesce_ms(gpuos_rt* rt, int ms) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  std::lock_guard<std::mutex> lk(rt->mu);
+  rt->idle_quiesce_ms = ms < 0 ? -1 : ms;
+  if (ms == 0) rt->hc->quit_epoch = rt->epoch;
+  return GPUOS_OK;
+}
+
+extern "C" const char* gpuos_rt_stat_names(void) {
+  return "head,tail,in_flight,capacity,processed,heartbeat,quit,host_tail_shadow,host_pending,"
+         "item_capacity,sync_processed,sync_heartbeat,sync_ready,sync_submitted,epoch,state,error,items_done,"
+         "completed_seq,last_seq";
+}
+
+extern "C" int gpuos_rt_stats(gpuos_rt* rt, int64_t* v, int n) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  std::lock_guard<std::mutex> lk(rt->mu);
+  reap_locked(rt);
+  int64_t vals[20];
+  vals[0] = (int64_t)rt->rep->head_mirror;
+  vals[1] = (int64_t)rt->item_pub;
+  vals[2] = (int64_t)(rt->item_pub - std::min(rt->item_pub, (uint64_t)rt->rep->items_done));
+  vals[3] = rt->capacity;
+  vals[4] = (int64_t)rt->processed;
+  vals[5] = (int64_t)rt->rep->heartbeat;
+  vals[6] = rt->hc->quit_epoch >= rt->epoch ? 1 : 0;
+  vals[7] = (int64_t)rt->item_pub;
+  vals[8] = (int64_t)rt->pend_reqs;
+  vals[9] = (int64_t)rt->item_cap;
+  vals[10] = (int64_t)rt->processed;
+  vals[11] = (int64_t)rt->rep->heartbeat;
+  vals[12] = gpuos_rt_poll_ready(rt);
+  vals[13] = (int64_t)rt->submitted;
+  vals[14] = (int64_t)rt->epoch;
+  vals[15] = (int64_t)(rt->rep->state & 0xff);
+  vals[16] = (int64_t)rt->rep->error;
+  vals[17] = (int64_t)rt->rep->items_done;
+  vals[18] = (int64_t)rt->completed_seq;
+  vals[19] = (int64_t)rt->last_seq;
+  for (int i = 0; i < n && i < 20; ++i) v[i] = vals[i];
+  return GPUOS_OK;
+}
+
+// ---- op table control --------------------------------------------------------------------
+extern "C" int gpuos_rt_set_slot(gpuos_rt* rt, int slot, OpPtrInt fn) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  if (slot < 0 || slot >= GPUOS_MAX_OPS) return fail(GPUOS_ERR_INVALID, "slot %d out of range", slot);
+  CK(cudaSetDevice(rt->device));
+  CK(gpu_set_op_table_async(slot, fn, rt->cstream));
+  CK(cudaStreamSynchronize(rt->cstream));
+  return GPUOS_OK;
+}
+
+extern "C" int gpuos_rt_get_slot(gpuos_rt* rt, int slot, OpPtrInt* fn) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  if (slot < 0 || slot >= GPUOS_MAX_OPS || !fn) return fail(GPUOS_ERR_INVALID, "slot %d out of range", slot);
+  CK(cudaSetDevice(rt->device));
+  CK(cudaMemcpyAsync(fn, static_cast<OpPtrInt*>(rt->op_table) + slot, sizeof(OpPtrInt), cudaMemcpyDeviceToHost,
+                     rt->cstream));
+  CK(cudaStreamSynchronize(rt->cstream));
+  return GPUOS_OK;
+}
+
+extern "C" int gpuos_rt_set_alias(gpuos_rt* rt, int logical, int physical) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  if (logical < 0 || logical >= GPUOS_MAX_OPS || physical < 0 || physical >= GPUOS_MAX_OPS)
+    return fail(GPUOS_ERR_INVALID, "alias %d -> %d out of range", logical, physical);
+  CK(cudaSetDevice(rt->device));
+  CK(gpu_set_alias_async(logical, physical, rt->cstream));
+  CK(cudaStreamSynchronize(rt->cstream));
+  return GPUOS_OK;
+}
+
+extern "C" int gpuos_rt_get_alias(gpuos_rt* rt, int logical, int* physical) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  if (logical < 0 || logical >= GPUOS_MAX_OPS || !physical) return fail(GPUOS_ERR_INVALID, "logical %d out of range", logical);
+  CK(cudaSetDevice(rt->device));
+  CK(cudaMemcpyAsync(physical, static_cast<int*>(rt->op_alias) + logical, sizeof(int), cudaMemcpyDeviceToHost,
+                     rt->cstream));
+  CK(cudaStreamSynchronize(rt->cstream));
+  return GPUOS_OK;
+}
+
+static int register_builtin_code(gpuos_rt* rt, int code, int* slot) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  OpPtrInt addr = 0;
+  CK(cudaSetDevice(rt->device));
+  CK(gpu_get_builtin_op_async(code, &addr, rt->cstream));
+  CK(cudaStreamSynchronize(rt->cstream));
+  if (!addr) return fail(GPUOS_ERR_INVALID, "no built-in operator %d", code);
+  int s;
+  {
+    std::lock_guard<std::mutex> lk(rt->mu);
+    if (rt->next_slot >= GPUOS_MAX_OPS) return fail(GPUOS_ERR_FULL, "op table full (%d slots)", GPUOS_MAX_OPS);
+    s = rt->next_slot++;
+  }
+  int e = gpuos_rt_set_slot(rt, s, addr);
+  if (e) return e;
+  if (slot) *slot = s;
+  return GPUOS_OK;
+}
+
+extern "C" int gpuos_rt_register_builtin_reduce(gpuos_rt* rt, int red_op, int* slot) {
+  if (red_op != GPUOS_RED_SUM && red_op != GPUOS_RED_MEAN) return fail(GPUOS_ERR_INVALID, "unknown reduction %d", red_op);
+  return register_builtin_code(rt, 100 + GPUOS_EW_NUM_OPS + red_op, slot);
+}
+
+extern "C" int gpuos_rt_register_builtin_ew(gpuos_rt* rt, int ew_op, int* slot) {
+  if (ew_op < 0 || ew_op >= GPUOS_EW_NUM_OPS) return fail(GPUOS_ERR_INVALID, "unknown element-wise op %d", ew_op);
+  return register_builtin_code(rt, 100 + ew_op, slot);
+}
+
+extern "C" int gpuos_rt_register_expr(gpuos_rt* rt, const char* key, const char* expr, int arity, int slot,
+                                      int* slot_out) {
+  (void)key;
+  (void)expr;
+  (void)arity;
+  (void)slot;
+  (void)slot_out;
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  return fail(GPUOS_ERR_UNSUPPORTED, "NVRTC operator injection is not available in this build");
+}
+
+// ---- planning hooks -----------------------------------------------------------------------
+static int copy_plan(const Plan& p, void* items_out, int max_items, void* layout_out, int* n_items) {
+  if (n_items) *n_items = (int)p.items.size();
+  if ((int)p.items.size() > max_items) return fail(GPUOS_ERR_FULL, "plan has %zu items", p.items.size());
+  if (items_out && !p.items.empty()) std::memcpy(items_out, p.items.data(), p.items.size() * sizeof(WorkItem));
+  if (layout_out) {
+    std::memset(layout_out, 0, 512);
+    if (p.has_layout) std::memcpy(layout_out, &p.layout, sizeof(Layout));
+  }
+  return GPUOS_OK;
+}
+
+extern "C" int gpuos_plan_ew(int op, const GpuosOperand* a, const GpuosOperand* b, int b_is_scalar, double b_scalar,
+                             const GpuosOperand* out, const float* params, int nparams, void* items_out, int max_items,
+                             void* layout_out, int* n_items) {
+  if (!a || !out) return fail(GPUOS_ERR_INVALID, "null operand");
+  EwReq r;
+  r.op = op;
+  r.a = a;
+  r.b = b_is_scalar ? nullptr : b;
+  r.b_imm = b_is_scalar != 0;
+  r.b_val = (float)b_scalar;
+  r.out = out;
+  for (int i = 0; i < 4; ++i) r.params[i] = (params && i < nparams) ? params[i] : 0.f;
+  Plan p;
+  int e = plan_ew(r, kHalfBytes, &p);
+  if (e) return e;
+  return copy_plan(p, items_out, max_items, layout_out, n_items);
+}
+
+extern "C" int gpuos_plan_reduce(int red_op, const GpuosOperand* x, const GpuosOperand* out, const int* axes, int naxes,
+                                 int keepdim, void* items_out, int max_items, void* layout_out, int* n_items) {
+  if (!x || !out) return fail(GPUOS_ERR_INVALID, "null operand");
+  Plan p;
+  int e = plan_reduce(red_op, *x, *out, axes, naxes, keepdim, kStageBytesDefault, &p);
+  if (e) return e;
+  return copy_plan(p, items_out, max_items, layout_out, n_items);
+}
+
+extern "C" int gpuos_abi_sizes(int64_t* out, int n) {
+  const int64_t v[] = {(int64_t)sizeof(TensorRef), (int64_t)sizeof(Task),       (int64_t)offsetof(Task, in0),
+                       (int64_t)offsetof(Task, in1), (int64_t)offsetof(Task, out0), (int64_t)sizeof(SyncState),
+                       (int64_t)sizeof(WorkQueue), (int64_t)sizeof(WorkItem),   (int64_t)sizeof(Layout),
+                       (int64_t)sizeof(GpuosOperand)};
+  const int m = (int)(sizeof(v) / sizeof(v[0]));
+  for (int i = 0; i < n && i < m; ++i) out[i] = v[i];
+  return m;
+}

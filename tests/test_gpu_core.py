@@ -1,0 +1,157 @@
+"""Persistent runtime on the GPU: the batched add/mul path (config 1 at full size), the
+reference's known answers, ordering of dependent requests, stream dependencies and
+completion accounting.  Parity oracle: PyTorch CPU eager, bit-exact."""
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.reference_semantics import same_bits
+
+pytestmark = pytest.mark.gpu
+GOLD = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "reference_known_answers.json")))
+
+
+def test_config1_full_size_bit_exact(rt):
+    # 4096 independent fp32 requests of 4096 elements, U(-1,1), op 50/50 add/mul
+    g = torch.Generator().manual_seed(1234 + 1)
+    n_req, n = 4096, 4096
+    A = (torch.rand(n_req, n, generator=g) * 2 - 1)
+    B = (torch.rand(n_req, n, generator=g) * 2 - 1)
+    ops = torch.randint(0, 2, (n_req,), generator=g)
+    a, b = A.cuda(), B.cuda()
+    out = torch.empty_like(a)
+    for i in range(n_req):
+        (rt.submit_add if ops[i] == 0 else rt.submit_mul)(a[i], b[i], out[i])
+    rt.flush(sync=True)
+    ref = torch.where(ops[:, None] == 0, A + B, A * B)
+    assert same_bits(out.cpu(), ref)
+
+
+def test_known_answer_test_py_in_order(rt):
+    # test/test.py: add, mul, sub, div into the same c in one flush -> c = a / b
+    a = torch.arange(16, device="cuda", dtype=torch.float32)
+    b = 2 * torch.ones_like(a)
+    c = torch.empty_like(a)
+    rt.submit_add(a, b, c)
+    rt.submit_mul(a, b, c)
+    rt.submit_sub(a, b, c)
+    rt.submit_div(a, b, c)
+    rt.flush(sync=True)
+    assert c.cpu().tolist() == GOLD["test_py"]["c"]
+    assert c[:4].tolist() == [0.0, 0.5, 1.0, 1.5]
+
+
+def test_known_answer_full_sync(rt):
+    g = GOLD["full_sync"]
+    rng = np.random.default_rng(g["seed"])
+    a = torch.from_numpy(rng.standard_normal(g["n"]).astype(np.float32)).cuda()
+    b = torch.from_numpy(rng.standard_normal(g["n"]).astype(np.float32)).cuda()
+    c = torch.empty_like(a)
+    before = rt.sync_poll_processed()
+    rt.submit_add(a, b, c)
+    rt.flush(sync=False)
+    rt.sync_wait(before + 1, 5000)
+    assert rt.sync_poll_processed() >= before + 1
+    rt.submit_mul(a, b, c)
+    rt.flush(sync=True)
+    for _ in range(5):
+        rt.submit_add(a, b, c)
+    rt.flush(sync=True)
+    assert same_bits(c.cpu(), (a.cpu() + b.cpu()))
+    st = rt.peek_queue()
+    assert st["sync_enabled"] and st["processed"] >= before + 7
+
+
+def test_dependent_chain_within_one_flush(rt):
+    # each request reads the previous output: RAW hazards inside one flush
+    x = torch.randn(5000, device="cuda")
+    y = torch.randn(5000, device="cuda")
+    bufs = [torch.empty_like(x) for _ in range(8)]
+    rt.submit_add(x, y, bufs[0])
+    for k in range(1, 8):
+        rt.submit_mul(bufs[k - 1], y, bufs[k])
+    rt.flush(sync=True)
+    r = x.cpu() + y.cpu()
+    for _ in range(7):
+        r = r * y.cpu()
+    assert same_bits(bufs[7].cpu(), r)
+
+
+def test_dependent_across_async_flushes(rt):
+    x = torch.randn(70_000, device="cuda")
+    y = torch.randn(70_000, device="cuda")
+    t = torch.empty_like(x)
+    u = torch.empty_like(x)
+    rt.submit_add(x, y, t)
+    rt.flush(sync=False)
+    rt.submit_mul(t, y, u)  # reads the output of the previous (possibly running) flush
+    rt.flush(sync=True)
+    assert same_bits(u.cpu(), (x.cpu() + y.cpu()) * y.cpu())
+
+
+def test_inputs_from_pending_torch_work(rt):
+    # inputs produced by torch kernels still queued on the current stream
+    big = torch.randn(64 << 20, device="cuda")
+    a = big.mul(2.0).narrow(0, 0, 4096).clone()
+    b = torch.full((4096,), 3.0, device="cuda")
+    out = torch.empty_like(a)
+    rt.submit_add(a, b, out)
+    rt.flush(sync=True)
+    assert same_bits(out.cpu(), a.cpu() + 3.0)
+
+
+def test_many_small_flushes_and_tickets(rt):
+    a = torch.randn(256, device="cuda")
+    outs = [torch.empty_like(a) for _ in range(300)]
+    seqs = []
+    for k, o in enumerate(outs):
+        rt.submit_mul(a, a, o) if k % 2 else rt.submit_add(a, a, o)
+        seqs.append(rt.flush(sync=False))
+    assert seqs == sorted(seqs) and len(set(seqs)) == len(seqs)
+    rt.wait(seqs[-1])
+    assert rt.completed() >= seqs[-1]
+    t0, t1 = rt.flush_times(seqs[-1])
+    assert t1 >= t0 > 0
+    ac = a.cpu()
+    for k, o in enumerate(outs):
+        assert same_bits(o.cpu(), ac * ac if k % 2 else ac + ac)
+
+
+def test_quiesce_and_relaunch(rt):
+    a = torch.randn(1000, device="cuda")
+    o = torch.empty_like(a)
+    rt.quiesce()
+    assert not rt.worker_alive()
+    n0 = rt.launches()
+    rt.submit_add(a, a, o)
+    rt.flush(sync=True)
+    assert rt.launches() == n0 + 1
+    assert same_bits(o.cpu(), a.cpu() * 2)
+
+
+def test_drain_mode_each_flush_launches(rt):
+    a = torch.randn(3000, device="cuda")
+    o = torch.empty_like(a)
+    rt.set_idle_quiesce_ms(0)
+    try:
+        n0 = rt.launches()
+        for _ in range(3):
+            rt.submit_mul(a, a, o)
+            rt.flush(sync=True)
+        assert rt.launches() >= n0 + 1
+        assert same_bits(o.cpu(), a.cpu() * a.cpu())
+    finally:
+        rt.set_idle_quiesce_ms(200)
+
+
+def test_errors_are_exceptions(rt):
+    a = torch.randn(4, device="cuda")
+    with pytest.raises(ValueError):
+        rt.submit_add(a, torch.randn(5, device="cuda"), torch.empty(5, device="cuda"))
+    with pytest.raises(ValueError):
+        rt.submit_add(a.double(), a.double(), a.double())
+    with pytest.raises(RuntimeError, match="CUDA"):
+        rt.submit_add(a.cpu(), a.cpu(), a.cpu())

@@ -1,0 +1,137 @@
+"""Every built-in element-wise operator of the batched path on the GPU against PyTorch CPU
+eager: bit-exact for the non-transcendental ops, at most 2 fp32 ulp for transcendentals
+(fp32 output), at most 1 ulp of the 16-bit output type otherwise."""
+import json
+import os
+
+import pytest
+import torch
+
+from oracle.reference_semantics import BINARY, EW, TRANSCENDENTAL, ew_torch, same_bits, ulp_diff
+
+pytestmark = pytest.mark.gpu
+
+PARAMS = {"LEAKY_RELU": (0.01, 0.0), "CLAMP": (-0.5, 0.5), "CLAMP_MIN": (-0.5, 0.0),
+          "CLAMP_MAX": (0.5, 0.0), "ELU": (1.0, 0.0), "SOFTPLUS": (1.0, 20.0), "ADD_ALPHA": (0.5, 0.0),
+          "SUB_ALPHA": (2.0, 0.0)}
+MAX_ULP_F32 = 2
+STATS = {}
+
+
+def inputs(name, n, g):
+    """Input domains of the mixed-op stream (x ~ U(-4,4); log/sqrt on |x|+1e-3; divisor
+    U(0.5,2); pow base U(0.1,2), exponent U(0.5,2)), plus special values for exact ops."""
+    x = torch.rand(n, generator=g) * 8 - 4
+    y = torch.rand(n, generator=g) * 8 - 4
+    if name in ("LOG", "SQRT"):
+        x = x.abs() + 1e-3
+    if name == "DIV":
+        y = torch.rand(n, generator=g) * 1.5 + 0.5
+    if name == "POW":
+        x = torch.rand(n, generator=g) * 1.9 + 0.1
+        y = torch.rand(n, generator=g) * 1.5 + 0.5
+    if name not in TRANSCENDENTAL_NAMES and n >= 16:
+        sp = torch.tensor([0.0, -0.0, float("inf"), -float("inf"), float("nan"), 3.0, -3.0, 1e-40])
+        x[: len(sp)] = sp
+        y[: len(sp)] = sp.flip(0)
+    return x, y
+
+
+TRANSCENDENTAL_NAMES = {k for k, v in EW.items() if v in TRANSCENDENTAL}
+
+
+def compare(name, got, ref, out_dtype):
+    op = EW[name]
+    if op not in TRANSCENDENTAL and name not in ("ADD_ALPHA", "SUB_ALPHA"):
+        ok = same_bits(got, ref)
+        STATS[f"{name}/{out_dtype}"] = 0 if ok else -1
+        return ok, "not bit-exact"
+    if out_dtype == torch.float32:
+        d = ulp_diff(got, ref)
+        m = int(d.max()) if d.numel() else 0
+        STATS[f"{name}/{out_dtype}"] = m
+        return m <= MAX_ULP_F32, f"max ulp {m}"
+    # 16-bit output: compare in units of the output type's ulp
+    w = torch.int16
+    g = got.cpu().contiguous().view(w).int()
+    r = ref.cpu().contiguous().view(w).int()
+    g = torch.where(g < 0, -(g & 0x7FFF), g)
+    r = torch.where(r < 0, -(r & 0x7FFF), r)
+    nan = torch.isnan(got.cpu().float()) & torch.isnan(ref.cpu().float())
+    d = torch.where(nan, torch.zeros_like(g), (g - r).abs())
+    m = int(d.max()) if d.numel() else 0
+    STATS[f"{name}/{out_dtype}"] = m
+    return m <= 1, f"max 16-bit ulp {m}"
+
+
+@pytest.mark.parametrize("name", sorted(EW))
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+def test_op_contiguous(rt, name, dtype):
+    g = torch.Generator().manual_seed(hash((name, str(dtype))) % (1 << 31))
+    op = EW[name]
+    p0, p1 = PARAMS.get(name, (0.0, 0.0))
+    for n in (1, 7, 4096, 100_003):
+        x, y = inputs(name, n, g)
+        x, y = x.to(dtype), y.to(dtype)
+        xd, yd = x.cuda(), y.cuda()
+        out = torch.empty(n, device="cuda", dtype=dtype)
+        rt.submit_elementwise(op, xd, yd if op in BINARY else None, out, p0, p1)
+        rt.flush(sync=True)
+        ref = ew_torch(op, x.float(), y.float() if op in BINARY else None, p0, p1).to(dtype)
+        ok, msg = compare(name, out.cpu(), ref, dtype)
+        assert ok, f"{name} {dtype} n={n}: {msg}"
+
+
+@pytest.mark.parametrize("name", ["ADD", "MUL", "MAXIMUM", "GELU", "SUB", "DIV"])
+def test_op_strided_broadcast_mixed(rt, name):
+    # config 3: a = transpose of [C,R] fp16 (view [R,C]), b = [C] bf16 broadcast, out fp32
+    g = torch.Generator().manual_seed(7)
+    op = EW[name]
+    for R, C in ((64, 512), (1, 32), (256, 2048), (37, 129)):
+        a = torch.randn(C, R, generator=g).half().t()
+        b = torch.randn(C, generator=g).bfloat16()
+        if name == "DIV":
+            b = (torch.rand(C, generator=g) * 1.5 + 0.5).bfloat16()
+        ad, bd = a.cuda(), b.cuda()
+        out = torch.empty(R, C, device="cuda", dtype=torch.float32)
+        rt.submit_elementwise(op, ad, bd if op in BINARY else None, out)
+        rt.flush(sync=True)
+        ref = ew_torch(op, a.float(), b.float() if op in BINARY else None)
+        ok, msg = compare(name, out.cpu(), ref, torch.float32)
+        assert ok, f"{name} R={R} C={C}: {msg}"
+
+
+def test_scalar_and_broadcast_operands(rt):
+    x = torch.randn(33, 65)
+    xd = x.cuda()
+    out = torch.empty_like(xd)
+    rt.submit_elementwise(EW["MUL"], xd, 0.5, out)
+    rt.flush(sync=True)
+    assert same_bits(out.cpu(), x * 0.5)
+    row = torch.randn(65)
+    rt.submit_elementwise(EW["ADD"], xd, row.cuda(), out)
+    rt.flush(sync=True)
+    assert same_bits(out.cpu(), x + row)
+    col = torch.randn(33, 1)
+    rt.submit_elementwise(EW["SUB"], xd, col.cuda(), out)
+    rt.flush(sync=True)
+    assert same_bits(out.cpu(), x - col)
+    one = torch.randn(1)
+    rt.submit_elementwise(EW["DIV"], one.cuda(), xd, out)
+    rt.flush(sync=True)
+    assert same_bits(out.cpu(), one / x)
+    # unaligned views (offset by one element) through the staged path
+    base = torch.randn(10001)
+    bd = base.cuda()
+    o2 = torch.empty(10000, device="cuda")
+    rt.submit_elementwise(EW["ADD"], bd[1:], bd[:-1], o2)
+    rt.flush(sync=True)
+    assert same_bits(o2.cpu(), base[1:] + base[:-1])
+
+
+def test_zz_dump_stats():
+    out_dir = os.environ.get("GPUOS_STATS_DIR")
+    if out_dir and STATS:
+        os.makedirs(out_dir, exist_ok=True)
+        with open(os.path.join(out_dir, "ulp_stats.json"), "w") as f:
+            json.dump(STATS, f, indent=1, sort_keys=True)
