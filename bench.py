@@ -35,7 +35,10 @@ import sys
 import threading
 import time
 
-import torch
+# the persistent worker holds one hardware work queue; give other streams their own
+os.environ.setdefault("CUDA_DEVICE_MAX_CONNECTIONS", "32")
+
+import torch  # noqa: E402
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)

@@ -7,11 +7,15 @@
 //     the 64-byte item from the ring in mapped pinned memory, waits on the item's
 //     dependency barrier, and stages contiguous operands into shared memory with TMA
 //     bulk copies (mbarrier complete_tx), up to `stages` items ahead;
-//   * warps 1.. are compute warps: they run the tile function for the item through the
+//   * warps 2.. are compute warps: they run the tile function for the item through the
 //     device function-pointer table (one indirect call per tile), or, for a reference
 //     Task, resolve g_op_alias/g_op_table at dequeue time and run it with the whole CTA;
-//   * completion is counted per flush; the last item of a flush writes that flush's
-//     ticket into mapped memory (single writer, no host-memory atomics);
+//     each compute warp signals a per-stage `done` barrier, with no CTA-wide barrier
+//     between tiles;
+//   * warp 1 is the completer: it returns finished stages to the dequeue warp at once and
+//     batches completion accounting (one fence for several items); completion is counted
+//     per flush and the last item of a flush writes that flush's ticket into mapped
+//     memory (single writer, no host-memory atomics);
 //   * every wait is bounded by %globaltimer; a wait that runs out records an error in the
 //     mapped report and the grid exits;
 //   * exit is coordinated so no ticket is lost: the CTAs park, the leader (CTA 0)
@@ -63,48 +67,90 @@ __device__ TileFn g_tile_fns[GPUOS_EW_NUM_OPS + 1] = {
     ew_tile<28>, ew_tile<29>, reduce_tile};
 
 // ---- completion ----------------------------------------------------------------------
-__device__ __forceinline__ void complete_item(const WorkerParams& P, const WorkItem& it) {
+// Completed items of one flush awaiting accounting (the completer warp batches them).
+struct DoneRun {
+  uint32_t batch, batch_items, batch_seq, n;
+};
+constexpr int kMaxRuns = 4;
+constexpr uint32_t kAccountEvery = 8;  // items per fence when completions stream in
+
+// One gpu-scope fence covers every item of the runs (their compute warps' stores were
+// ordered before the completer by the per-stage done barriers); then the per-flush
+// counters; the last item of a flush writes the flush's ticket into mapped memory.
+__device__ void account(const WorkerParams& P, const DoneRun* runs, int nruns) {
   ptx::fence_acq_rel_gpu();
-  atomicAdd(&P.dc->items_done, 1ull);
-  const unsigned int prev = atomicAdd(&P.dc->batch_done[it.batch], 1u);
-  if (prev + 1 == it.batch_items) {
-    ptx::fence_acq_rel_gpu();
-    P.dc->batch_done[it.batch] = 0u;
-    const unsigned long long t0 = atomicExch(&P.dc->batch_t0[it.batch], ~0ull);
-    Ticket& tk = P.tickets[it.batch];
-    ptx::st_relaxed_sys(&tk.t_start, t0);
-    ptx::st_relaxed_sys(&tk.t_end, ptx::now_ns());
-    ptx::fence_sc_sys();
-    ptx::st_relaxed_sys(&tk.seq, it.batch_seq);
+  unsigned long long total = 0;
+  for (int r = 0; r < nruns; ++r) {
+    const DoneRun& d = runs[r];
+    total += d.n;
+    const unsigned int prev = atomicAdd(&P.dc->batch_done[d.batch], d.n);
+    if (prev + d.n == d.batch_items) {
+      ptx::fence_acq_rel_gpu();
+      P.dc->batch_done[d.batch] = 0u;
+      const unsigned long long t0 = atomicExch(&P.dc->batch_t0[d.batch], ~0ull);
+      Ticket& tk = P.tickets[d.batch];
+      ptx::st_relaxed_sys(&tk.t_start, t0);
+      ptx::st_relaxed_sys(&tk.t_end, ptx::now_ns());
+      ptx::fence_sc_sys();
+      ptx::st_relaxed_sys(&tk.seq, d.batch_seq);
+    }
   }
+  atomicAdd(&P.dc->items_done, total);
+}
+
+// Bounded wait on an mbarrier phase (one lane).  `alive` is a %globaltimer stamp another
+// role refreshes while it makes progress; the wait fails once it is older than `limit`.
+__device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, const unsigned long long* alive,
+                                           uint64_t limit) {
+  uint32_t spins = 0;
+  while (!ptx::mbar_try_wait(bar, parity)) {
+    if ((++spins & 1023u) == 0) {
+      const uint64_t a = *reinterpret_cast<const volatile unsigned long long*>(alive);
+      if (ptx::now_ns() - a > limit) return false;
+    }
+  }
+  return true;
 }
 
 // ---- compute warps ----------------------------------------------------------------------
 __device__ void compute_loop(const WorkerParams& P, const WorkerShared& W, uint32_t ctid, uint32_t nct) {
   SmemHeader& H = *W.H;
   const uint32_t S = P.stages;
-  for (uint64_t iter = 0;; ++iter) {
-    const uint32_t s = (uint32_t)(iter % S);
-    const uint32_t parity = (uint32_t)((iter / S) & 1);
-    const uint32_t full = ptx::smem_addr(&H.full[s]);
-    uint32_t spins = 0;
-    while (!ptx::mbar_try_wait(full, parity)) {
-      if ((++spins & 1023u) == 0) {
-        const uint64_t alive = *reinterpret_cast<volatile unsigned long long*>(&H.prod_alive);
-        if (ptx::now_ns() - alive > P.hc->wait_limit_ns + P.hc->safety_idle_ns) {
-          report_error(P, DE_WAIT_FULL, iter);
-          return;
-        }
+  unsigned long long dg[4] = {0, 0, 0, 0};
+  unsigned long long n_items = 0;
+  struct Flush {
+    const WorkerParams& P;
+    uint32_t ctid;
+    unsigned long long* dg;
+    unsigned long long* n;
+    __device__ ~Flush() {
+      if (ctid == 0 && blockIdx.x < kDiagCtas) {
+        unsigned long long* row = P.dc->diag[blockIdx.x];
+        row[DG_C_WAIT_FULL] = dg[0];
+        row[DG_C_TILE] = dg[1];
+        row[DG_C_ITEMS] = *n;
       }
+    }
+  } flush_diag{P, ctid, dg, &n_items};
+  const uint32_t shift = __ffs(S) - 1;  // S is a power of two
+  for (uint64_t iter = 0;; ++iter) {
+    unsigned long long c0 = clock64();
+    const uint32_t s = (uint32_t)iter & (S - 1);
+    const uint32_t parity = (uint32_t)(iter >> shift) & 1;
+    if (!wait_phase(ptx::smem_addr(&H.full[s]), parity, &H.prod_alive, H.full_wait_ns)) {
+      report_error(P, DE_WAIT_FULL, iter);
+      return;
     }
     const StageMeta& m = H.meta[s];
     const uint8_t kind = m.item.kind;
+    unsigned long long c1 = clock64();
+    dg[0] += c1 - c0;
     if (kind == IK_EXIT) return;
     if (kind == IK_TASK) {
-      ptx::named_bar_sync(kBarTask, nct + 32);
+      ptx::named_bar_sync(kBarTask, blockDim.x);
       OpFn fn = reinterpret_cast<OpFn>(m.item.x);
       fn(m.ext.task);
-      ptx::named_bar_sync(kBarTask, nct + 32);
+      ptx::named_bar_sync(kBarTask, blockDim.x);
     } else {
       TileCtx ctx;
       ctx.m = &m;
@@ -116,18 +162,114 @@ __device__ void compute_loop(const WorkerParams& P, const WorkerShared& W, uint3
       TileFn fn = g_tile_fns[fi];
       fn(ctx);
     }
-    ptx::named_bar_sync(kBarCompute, nct);
+    // this warp is done with the stage; no CTA-wide barrier between tiles
+    __syncwarp();
+    if ((ctid & 31) == 0) ptx::mbar_arrive(ptx::smem_addr(&H.done[s]));
     if (ctid == 0) {
-      complete_item(P, m.item);
-      ptx::mbar_arrive(ptx::smem_addr(&H.empty[s]));
+      dg[1] += clock64() - c1;
+      ++n_items;
+    }
+  }
+}
+
+// ---- completer warp ------------------------------------------------------------------------
+// Follows the stages in order: once every compute warp has signalled `done`, it hands the
+// stage back to the dequeue warp and batches the completion accounting of several items
+// behind one fence.  Before it would block it publishes what it has, so a lone item is
+// accounted immediately.
+__device__ void completer_loop(const WorkerParams& P, const WorkerShared& W, uint32_t lane) {
+  SmemHeader& H = *W.H;
+  const uint32_t S = P.stages;
+  const uint32_t shift = __ffs(S) - 1;
+  DoneRun runs[kMaxRuns];
+  int nruns = 0;
+  uint32_t pending = 0;
+  unsigned long long t_wait = 0, t_acc = 0, n_items = 0;
+  for (uint64_t iter = 0;; ++iter) {
+    const uint32_t s = (uint32_t)iter & (S - 1);
+    const uint32_t parity = (uint32_t)(iter >> shift) & 1;
+    int kind = 0;
+    uint32_t batch = 0, batch_items = 0, batch_seq = 0;
+    if (lane == 0) {
+      unsigned long long c0 = clock64();
+      const uint32_t full = ptx::smem_addr(&H.full[s]);
+      if (nruns && !ptx::mbar_test_wait(full, parity)) {
+        unsigned long long a0 = clock64();
+        account(P, runs, nruns);
+        t_acc += clock64() - a0;
+        nruns = 0;
+        pending = 0;
+      }
+      if (!wait_phase(full, parity, &H.prod_alive, H.full_wait_ns)) {
+        report_error(P, DE_WAIT_FULL, iter);
+        kind = IK_EXIT;
+      } else {
+        const WorkItem& it = H.meta[s].item;
+        kind = it.kind;
+        batch = it.batch;
+        batch_items = it.batch_items;
+        batch_seq = it.batch_seq;
+      }
+      t_wait += clock64() - c0;
+    }
+    kind = __shfl_sync(0xffffffffu, kind, 0);
+    if (kind == IK_EXIT) break;
+    if (kind == IK_TASK) {
+      ptx::named_bar_sync(kBarTask, blockDim.x);
+      OpFn fn = reinterpret_cast<OpFn>(H.meta[s].item.x);
+      fn(H.meta[s].ext.task);
+      ptx::named_bar_sync(kBarTask, blockDim.x);
+    }
+    if (lane == 0) {
+      unsigned long long c0 = clock64();
+      const uint32_t done = ptx::smem_addr(&H.done[s]);
+      if (nruns && !ptx::mbar_test_wait(done, parity)) {
+        account(P, runs, nruns);
+        nruns = 0;
+        pending = 0;
+      }
+      bool ok = wait_phase(done, parity, &H.prod_alive, H.full_wait_ns);
+      unsigned long long c1 = clock64();
+      t_wait += c1 - c0;
+      if (!ok) {
+        report_error(P, DE_WAIT_FULL, iter);
+      } else {
+        ptx::mbar_arrive(ptx::smem_addr(&H.empty[s]));  // stage back to the dequeue warp
+        if (nruns && runs[nruns - 1].batch == batch && runs[nruns - 1].batch_seq == batch_seq) {
+          runs[nruns - 1].n += 1;
+        } else {
+          runs[nruns++] = DoneRun{batch, batch_items, batch_seq, 1u};
+        }
+        ++pending;
+        ++n_items;
+        if (pending >= kAccountEvery || nruns == kMaxRuns) {
+          account(P, runs, nruns);
+          nruns = 0;
+          pending = 0;
+        }
+        t_acc += clock64() - c1;
+      }
+    }
+    __syncwarp();
+  }
+  if (lane == 0) {
+    if (nruns) account(P, runs, nruns);
+    if (blockIdx.x < kDiagCtas) {
+      P.dc->diag[blockIdx.x][DG_C_BAR] = t_wait;
+      P.dc->diag[blockIdx.x][DG_C_COMPLETE] = t_acc;
     }
   }
 }
 
 // ---- dequeue warp -------------------------------------------------------------------------
+constexpr uint32_t kChunk = 4;  // tickets claimed per atomic when work is plentiful
+
 struct ProdState {
   uint64_t iter;        // items staged so far
-  uint64_t ticket;      // held ticket (kNoTicket if none)
+  uint64_t ticket;      // lowest unprocessed ticket held
+  uint64_t chunk_end;   // tickets [ticket, chunk_end) are claimed by this CTA
+  uint64_t desc_end;    // descriptors of tickets < desc_end are in the shared cache
+  uint32_t last_seq;    // flush of the last staged item (start stamp once per flush)
   uint64_t tail_cache;
   uint64_t items_done_cache;
   uint64_t seen_round;  // last closing round handled
@@ -135,13 +277,32 @@ struct ProdState {
   uint64_t beat_val;    // leader: last observed host beat
   uint64_t beat_t;      // leader: when it changed
   uint64_t polls;
+  // leader: cached host control words (refreshed every few polls, not every poll)
+  uint64_t quit_epoch, yield_every, safety_ns;
+  uint32_t spin_ns;
+  // leader: diagnostics
+  uint64_t read_sum, read_n, read_max;
+  uint64_t rounds, timeouts, work_resumes, parked_seen;
+  unsigned long long dg[6];
 };
+
+__device__ __forceinline__ void publish_diag(const WorkerParams& P, const ProdState& st) {
+  ptx::st_relaxed_sys(&P.rep->heartbeat, st.polls);
+  ptx::st_relaxed_sys(&P.rep->head_mirror, *reinterpret_cast<volatile unsigned long long*>(&P.dc->head));
+  ptx::st_relaxed_sys(&P.rep->items_done, *reinterpret_cast<volatile unsigned long long*>(&P.dc->items_done));
+  ptx::st_relaxed_sys(&P.rep->park_rounds, st.rounds);
+  ptx::st_relaxed_sys(&P.rep->park_timeouts, st.timeouts);
+  ptx::st_relaxed_sys(&P.rep->park_work, st.work_resumes);
+  ptx::st_relaxed_sys(&P.rep->parked_seen, st.parked_seen);
+  ptx::st_relaxed_sys(&P.rep->host_read_ns_max, st.read_max);
+  ptx::st_relaxed_sys(&P.rep->host_read_ns_avg, st.read_n ? st.read_sum / st.read_n : 0);
+}
 
 // Wait (lane 0) until compute warps released stage use `use` (i.e. iteration use-1 done).
 __device__ bool wait_empty(const WorkerParams& P, SmemHeader& H, uint64_t iter, uint32_t S) {
   if (iter < S) return true;
-  const uint32_t s = (uint32_t)(iter % S);
-  const uint32_t parity = (uint32_t)(((iter / S) - 1) & 1);
+  const uint32_t s = (uint32_t)iter & (S - 1);
+  const uint32_t parity = (uint32_t)(((iter >> (__ffs(S) - 1)) - 1) & 1);
   const uint32_t bar = ptx::smem_addr(&H.empty[s]);
   const uint64_t t0 = ptx::now_ns();
   uint32_t spins = 0;
@@ -163,8 +324,8 @@ __device__ bool drain_own(const WorkerParams& P, SmemHeader& H, uint64_t iter, u
   const uint64_t lo = iter > S ? iter - S : 0;
   for (uint64_t u = lo; u < iter; ++u) {
     // use u was released when the empty barrier of its stage completed phase (u / S)
-    const uint32_t s = (uint32_t)(u % S);
-    const uint32_t parity = (uint32_t)((u / S) & 1);
+    const uint32_t s = (uint32_t)u & (S - 1);
+    const uint32_t parity = (uint32_t)((u >> (__ffs(S) - 1)) & 1);
     const uint32_t bar = ptx::smem_addr(&H.empty[s]);
     const uint64_t t0 = ptx::now_ns();
     uint32_t spins = 0;
@@ -216,11 +377,18 @@ __device__ int park(const WorkerParams& P, SmemHeader& H, ProdState& st, uint64_
       }
       if (*reinterpret_cast<volatile unsigned int*>(&dc->abort)) break;
       const uint64_t t = ptx::ld_acquire_sys(&P.hc->tail);
-      if (t > *reinterpret_cast<volatile unsigned long long*>(&dc->park_min)) break;  // work for a parked CTA
+      if (t > *reinterpret_cast<volatile unsigned long long*>(&dc->park_min)) {  // work for a parked CTA
+        ++st.work_resumes;
+        break;
+      }
       if ((++spins & 15u) == 0) {
         const uint64_t now = ptx::now_ns();
         *reinterpret_cast<volatile unsigned long long*>(&H.prod_alive) = now;
-        if (now - t0 > kGatherNs) break;  // someone is still busy: retry later
+        if (now - t0 > kGatherNs) {  // someone is still busy: retry later
+          ++st.timeouts;
+          st.parked_seen = ptx::ld_acquire_gpu(&dc->park_word) & 0xffffffffull;
+          break;
+        }
       }
       ptx::nanosleep(128);
     }
@@ -237,12 +405,14 @@ __device__ int park(const WorkerParams& P, SmemHeader& H, ProdState& st, uint64_
     const uint64_t T = ptx::ld_acquire_sys(&P.hc->tail);
     const uint64_t pm = *reinterpret_cast<volatile unsigned long long*>(&dc->park_min);
     if (!aborted && T > pm) {
+      ++st.work_resumes;
       ptx::st_relaxed_sys(&P.rep->state, (P.epoch << 8) | WS_RUNNING);
       ptx::st_release_gpu(&dc->tail_mirror, T);
       ptx::st_release_gpu(&dc->verdict, (round << 2) | PV_RESUME);
       return PV_RESUME;
     }
     dc->exit_tail = pm;
+    publish_diag(P, st);
     ptx::st_release_gpu(&dc->verdict, (round << 2) | PV_EXIT);
     return PV_EXIT;
   }
@@ -283,10 +453,12 @@ __device__ __forceinline__ void arm_exit(SmemHeader& H, uint32_t s) {
 __device__ bool stage_item(const WorkerParams& P, const WorkerShared& W, ProdState& st, uint32_t lane) {
   SmemHeader& H = *W.H;
   const uint32_t S = P.stages;
-  const uint32_t s = (uint32_t)(st.iter % S);
+  const uint32_t s = (uint32_t)st.iter & (S - 1);
   StageMeta& m = H.meta[s];
-  const WorkItem* src = P.items + (st.ticket & P.item_mask);
-  warp_copy16(&m.item, src, sizeof(WorkItem), lane);
+  if (lane < 4) {
+    const uint4* src = reinterpret_cast<const uint4*>(&H.dcache[st.ticket & 7]);
+    reinterpret_cast<uint4*>(&m.item)[lane] = src[lane];
+  }
   __syncwarp();
   const WorkItem it = m.item;
   int ok = 1;
@@ -316,8 +488,12 @@ __device__ bool stage_item(const WorkerParams& P, const WorkerShared& W, ProdSta
         ptx::nanosleep(64);
       }
     }
-    if (ok) atomicMin(&P.dc->batch_t0[it.batch], (unsigned long long)ptx::now_ns());
-    else arm_exit(H, s);
+    // start stamp of the flush: the first item each CTA stages from it is enough
+    if (ok && it.batch_seq != st.last_seq) {
+      atomicMin(&P.dc->batch_t0[it.batch], (unsigned long long)ptx::now_ns());
+      st.last_seq = it.batch_seq;
+    }
+    if (!ok) arm_exit(H, s);
   }
   ok = __shfl_sync(0xffffffffu, ok, 0);
   if (!ok) return false;
@@ -408,7 +584,7 @@ __device__ void push_exit(const WorkerParams& P, SmemHeader& H, ProdState& st, u
   const uint32_t S = P.stages;
   if (lane == 0) {
     wait_empty(P, H, st.iter, S);
-    arm_exit(H, (uint32_t)(st.iter % S));
+    arm_exit(H, (uint32_t)st.iter & (S - 1));
   }
   __syncwarp();
 }
@@ -420,7 +596,10 @@ __device__ void producer_loop(const WorkerParams& P, const WorkerShared& W, uint
   const bool leader = blockIdx.x == 0;
   ProdState st;
   st.iter = 0;
-  st.ticket = kNoTicket;
+  st.ticket = 0;
+  st.chunk_end = 0;
+  st.desc_end = 0;
+  st.last_seq = 0;
   st.tail_cache = ptx::ld_acquire_gpu(&dc->tail_mirror);
   st.items_done_cache = 0;
   st.seen_round = 0;
@@ -428,20 +607,59 @@ __device__ void producer_loop(const WorkerParams& P, const WorkerShared& W, uint
   st.beat_val = P.hc->host_beat;
   st.beat_t = ptx::now_ns();
   st.polls = 0;
+  st.quit_epoch = P.hc->quit_epoch;
+  st.yield_every = P.hc->yield_every;
+  st.safety_ns = P.hc->safety_idle_ns;
+  st.spin_ns = P.hc->spin_ns;
+  st.read_sum = st.read_n = st.read_max = 0;
+  st.rounds = st.timeouts = st.work_resumes = st.parked_seen = 0;
+  for (int k = 0; k < 6; ++k) st.dg[k] = 0;
+  struct Flush {
+    const WorkerParams& P;
+    uint32_t lane;
+    ProdState& st;
+    __device__ ~Flush() {
+      if (lane == 0 && blockIdx.x < kDiagCtas) {
+        unsigned long long* row = P.dc->diag[blockIdx.x];
+        for (int k = 0; k < 6; ++k) row[k] = st.dg[k];
+      }
+    }
+  } flush_diag{P, lane, st};
 
   while (true) {
     int action = 0;  // 0: stage ticket, 1: exit
     if (lane == 0) {
-      if (st.ticket == kNoTicket) {
-        if (!wait_empty(P, H, st.iter, S)) action = 1;
-        else st.ticket = atomicAdd(&dc->head, 1ull);
+      unsigned long long c0 = clock64();
+      const bool empty_ok = wait_empty(P, H, st.iter, S);
+      unsigned long long c1 = clock64();
+      st.dg[DG_P_WAIT_EMPTY] += c1 - c0;
+      if (!empty_ok) {
+        action = 1;
+      } else if (st.ticket == st.chunk_end) {
+        // Claim a chunk: several tickets per atomic while plenty of published work lies
+        // ahead, single tickets near the end of the published work (load balance).
+        const uint64_t ahead = st.tail_cache > st.chunk_end ? st.tail_cache - st.chunk_end : 0;
+        uint64_t k = ahead / (2ull * gridDim.x);
+        k = k < 1 ? 1 : (k > kChunk ? kChunk : k);
+        st.ticket = atomicAdd(&dc->head, k);
+        st.chunk_end = st.ticket + k;
+        st.desc_end = st.ticket;
+        c0 = clock64();
+        st.dg[DG_P_CLAIM] += c0 - c1;
+        c1 = c0;
       }
       while (action == 0 && st.ticket >= st.tail_cache) {
         // idle: poll for publication, watch for exit conditions
         ++st.polls;
         uint64_t t;
-        if (leader || (st.polls & 15u) == 0) {
+        if (leader) {
+          // only the leader reads host memory; everybody else polls its device mirror
+          const uint64_t r0 = ptx::now_ns();
           t = ptx::ld_acquire_sys(&P.hc->tail);
+          const uint64_t dr = ptx::now_ns() - r0;
+          st.read_sum += dr;
+          ++st.read_n;
+          if (dr > st.read_max) st.read_max = dr;
           if (t > *reinterpret_cast<volatile unsigned long long*>(&dc->tail_mirror)) ptx::st_release_gpu(&dc->tail_mirror, t);
         } else {
           t = ptx::ld_acquire_gpu(&dc->tail_mirror);
@@ -457,22 +675,24 @@ __device__ void producer_loop(const WorkerParams& P, const WorkerShared& W, uint
           break;
         }
         if (leader && (st.polls & 7u) == 0) {
-          if ((st.polls & 63u) == 0) {
-            ptx::st_relaxed_sys(&P.rep->heartbeat, st.polls);
-            ptx::st_relaxed_sys(&P.rep->head_mirror, *reinterpret_cast<volatile unsigned long long*>(&dc->head));
-            ptx::st_relaxed_sys(&P.rep->items_done, *reinterpret_cast<volatile unsigned long long*>(&dc->items_done));
-          }
+          st.quit_epoch = P.hc->quit_epoch;
           const uint64_t beat = P.hc->host_beat;
           if (beat != st.beat_val) {
             st.beat_val = beat;
             st.beat_t = now;
           }
-          bool want_exit = P.hc->quit_epoch >= P.epoch;
-          const uint64_t ye = P.hc->yield_every;
-          if (ye && ptx::ld_acquire_gpu(&dc->items_done) - dc->yield_base >= ye) want_exit = true;
-          if (now - st.beat_t > P.hc->safety_idle_ns) want_exit = true;
+          if ((st.polls & 63u) == 0) {
+            st.yield_every = P.hc->yield_every;
+            st.safety_ns = P.hc->safety_idle_ns;
+            st.spin_ns = P.hc->spin_ns;
+            publish_diag(P, st);
+          }
+          bool want_exit = st.quit_epoch >= P.epoch;
+          if (st.yield_every && ptx::ld_acquire_gpu(&dc->items_done) - dc->yield_base >= st.yield_every) want_exit = true;
+          if (now - st.beat_t > st.safety_ns) want_exit = true;
           if (want_exit) {
             st.round = (st.round > st.seen_round ? st.round : st.seen_round) + 1;
+            ++st.rounds;
             dc->park_min = ~0ull;
             atomicExch(&dc->park_word, (unsigned long long)st.round << 32);
             ptx::fence_acq_rel_gpu();
@@ -489,8 +709,9 @@ __device__ void producer_loop(const WorkerParams& P, const WorkerShared& W, uint
           st.tail_cache = ptx::ld_acquire_gpu(&dc->tail_mirror);
           continue;
         }
-        ptx::nanosleep(leader ? P.hc->spin_ns : 256);
+        ptx::nanosleep(leader ? st.spin_ns : 256);
       }
+      st.dg[DG_P_IDLE] += clock64() - c1;
     }
     action = __shfl_sync(0xffffffffu, action, 0);
     if (action == 1) {
@@ -498,9 +719,29 @@ __device__ void producer_loop(const WorkerParams& P, const WorkerShared& W, uint
       return;
     }
     st.ticket = __shfl_sync(0xffffffffu, st.ticket, 0);
+    st.chunk_end = __shfl_sync(0xffffffffu, st.chunk_end, 0);
+    st.desc_end = __shfl_sync(0xffffffffu, st.desc_end, 0);
+    st.tail_cache = __shfl_sync(0xffffffffu, st.tail_cache, 0);
+    unsigned long long cd = clock64();
+    if (st.ticket >= st.desc_end) {
+      // one warp-wide read fetches the descriptors of every published ticket of the chunk
+      const uint64_t hi = st.chunk_end < st.tail_cache ? st.chunk_end : st.tail_cache;
+      const uint32_t cnt = (uint32_t)(hi - st.ticket);
+      if (lane < 4 * cnt) {
+        const uint64_t t = st.ticket + (lane >> 2);
+        const unsigned char* src = reinterpret_cast<const unsigned char*>(P.items + (t & P.item_mask)) + (lane & 3) * 16;
+        reinterpret_cast<uint4*>(&H.dcache[t & 7])[lane & 3] = ptx::ld_volatile_v4(src);
+      }
+      __syncwarp();
+      st.desc_end = hi;
+    }
+    unsigned long long ce = clock64();
+    st.dg[DG_P_DESC] += ce - cd;
     if (!stage_item(P, W, st, lane)) return;
+    st.dg[DG_P_STAGE] += clock64() - ce;
+    st.dg[DG_P_ITEMS] += 1;
     st.iter = __shfl_sync(0xffffffffu, st.iter, 0) + 1;
-    st.ticket = kNoTicket;
+    st.ticket += 1;
   }
 }
 
@@ -518,9 +759,11 @@ __device__ void batch_worker_body(const WorkerParams& P, unsigned char* smem_raw
     for (uint32_t s = 0; s < S; ++s) {
       ptx::mbar_init(ptx::smem_addr(&H->full[s]), 1);
       ptx::mbar_init(ptx::smem_addr(&H->empty[s]), 1);
+      ptx::mbar_init(ptx::smem_addr(&H->done[s]), (blockDim.x - 64) / 32);
     }
     ptx::fence_mbar_init();
     H->prod_alive = ptx::now_ns();
+    H->full_wait_ns = P.hc->wait_limit_ns + P.hc->safety_idle_ns;
     H->exit_flag = 0;
   }
   __syncthreads();
@@ -542,6 +785,7 @@ __device__ void batch_worker_body(const WorkerParams& P, unsigned char* smem_raw
       dc->tail_mirror = ptx::ld_acquire_sys(&P.hc->tail);
       ptx::fence_acq_rel_gpu();
       ptx::st_release_gpu(&dc->launch_epoch, P.epoch);
+      ptx::st_relaxed_sys(&P.rep->t_launch, ptx::now_ns());
       ptx::st_relaxed_sys(&P.rep->state, (P.epoch << 8) | WS_RUNNING);
       ptx::fence_acq_rel_sys();
       ptx::st_relaxed_sys(&P.rep->ready_epoch, P.epoch);
@@ -558,17 +802,21 @@ __device__ void batch_worker_body(const WorkerParams& P, unsigned char* smem_raw
     }
   }
   __syncthreads();
+  const unsigned long long cta_c0 = clock64();
   if (start_ok) {
     const uint32_t warp = threadIdx.x >> 5;
     if (warp == 0) producer_loop(P, W, threadIdx.x & 31);
-    else compute_loop(P, W, threadIdx.x - 32, blockDim.x - 32);
+    else if (warp == 1) completer_loop(P, W, threadIdx.x & 31);
+    else compute_loop(P, W, threadIdx.x - 64, blockDim.x - 64);
   }
   __syncthreads();
   if (threadIdx.x == 0) {
+    if (blockIdx.x < kDiagCtas) dc->diag[blockIdx.x][DG_CYCLES] = clock64() - cta_c0;
     ptx::fence_acq_rel_gpu();
     const unsigned int n = atomicAdd(&dc->exited, 1u) + 1;
     if (n == gridDim.x) {
       ptx::st_relaxed_sys(&P.rep->exit_tail, dc->exit_tail);
+      ptx::st_relaxed_sys(&P.rep->t_exit, ptx::now_ns());
       ptx::st_relaxed_sys(&P.rep->items_done, dc->items_done);
       ptx::fence_sc_sys();
       ptx::st_relaxed_sys(&P.rep->state, (P.epoch << 8) | WS_EXITED);

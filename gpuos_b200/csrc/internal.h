@@ -111,7 +111,15 @@ struct alignas(128) DevReport {
   volatile uint64_t error_item;      // item index involved in the error
   volatile uint64_t head_mirror;     // dequeue position (for peek_queue)
   volatile uint64_t items_done;      // completed items (mirror)
-  uint64_t _pad[8];
+  // diagnostics (leader / last CTA)
+  volatile uint64_t t_launch;        // %globaltimer when CTA 0 initialised the launch
+  volatile uint64_t t_exit;          // %globaltimer when the last CTA left
+  volatile uint64_t park_rounds;     // exit rounds started by the leader (this launch)
+  volatile uint64_t park_timeouts;   // rounds abandoned because not every CTA parked in time
+  volatile uint64_t park_work;       // rounds abandoned because work arrived
+  volatile uint64_t host_read_ns_max;  // slowest leader read of the host tail
+  volatile uint64_t host_read_ns_avg;  // average leader read of the host tail
+  volatile uint64_t parked_seen;     // CTAs parked when the last round was abandoned
 };
 
 enum DeviceError : uint32_t {
@@ -136,6 +144,24 @@ struct alignas(32) Ticket {
 
 constexpr int kNumBatchSlots = 1024;
 
+// Per-CTA cycle counters (clock64) of one launch, written when the CTA exits.
+enum DiagSlot {
+  DG_P_WAIT_EMPTY = 0,  // dequeue warp: waiting for a free stage
+  DG_P_CLAIM,           // dequeue warp: ticket atomics
+  DG_P_IDLE,            // dequeue warp: waiting for publication (idle / park)
+  DG_P_DESC,            // dequeue warp: descriptor fetch from the mapped ring
+  DG_P_STAGE,           // dequeue warp: staging (barrier check, TMA issue, Task run)
+  DG_P_ITEMS,           // items staged
+  DG_C_WAIT_FULL,       // compute thread 0: waiting for a filled stage
+  DG_C_TILE,            // compute thread 0: tile function
+  DG_C_BAR,             // compute thread 0: compute-warp barrier after the tile
+  DG_C_COMPLETE,        // compute thread 0: completion accounting
+  DG_C_ITEMS,           // items computed
+  DG_CYCLES,            // total cycles of the CTA
+  kDiagSlots = 12
+};
+constexpr int kDiagCtas = 256;
+
 // Device-memory control block (cudaMalloc, zeroed at init).
 struct alignas(128) DevCtl {
   unsigned long long head;         // next item ticket
@@ -153,6 +179,7 @@ struct alignas(128) DevCtl {
   unsigned long long _pad[5];
   unsigned int batch_done[kNumBatchSlots];
   unsigned long long batch_t0[kNumBatchSlots];
+  unsigned long long diag[kDiagCtas][kDiagSlots];  // per-CTA cycle counters of the last launch
 };
 
 // ---- worker launch parameters ---------------------------------------------------------
@@ -195,12 +222,15 @@ struct alignas(16) StageMeta {
 // Worker shared-memory header (stage buffers follow, 128-byte aligned).
 constexpr int kMaxStages = 8;
 struct alignas(128) SmemHeader {
-  unsigned long long full[kMaxStages];
-  unsigned long long empty[kMaxStages];
+  unsigned long long full[kMaxStages];   // dequeue warp -> compute warps (+ TMA bytes)
+  unsigned long long empty[kMaxStages];  // completer -> dequeue warp
+  unsigned long long done[kMaxStages];   // compute warps -> completer
   unsigned long long prod_alive;   // %globaltimer stamp of the dequeue warp
+  unsigned long long full_wait_ns; // compute warps' bound on a silent dequeue warp
   unsigned int exit_flag;
   unsigned int _pad;
   StageMeta meta[kMaxStages];
+  WorkItem dcache[8];              // descriptors of the claimed chunk (ticket & 7)
 };
 
 constexpr uint32_t kStageBytesDefault = 32768 + 128;  // two 16 KB operand halves + slack

@@ -661,6 +661,24 @@ PyObject* py_debug_inject_stall(PyObject*, PyObject* args, PyObject* kw) {
   Py_RETURN_NONE;
 }
 
+PyObject* py_debug_counters(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"device", nullptr};
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "|O", const_cast<char**>(kwlist), &devobj)) return nullptr;
+  gpuos_rt* rt = rt_arg(devobj, nullptr);
+  if (!rt) return nullptr;
+  std::vector<uint64_t> buf(256 * 12);
+  const int ctas = gpuos_rt_debug_counters(rt, buf.data(), (int)buf.size());
+  if (ctas < 0) return raise_status(-ctas);
+  PyObject* rows = PyList_New(ctas);
+  for (int c = 0; c < ctas; ++c) {
+    PyObject* row = PyList_New(12);
+    for (int k = 0; k < 12; ++k) PyList_SET_ITEM(row, k, PyLong_FromUnsignedLongLong(buf[c * 12 + k]));
+    PyList_SET_ITEM(rows, c, row);
+  }
+  return rows;
+}
+
 PyObject* py_launches(PyObject*, PyObject* args, PyObject* kw) {
   static const char* kwlist[] = {"device", nullptr};
   PyObject* devobj = Py_None;
@@ -945,6 +963,8 @@ PyMethodDef kMethods[] = {
      "raw handle of the worker kernel's stream"},
     {"launches", (PyCFunction)(void (*)(void))py_launches, METH_VARARGS | METH_KEYWORDS, "worker launches so far"},
     {"set_device_wait_ms", py_set_device_wait_ms, METH_VARARGS, "bound of the worker's in-grid waits"},
+    {"debug_counters", (PyCFunction)(void (*)(void))py_debug_counters, METH_VARARGS | METH_KEYWORDS,
+     "per-CTA cycle counters of the last worker launch"},
     {"debug_inject_stall", (PyCFunction)(void (*)(void))py_debug_inject_stall, METH_VARARGS | METH_KEYWORDS,
      "publish an item whose dependency barrier never opens (failure-path test)"},
     {"submit_unary", (PyCFunction)(void (*)(void))py_submit_unary, METH_FASTCALL, "submit_unary(slot, a, out)"},

@@ -39,6 +39,7 @@ extern "C" cudaError_t gpuos_internal_launch_batch_worker(const WorkerParams* p,
                                                           size_t smem, cudaStream_t s);
 extern "C" cudaError_t gpuos_internal_set_worker_smem(size_t smem);
 extern "C" cudaError_t gpuos_internal_table_ptrs(void** table, void** alias);
+extern "C" cudaError_t gpuos_internal_preload_kernels();
 extern "C" size_t gpuos_internal_smem_header_bytes();
 
 // ---- errors -----------------------------------------------------------------------------
@@ -367,7 +368,7 @@ int plan_reduce(int rop, const GpuosOperand& x, const GpuosOperand& out, const i
   p->nreads = 0;
   const int64_t nout = numel_of(out.ndim, out.sizes);
   if (nout == 0) return GPUOS_OK;
-  if (!x.data || !out.data) return fail(GPUOS_ERR_INVALID, "null data pointer");
+  if (!out.data || (!x.data && numel_of(x.ndim, x.sizes) != 0)) return fail(GPUOS_ERR_INVALID, "null data pointer");
 
   Dims kept, rd;
   kept.nd = 0;
@@ -409,7 +410,7 @@ int plan_reduce(int rop, const GpuosOperand& x, const GpuosOperand& out, const i
     const int64_t C = rd.size[0], is = rd.st[0][0];
     const int64_t rows = kept.nd ? kept.size[0] : 1;
     const int64_t rs = kept.nd ? kept.st[0][0] : 0;
-    if (is >= 1 && (rows == 1 || C * is <= rs) && C <= 0x7fffffff) {
+    if (C > 0 && is >= 1 && (rows == 1 || C * is <= rs) && C <= 0x7fffffff) {
       const int64_t row_span = ((C - 1) * is + 1) * es;
       int64_t rows_per;
       uint8_t fl = proto.flags;
@@ -733,7 +734,8 @@ static int launch_worker_locked(gpuos_rt* rt) {
   P.stage_bytes = rt->stage_bytes;
   P.compute_threads = (uint32_t)rt->tpb;
   CK(cudaSetDevice(rt->device));
-  CK(gpuos_internal_launch_batch_worker(&P, rt->sm_count, rt->tpb + 32, rt->smem, rt->kstream));
+  // one dequeue warp + one completer warp + threads_per_block compute threads
+  CK(gpuos_internal_launch_batch_worker(&P, rt->sm_count, rt->tpb + 64, rt->smem, rt->kstream));
   rt->launched = true;
   return GPUOS_OK;
 }
@@ -897,8 +899,8 @@ extern "C" int gpuos_rt_init(int device, int capacity, int threads_per_block, gp
   }
   if (capacity <= 0) capacity = 4096;
   if (threads_per_block <= 0) threads_per_block = 256;
-  if (threads_per_block % 32 != 0 || threads_per_block < 64 || threads_per_block > 992)
-    return fail(GPUOS_ERR_INVALID, "threads_per_block must be a multiple of 32 in [64, 992]");
+  if (threads_per_block % 32 != 0 || threads_per_block < 64 || threads_per_block > 960)
+    return fail(GPUOS_ERR_INVALID, "threads_per_block must be a multiple of 32 in [64, 960]");
   int ndev = 0;
   CK(cudaGetDeviceCount(&ndev));
   if (device < 0 || device >= ndev) return fail(GPUOS_ERR_INVALID, "device %d out of range (%d devices)", device, ndev);
@@ -910,7 +912,12 @@ extern "C" int gpuos_rt_init(int device, int capacity, int threads_per_block, gp
   rt->tpb = threads_per_block;
   rt->verbose = env_int("GPUOS_VERBOSE", 0);
   rt->idle_quiesce_ms = env_int("GPUOS_IDLE_QUIESCE_MS", 200);
-  rt->stages = (uint32_t)std::max(2, std::min(kMaxStages, env_int("GPUOS_STAGES", 4)));
+  {
+    // stage count: a power of two in [2, kMaxStages]
+    const int want = std::max(2, std::min(kMaxStages, env_int("GPUOS_STAGES", 4)));
+    rt->stages = 2;
+    while ((int)rt->stages * 2 <= want) rt->stages *= 2;
+  }
   auto cleanup = [&](int code) {
     if (rt->host_block) cudaFreeHost(rt->host_block);
     if (rt->dc) cudaFree(rt->dc);
@@ -925,7 +932,7 @@ extern "C" int gpuos_rt_init(int device, int capacity, int threads_per_block, gp
   cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
   rt->smem = gpuos_internal_smem_header_bytes() + (size_t)rt->stages * rt->stage_bytes;
   while (rt->smem > (size_t)smem_optin && rt->stages > 2) {
-    --rt->stages;
+    rt->stages /= 2;
     rt->smem = gpuos_internal_smem_header_bytes() + (size_t)rt->stages * rt->stage_bytes;
   }
   rt->item_cap = pow2_at_least(std::max<uint64_t>((uint64_t)capacity * 8, 1u << 16));
@@ -965,6 +972,7 @@ extern "C" int gpuos_rt_init(int device, int capacity, int threads_per_block, gp
   if (e == cudaSuccess) e = cudaStreamSynchronize(rt->cstream);
   if (e == cudaSuccess) e = gpuos_internal_table_ptrs(&rt->op_table, &rt->op_alias);
   if (e == cudaSuccess) e = gpuos_internal_set_worker_smem(rt->smem);
+  if (e == cudaSuccess) e = gpuos_internal_preload_kernels();
   if (e != cudaSuccess) return cleanup(fail(GPUOS_ERR_CUDA, "runtime setup: %s", cudaGetErrorString(e)));
   rt->last_activity_ns = mono_ns();
   {
@@ -1270,6 +1278,21 @@ extern "C" int gpuos_rt_set_yield_every(gpuos_rt* rt, uint64_t every) {
   return GPUOS_OK;
 }
 
+extern "C" int gpuos_rt_debug_counters(gpuos_rt* rt, uint64_t* out, int n) {
+  if (!rt) return -fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  const int ctas = std::min(rt->sm_count, kDiagCtas);
+  std::vector<unsigned long long> buf((size_t)ctas * kDiagSlots);
+  cudaError_t e = cudaSetDevice(rt->device);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(buf.data(), rt->dc->diag, buf.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost,
+                        rt->cstream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(rt->cstream);
+  if (e != cudaSuccess) return -fail(GPUOS_ERR_CUDA, "debug_counters: %s", cudaGetErrorString(e));
+  const int m = std::min<int>(n, (int)buf.size());
+  for (int i = 0; i < m; ++i) out[i] = buf[i];
+  return ctas;
+}
+
 extern "C" int gpuos_rt_set_device_wait_ms(gpuos_rt* rt, int ms) {
   if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
   if (ms <= 0) return fail(GPUOS_ERR_INVALID, "device wait bound must be positive");
@@ -1308,14 +1331,15 @@ extern "C" int gpuos_rt_set_idle_quiesce_ms(gpuos_rt* rt, int ms) {
 extern "C" const char* gpuos_rt_stat_names(void) {
   return "head,tail,in_flight,capacity,processed,heartbeat,quit,host_tail_shadow,host_pending,"
          "item_capacity,sync_processed,sync_heartbeat,sync_ready,sync_submitted,epoch,state,error,items_done,"
-         "completed_seq,last_seq";
+         "completed_seq,last_seq,t_launch_ns,t_exit_ns,park_rounds,park_timeouts,park_work,host_read_ns_max,"
+         "host_read_ns_avg,parked_seen";
 }
 
 extern "C" int gpuos_rt_stats(gpuos_rt* rt, int64_t* v, int n) {
   if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
   std::lock_guard<std::mutex> lk(rt->mu);
   reap_locked(rt);
-  int64_t vals[20];
+  int64_t vals[28];
   vals[0] = (int64_t)rt->rep->head_mirror;
   vals[1] = (int64_t)rt->item_pub;
   vals[2] = (int64_t)(rt->item_pub - std::min(rt->item_pub, (uint64_t)rt->rep->items_done));
@@ -1336,7 +1360,15 @@ extern "C" int gpuos_rt_stats(gpuos_rt* rt, int64_t* v, int n) {
   vals[17] = (int64_t)rt->rep->items_done;
   vals[18] = (int64_t)rt->completed_seq;
   vals[19] = (int64_t)rt->last_seq;
-  for (int i = 0; i < n && i < 20; ++i) v[i] = vals[i];
+  vals[20] = (int64_t)rt->rep->t_launch;
+  vals[21] = (int64_t)rt->rep->t_exit;
+  vals[22] = (int64_t)rt->rep->park_rounds;
+  vals[23] = (int64_t)rt->rep->park_timeouts;
+  vals[24] = (int64_t)rt->rep->park_work;
+  vals[25] = (int64_t)rt->rep->host_read_ns_max;
+  vals[26] = (int64_t)rt->rep->host_read_ns_avg;
+  vals[27] = (int64_t)rt->rep->parked_seen;
+  for (int i = 0; i < n && i < 28; ++i) v[i] = vals[i];
   return GPUOS_OK;
 }
 

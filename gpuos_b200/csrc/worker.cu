@@ -166,8 +166,22 @@ extern "C" cudaError_t launch_init_builtin_ops(cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+// Under CUDA's default lazy module loading a kernel is loaded on its first launch, and that
+// load can wait for kernels already running on the device.  A persistent worker never
+// finishes on its own, so every kernel of this library is loaded before a worker starts.
+extern "C" cudaError_t gpuos_internal_preload_kernels() {
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaFuncGetAttributes(&fa, init_builtin_ops_kernel);
+  if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, builtin_addr_kernel);
+  if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, gpuos_batch_worker);
+  if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, ring_worker_kernel);
+  return e;
+}
+
 extern "C" cudaError_t launch_persistent_worker(WorkQueue q, int blocks, int threads, cudaStream_t stream) {
   if (blocks <= 0 || threads <= 0 || threads > 1024) return cudaErrorInvalidValue;
+  cudaError_t e = gpuos_internal_preload_kernels();
+  if (e != cudaSuccess) return e;
   ring_worker_kernel<<<blocks, threads, 0, stream>>>(q);
   return cudaGetLastError();
 }

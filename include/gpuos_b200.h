@@ -274,6 +274,13 @@ int gpuos_rt_flush_times(gpuos_rt* rt, uint64_t seq, uint64_t* t_start, uint64_t
 cudaStream_t gpuos_rt_kernel_stream(gpuos_rt* rt);
 uint64_t gpuos_rt_launches(gpuos_rt* rt);
 
+/* Per-CTA cycle counters of the last worker launch (valid once it has exited, e.g.
+ * after gpuos_rt_quiesce): rows of 12 counters (stage wait, claim, idle, descriptor
+ * fetch, staging, items staged, fill wait, tile, barrier, completion, items computed,
+ * total cycles), one row per CTA.  Copies min(n, ctas*12) values into out and returns
+ * the number of CTAs (negative status on error). */
+int gpuos_rt_debug_counters(gpuos_rt* rt, uint64_t* out, int n);
+
 /* Device-free planning hooks (no CUDA call): the 64-byte work items (and, for strided
  * requests, the 432-byte layout record) a request would be split into.  Used to test
  * broadcast, dimension coalescing and tiling on hosts without a GPU.  items_out holds

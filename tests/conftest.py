@@ -3,6 +3,10 @@ import sys
 
 import pytest
 
+# One hardware work queue per persistent kernel: keep other streams off it (see
+# gpuos_b200/__init__.py); must be set before CUDA initialises.
+os.environ.setdefault("CUDA_DEVICE_MAX_CONNECTIONS", "32")
+
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)

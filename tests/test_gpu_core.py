@@ -133,15 +133,22 @@ def test_quiesce_and_relaunch(rt):
 
 
 def test_drain_mode_each_flush_launches(rt):
+    # drain mode: the worker exits once the ring is drained, the next flush relaunches it
+    import time
     a = torch.randn(3000, device="cuda")
     o = torch.empty_like(a)
     rt.set_idle_quiesce_ms(0)
     try:
+        rt.quiesce()
         n0 = rt.launches()
         for _ in range(3):
             rt.submit_mul(a, a, o)
             rt.flush(sync=True)
-        assert rt.launches() >= n0 + 1
+            t0 = time.time()
+            while rt.worker_alive() and time.time() - t0 < 5:
+                time.sleep(0.001)
+            assert not rt.worker_alive()
+        assert rt.launches() == n0 + 3
         assert same_bits(o.cpu(), a.cpu() * a.cpu())
     finally:
         rt.set_idle_quiesce_ms(200)

@@ -14,7 +14,7 @@ pytestmark = pytest.mark.gpu
 
 def check(rt, x_cpu, axes, keepdim, mean, x_dev=None):
     x_dev = x_cpu.cuda() if x_dev is None else x_dev
-    ax = sorted(a % x_cpu.dim() for a in axes)
+    ax = sorted(a % x_cpu.dim() for a in axes) if axes else list(range(x_cpu.dim()))
     shape = list(x_cpu.shape)
     out_shape = [1 if i in ax else s for i, s in enumerate(shape)] if keepdim else \
         [s for i, s in enumerate(shape) if i not in ax]

@@ -165,6 +165,18 @@ def test_reference_task_ring_worker_c_abi(rt):
     lib.gpu_get_processed_count_async(ctypes.byref(proc), s)
     stream.synchronize()
     base = proc.value
+    # The ring is filled and tail/quit are published with copies from pinned host memory on
+    # a second stream: copies need no kernel, and a kernel that is not loaded yet could wait
+    # for the running ring worker under lazy module loading.
+    side = torch.cuda.Stream()
+    word = torch.zeros(1, dtype=torch.int32).pin_memory()
+
+    def publish(index, value):
+        word[0] = value
+        with torch.cuda.stream(side):
+            ctl[index:index + 1].copy_(word, non_blocking=True)
+        side.synchronize()
+
     try:
         assert lib.launch_persistent_worker(q, 8, 128, s) == 0
         tail = 0
@@ -173,23 +185,28 @@ def test_reference_task_ring_worker_c_abi(rt):
                 rt.set_alias(0, 1)
             if phase == 2:
                 rt.set_alias(0, 0)
-            torch.cuda.current_stream().synchronize()
-            host = torch.frombuffer(tasks_bytes(out, tail), dtype=torch.uint8)
-            ring[(tail % cap) * 496:(tail % cap) * 496 + ntask * 496].copy_(host)
+            host = torch.frombuffer(bytearray(tasks_bytes(out, tail)), dtype=torch.uint8).pin_memory()
+            with torch.cuda.stream(side):
+                ring[(tail % cap) * 496:(tail % cap) * 496 + ntask * 496].copy_(host, non_blocking=True)
+            side.synchronize()
             tail += ntask
-            ctl[1:2].fill_(tail)
-            torch.cuda.current_stream().synchronize()
+            publish(1, tail)
             deadline = 0
             while True:
-                pv = int(torch.frombuffer(bytes(sync[:8]), dtype=torch.int64)[0])
+                pv = int(torch.frombuffer(bytearray(bytes(sync[:8])), dtype=torch.int64)[0])
                 if pv - base >= tail or deadline > 20000:
                     break
                 time.sleep(0.0005)
                 deadline += 1
-            assert pv - base >= tail, (phase, pv, base, tail)
+            if pv - base < tail:
+                dbg = torch.cuda.Stream()
+                pc = ctypes.c_ulonglong(0)
+                lib.gpu_get_processed_count_async(ctypes.byref(pc), ctypes.c_void_p(dbg.cuda_stream))
+                dbg.synchronize()
+                raise AssertionError(f"phase {phase}: sync.processed={pv} device processed={pc.value} "
+                                     f"ring_stream_done={stream.query()}")
     finally:
-        ctl[2:3].fill_(1)  # quit
-        torch.cuda.current_stream().synchronize()
+        publish(2, 1)  # quit
         stream.synchronize()
         rt.set_alias(0, 0)
     assert mul_addr != 0
