@@ -236,6 +236,25 @@ struct alignas(128) SmemHeader {
 constexpr uint32_t kStageBytesDefault = 32768 + 128;  // two 16 KB operand halves + slack
 constexpr uint32_t kHalfBytes = 16384;                // one operand tile
 
+// ---- fixed device scratch of gpuos_ew_batch_noalloc ----------------------------------
+// One statically sized block per device holds everything a one-shot worker launch needs
+// besides the caller's operands: control words, the completion ticket, strided layouts
+// and the tile descriptors.  Offsets are bytes from the start of the block.
+constexpr size_t round_up256(size_t x) { return (x + 255) & ~size_t(255); }
+struct StaticScratch {
+  static constexpr uint64_t kMaxItems = GPUOS_NOALLOC_MAX_TILES;     // power of two
+  static constexpr uint32_t kMaxLayouts = GPUOS_NOALLOC_MAX_STRIDED;  // power of two
+  static constexpr size_t kHostCtl = 0;
+  static constexpr size_t kReport = 128;
+  static constexpr size_t kDevCtl = 256;
+  static constexpr size_t kTickets = round_up256(kDevCtl + sizeof(DevCtl));
+  static constexpr size_t kLayouts = kTickets + 256;  // tickets of batch slots 0..7
+  static constexpr size_t kItems = round_up256(kLayouts + kMaxLayouts * sizeof(Layout));
+  static constexpr size_t kBytes = kItems + kMaxItems * sizeof(WorkItem);
+};
+static_assert((StaticScratch::kMaxItems & (StaticScratch::kMaxItems - 1)) == 0, "tile capacity: power of two");
+static_assert((StaticScratch::kMaxLayouts & (StaticScratch::kMaxLayouts - 1)) == 0, "layout capacity: power of two");
+
 GPUOS_HD inline int dtype_size(int dt) {
   return dt == kF32 ? 4 : (dt == kF16 || dt == kBF16) ? 2 : dt == kF64 ? 8 : 4;
 }

@@ -1500,3 +1500,164 @@ extern "C" int gpuos_abi_sizes(int64_t* out, int n) {
   for (int i = 0; i < n && i < m; ++i) out[i] = v[i];
   return m;
 }
+
+// =========================================================================================
+// gpuos_ew_batch_noalloc: one drain-mode launch of the batch worker over a fixed scratch array
+// =========================================================================================
+// For callers that may not allocate device memory where they run.  Everything the launch needs
+// besides the caller's operands -- control words, the completion ticket, layouts and tile
+// descriptors -- is written into the library's fixed scratch array (StaticScratch) with one
+// stream-ordered copy, and the worker runs once in drain mode (it exits when the last tile
+// is done).  Device memory is never allocated; host staging buffers are per thread and reused.
+extern "C" cudaError_t gpuos_internal_noalloc_scratch(size_t smem, void** ptr, size_t* bytes);
+
+extern "C" int gpuos_ew_batch_noalloc(const GpuosEwRequest* reqs, int nreq, int flags, cudaStream_t stream) {
+  using SS = StaticScratch;
+  if (nreq < 0 || (nreq > 0 && !reqs)) return fail(GPUOS_ERR_INVALID, "null request array");
+  if (flags & ~GPUOS_FLUSH_SYNC) return fail(GPUOS_ERR_INVALID, "unsupported flags 0x%x (only GPUOS_FLUSH_SYNC)", flags);
+
+  struct Staging {
+    Plan plan;
+    HazardMap hz;
+    std::vector<WorkItem> items;
+    std::vector<Layout> layouts;
+    std::vector<unsigned char> image;
+  };
+  static thread_local Staging h;
+  h.items.clear();
+  h.layouts.clear();
+  h.hz.clear();
+  uint64_t seg_wait = 0;
+  for (int i = 0; i < nreq; ++i) {
+    const GpuosEwRequest& q = reqs[i];
+    if (!q.a || !q.out) return fail(GPUOS_ERR_INVALID, "request %d: null operand", i);
+    EwReq r;
+    r.op = q.op;
+    r.a = q.a;
+    r.b = q.b_is_scalar ? nullptr : q.b;
+    r.b_imm = q.b_is_scalar != 0;
+    r.b_val = (float)q.b_scalar;
+    r.out = q.out;
+    for (int k = 0; k < 4; ++k) r.params[k] = k < q.nparams ? q.params[k] : 0.f;
+    int e = plan_ew(r, kHalfBytes, &h.plan);
+    if (e) return fail(e, "request %d: %s", i, gpuos_rt_last_error());
+    const Plan& p = h.plan;
+    if (h.items.size() + p.items.size() > SS::kMaxItems)
+      return fail(GPUOS_ERR_INVALID,
+                  "batch needs more than %llu tiles (request %d brings the total to %llu); "
+                  "gpuos_ew_batch_noalloc takes at most GPUOS_NOALLOC_MAX_TILES = %llu",
+                  (unsigned long long)SS::kMaxItems, i, (unsigned long long)(h.items.size() + p.items.size()),
+                  (unsigned long long)SS::kMaxItems);
+    if (p.has_layout && h.layouts.size() + 1 > SS::kMaxLayouts)
+      return fail(GPUOS_ERR_INVALID,
+                  "batch has more than %u strided or broadcast requests; gpuos_ew_batch_noalloc takes at most "
+                  "GPUOS_NOALLOC_MAX_STRIDED = %u",
+                  SS::kMaxLayouts, SS::kMaxLayouts);
+    // requests that touch memory an earlier request of this call writes (or writes memory it
+    // reads) start a new segment: its tiles wait until every earlier tile has completed
+    bool hazard = false;
+    for (int k = 0; k < p.nreads && !hazard; ++k) hazard = h.hz.conflicts(p.reads[k], false);
+    if (!hazard) hazard = h.hz.conflicts(p.write, true);
+    if (hazard) {
+      h.hz.clear();
+      seg_wait = h.items.size();
+    }
+    for (int k = 0; k < p.nreads; ++k) h.hz.insert(p.reads[k], false);
+    h.hz.insert(p.write, true);
+    const uint32_t layout_idx = (uint32_t)h.layouts.size();
+    if (p.has_layout) h.layouts.push_back(p.layout);
+    for (const WorkItem& src : p.items) {
+      WorkItem it = src;
+      it.wait_items = seg_wait;
+      if (p.has_layout) it.aux = layout_idx;
+      h.items.push_back(it);
+    }
+  }
+  const uint64_t n = h.items.size();
+  if (n == 0) {
+    if (flags & GPUOS_FLUSH_SYNC) CK(cudaStreamSynchronize(stream));
+    return GPUOS_OK;
+  }
+
+  int dev = 0, sm_count = 0, smem_optin = 0;
+  CK(cudaGetDevice(&dev));
+  CK(cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev));
+  CK(cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+  // same stage rule as gpuos_rt_init, so both entry points set the same shared-memory limit
+  const int want = std::max(2, std::min(kMaxStages, env_int("GPUOS_STAGES", 4)));
+  uint32_t stages = 2;
+  while ((int)stages * 2 <= want) stages *= 2;
+  size_t smem = gpuos_internal_smem_header_bytes() + (size_t)stages * kStageBytesDefault;
+  while (smem > (size_t)smem_optin && stages > 2) {
+    stages /= 2;
+    smem = gpuos_internal_smem_header_bytes() + (size_t)stages * kStageBytesDefault;
+  }
+  void* scratch = nullptr;
+  size_t scratch_bytes = 0;
+  CK(gpuos_internal_noalloc_scratch(smem, &scratch, &scratch_bytes));
+  void *op_table = nullptr, *op_alias = nullptr;
+  CK(gpuos_internal_table_ptrs(&op_table, &op_alias));
+
+  // host image of the scratch block up to the last tile descriptor; all of it is rewritten
+  // by every call, so nothing of an earlier call survives into this one
+  const uint64_t seq = 1;
+  const uint16_t slot = (uint16_t)(seq % kNumBatchSlots);
+  const size_t image_bytes = SS::kItems + n * sizeof(WorkItem);
+  h.image.assign(image_bytes, 0);
+  unsigned char* img = h.image.data();
+  HostCtl* hc = reinterpret_cast<HostCtl*>(img + SS::kHostCtl);
+  hc->tail = n;
+  hc->quit_epoch = 1;  // drain mode: the launch of epoch 1 exits once every tile is done
+  hc->safety_idle_ns = (uint64_t)env_int("GPUOS_SAFETY_IDLE_MS", 10000) * 1000000ull;
+  hc->spin_ns = (uint32_t)env_int("GPUOS_SPIN_NS", 32);
+  hc->wait_limit_ns = (uint64_t)env_int("GPUOS_DEVICE_WAIT_MS", 5000) * 1000000ull;
+  DevCtl* dc_img = reinterpret_cast<DevCtl*>(img + SS::kDevCtl);
+  std::memset(dc_img->batch_t0, 0xff, sizeof(dc_img->batch_t0));
+  if (!h.layouts.empty())
+    std::memcpy(img + SS::kLayouts, h.layouts.data(), h.layouts.size() * sizeof(Layout));
+  WorkItem* items = reinterpret_cast<WorkItem*>(img + SS::kItems);
+  for (uint64_t i = 0; i < n; ++i) {
+    WorkItem it = h.items[i];
+    it.batch = slot;
+    it.batch_items = (uint32_t)n;
+    it.batch_seq = seq;
+    items[i] = it;
+  }
+  unsigned char* base = static_cast<unsigned char*>(scratch);
+  CK(cudaMemcpyAsync(base, img, image_bytes, cudaMemcpyHostToDevice, stream));
+
+  WorkerParams P;
+  std::memset(&P, 0, sizeof(P));
+  P.hc = reinterpret_cast<HostCtl*>(base + SS::kHostCtl);
+  P.rep = reinterpret_cast<DevReport*>(base + SS::kReport);
+  P.tickets = reinterpret_cast<Ticket*>(base + SS::kTickets);
+  P.items = reinterpret_cast<const WorkItem*>(base + SS::kItems);
+  P.tasks = nullptr;  // element-wise requests produce no Task items
+  P.layouts = reinterpret_cast<const Layout*>(base + SS::kLayouts);
+  P.dc = reinterpret_cast<DevCtl*>(base + SS::kDevCtl);
+  P.op_table = reinterpret_cast<OpFn*>(op_table);
+  P.op_alias = reinterpret_cast<int*>(op_alias);
+  P.item_mask = SS::kMaxItems - 1;
+  P.task_mask = 0;
+  P.layout_mask = SS::kMaxLayouts - 1;
+  P.epoch = 1;
+  P.stages = stages;
+  P.stage_bytes = kStageBytesDefault;
+  P.compute_threads = 256;
+  CK(gpuos_internal_launch_batch_worker(&P, sm_count, 256 + 64, smem, stream));
+  if (!(flags & GPUOS_FLUSH_SYNC)) return GPUOS_OK;
+
+  DevReport rep;
+  Ticket tk;
+  CK(cudaMemcpyAsync(&rep, base + SS::kReport, sizeof(rep), cudaMemcpyDeviceToHost, stream));
+  CK(cudaMemcpyAsync(&tk, base + SS::kTickets + slot * sizeof(Ticket), sizeof(tk), cudaMemcpyDeviceToHost, stream));
+  CK(cudaStreamSynchronize(stream));
+  if (rep.error != 0)
+    return fail(GPUOS_ERR_DEVICE, "worker error code %llu detail %llu at tile %llu",
+                (unsigned long long)(rep.error >> 32), (unsigned long long)(rep.error & 0xffffffffull),
+                (unsigned long long)rep.error_item);
+  if (rep.items_done != n || tk.seq != seq)
+    return fail(GPUOS_ERR_DEVICE, "worker exited after %llu of %llu tiles", (unsigned long long)rep.items_done,
+                (unsigned long long)n);
+  return GPUOS_OK;
+}

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdio.h>
 
+#include <mutex>
+
 #include "internal.h"
 #include "device/ptx.cuh"
 #include "device/ops.cuh"
@@ -266,3 +268,41 @@ extern "C" cudaError_t gpuos_internal_table_ptrs(void** table, void** alias) {
 }
 
 extern "C" size_t gpuos_internal_smem_header_bytes() { return (sizeof(SmemHeader) + 127) & ~size_t(127); }
+
+// ---- fixed scratch of the no-allocation entry point ------------------------------------------
+// gpuos_ew_batch_noalloc serves callers that may not allocate device memory, so the control
+// words, ticket, layouts and tile descriptors of its one-shot worker launch live in this array,
+// which every device that loads the library holds until the process exits.  In host code the
+// name stands in for the array only; its device address comes from cudaGetSymbolAddress.
+static_assert(StaticScratch::kBytes == 1113856, "the documented scratch size has changed");
+static __device__ __align__(256) unsigned char g_noalloc_scratch[StaticScratch::kBytes];
+
+namespace {
+constexpr int kMaxScratchDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[kMaxScratchDevices];
+}  // namespace
+
+// Device address of the scratch array on the current device.  The first call on a device
+// resolves the address, loads this library's kernels and sets the worker's shared-memory
+// limit to `smem`; later calls return the cached address.
+extern "C" cudaError_t gpuos_internal_noalloc_scratch(size_t smem, void** ptr, size_t* bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxScratchDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    e = gpuos_internal_preload_kernels();
+    if (e != cudaSuccess) return e;
+    e = gpuos_internal_set_worker_smem(smem);
+    if (e != cudaSuccess) return e;
+    g_scratch_ptr[dev] = p;
+  }
+  *ptr = g_scratch_ptr[dev];
+  *bytes = StaticScratch::kBytes;
+  return cudaSuccess;
+}

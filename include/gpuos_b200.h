@@ -292,6 +292,50 @@ int gpuos_plan_reduce(int red_op, const GpuosOperand* x, const GpuosOperand* out
                       int naxes, int keepdim, void* items_out, int max_items, void* layout_out,
                       int* n_items);
 
+/* ---- element-wise batch without device allocation ----------------------------------------
+ * No counterpart in the reference: the reference allocates its queue and control state with
+ * cudaMalloc/cudaHostAlloc at init.  Some callers may not allocate device memory where they
+ * run: an execute hook inside a host engine that owns every byte of device memory and forbids
+ * allocation while it executes, or a latency-critical path that cannot afford cudaMalloc's
+ * implicit device synchronisation.  gpuos_ew_batch_noalloc runs the same worker kernel as
+ * gpuos_rt_submit_ew + gpuos_rt_flush, once, on `stream`, over `nreq` element-wise requests,
+ * with all of its scratch (control words, completion ticket, tile descriptors, strided
+ * layouts) in one fixed array of device memory that is part of this library: 1,113,856 bytes
+ * (1.06 MiB) per device, held by every device that loads the library until the process exits.  It calls
+ * no cudaMalloc, cudaFree or other allocating routine.
+ *
+ * Limits: the requests together may be split into at most GPUOS_NOALLOC_MAX_TILES tiles
+ * (16 KiB of one operand each: 4096 float32 or 8192 16-bit elements), of which at most
+ * GPUOS_NOALLOC_MAX_STRIDED requests may need the strided/broadcast path; larger batches are
+ * rejected with GPUOS_ERR_INVALID before anything runs.
+ *
+ * The work runs on the current device, in stream order on `stream`: requests see earlier
+ * work on `stream`, later work on `stream` sees their results, and requests of one call that
+ * overlap in memory run in submission order.  Without GPUOS_FLUSH_SYNC the call returns once
+ * the work is enqueued; with it, the call waits for `stream` and reports a device-side error
+ * (GPUOS_ERR_DEVICE).  Every call shares the one scratch array and resets it: calls that
+ * overlap on the GPU (issued on different streams, or from different threads) race and
+ * corrupt each other.  The first call on a device resolves the array's address and sets up
+ * the kernel; make that first call before any stream capture is begun.  The persistent
+ * worker of gpuos_rt_init, while running on the same device, holds the SMs this launch needs,
+ * so the launch starts once that worker has gone idle (GPUOS_IDLE_QUIESCE_MS). */
+#define GPUOS_NOALLOC_MAX_TILES 16384
+#define GPUOS_NOALLOC_MAX_STRIDED 64
+
+typedef struct GpuosEwRequest {
+  int op;                  /* GpuosEwOp */
+  int b_is_scalar;         /* nonzero: b is ignored and b_scalar is the second operand */
+  int nparams;             /* entries of params in use (0..4) */
+  int _pad;
+  double b_scalar;
+  const GpuosOperand* a;   /* as gpuos_rt_submit_ew */
+  const GpuosOperand* b;   /* may be NULL for unary ops */
+  const GpuosOperand* out;
+  float params[4];
+} GpuosEwRequest;
+
+int gpuos_ew_batch_noalloc(const GpuosEwRequest* reqs, int nreq, int flags, cudaStream_t stream);
+
 /* Last error message of this thread (never NULL). */
 const char* gpuos_rt_last_error(void);
 
