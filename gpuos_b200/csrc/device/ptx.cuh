@@ -110,6 +110,20 @@ __device__ __forceinline__ void st_relaxed_sys(volatile uint64_t* p, uint64_t v)
   asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
+// 16-byte weak load that bypasses L1 (ld.global.cg).  Used for descriptors in mapped host
+// memory: they are read only after an acquire of the published tail (directly, or through
+// the leader's release of its device mirror), which orders the host's writes of those
+// descriptors before the load; L1, the one cache that is not coherent, is bypassed.  Unlike
+// strong system-scope loads, these do not queue behind each other across the grid.
+__device__ __forceinline__ uint4 ld_cg_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p)
+               : "memory");
+  return r;
+}
+
 // 16-byte load that always observes the coherent (host-written) value.
 __device__ __forceinline__ uint4 ld_volatile_v4(const void* p) {
   uint4 r;

@@ -49,6 +49,11 @@ __device__ __forceinline__ void report_error(const WorkerParams& P, uint32_t cod
   }
 }
 
+// First occurrence of a launch event (see TimelineSlot); callers mark each event once.
+__device__ __forceinline__ void tl_mark(const WorkerParams& P, int slot) {
+  if (gridDim.x < kDiagCtas) atomicMin(&P.dc->diag[gridDim.x][slot], (unsigned long long)ptx::now_ns());
+}
+
 // Table lookup at dequeue time (persistent_kernel.cu:184-193).
 __device__ __forceinline__ OpFn resolve_op(const WorkerParams& P, int op) {
   if (op < 0 || op >= GPUOS_MAX_OPS) return nullptr;
@@ -77,7 +82,11 @@ constexpr uint32_t kAccountEvery = 8;  // items per fence when completions strea
 // One gpu-scope fence covers every item of the runs (their compute warps' stores were
 // ordered before the completer by the per-stage done barriers); then the per-flush
 // counters; the last item of a flush writes the flush's ticket into mapped memory.
-__device__ void account(const WorkerParams& P, const DoneRun* runs, int nruns) {
+__device__ void account(const WorkerParams& P, const DoneRun* runs, int nruns, bool* first) {
+  if (*first) {
+    tl_mark(P, TL_ACCOUNT);
+    *first = false;
+  }
   ptx::fence_acq_rel_gpu();
   unsigned long long total = 0;
   for (int r = 0; r < nruns; ++r) {
@@ -113,7 +122,7 @@ __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, const 
 }
 
 // ---- compute warps ----------------------------------------------------------------------
-__device__ void compute_loop(const WorkerParams& P, const WorkerShared& W, uint32_t ctid, uint32_t nct) {
+__device__ __forceinline__ void compute_loop(const WorkerParams& P, const WorkerShared& W, uint32_t ctid, uint32_t nct) {
   SmemHeader& H = *W.H;
   const uint32_t S = P.stages;
   unsigned long long dg[4] = {0, 0, 0, 0};
@@ -128,7 +137,6 @@ __device__ void compute_loop(const WorkerParams& P, const WorkerShared& W, uint3
         unsigned long long* row = P.dc->diag[blockIdx.x];
         row[DG_C_WAIT_FULL] = dg[0];
         row[DG_C_TILE] = dg[1];
-        row[DG_C_ITEMS] = *n;
       }
     }
   } flush_diag{P, ctid, dg, &n_items};
@@ -160,7 +168,9 @@ __device__ void compute_loop(const WorkerParams& P, const WorkerShared& W, uint3
       ctx.nt = nct;
       const uint32_t fi = (kind == IK_EW_CONTIG || kind == IK_EW_GENERIC) ? m.item.op : GPUOS_EW_NUM_OPS;
       TileFn fn = g_tile_fns[fi];
+      if (iter == 0 && ctid == 0) tl_mark(P, TL_TILE0);
       fn(ctx);
+      if (iter == 0 && ctid == 0) tl_mark(P, TL_TILE1);
     }
     // this warp is done with the stage; no CTA-wide barrier between tiles
     __syncwarp();
@@ -177,12 +187,13 @@ __device__ void compute_loop(const WorkerParams& P, const WorkerShared& W, uint3
 // stage back to the dequeue warp and batches the completion accounting of several items
 // behind one fence.  Before it would block it publishes what it has, so a lone item is
 // accounted immediately.
-__device__ void completer_loop(const WorkerParams& P, const WorkerShared& W, uint32_t lane) {
+__device__ __forceinline__ void completer_loop(const WorkerParams& P, const WorkerShared& W, uint32_t lane) {
   SmemHeader& H = *W.H;
   const uint32_t S = P.stages;
   const uint32_t shift = __ffs(S) - 1;
   DoneRun runs[kMaxRuns];
   int nruns = 0;
+  bool first_account = true;
   uint32_t pending = 0;
   unsigned long long t_wait = 0, t_acc = 0, n_items = 0;
   for (uint64_t iter = 0;; ++iter) {
@@ -195,7 +206,7 @@ __device__ void completer_loop(const WorkerParams& P, const WorkerShared& W, uin
       const uint32_t full = ptx::smem_addr(&H.full[s]);
       if (nruns && !ptx::mbar_test_wait(full, parity)) {
         unsigned long long a0 = clock64();
-        account(P, runs, nruns);
+        account(P, runs, nruns, &first_account);
         t_acc += clock64() - a0;
         nruns = 0;
         pending = 0;
@@ -224,7 +235,7 @@ __device__ void completer_loop(const WorkerParams& P, const WorkerShared& W, uin
       unsigned long long c0 = clock64();
       const uint32_t done = ptx::smem_addr(&H.done[s]);
       if (nruns && !ptx::mbar_test_wait(done, parity)) {
-        account(P, runs, nruns);
+        account(P, runs, nruns, &first_account);
         nruns = 0;
         pending = 0;
       }
@@ -243,7 +254,7 @@ __device__ void completer_loop(const WorkerParams& P, const WorkerShared& W, uin
         ++pending;
         ++n_items;
         if (pending >= kAccountEvery || nruns == kMaxRuns) {
-          account(P, runs, nruns);
+          account(P, runs, nruns, &first_account);
           nruns = 0;
           pending = 0;
         }
@@ -253,7 +264,7 @@ __device__ void completer_loop(const WorkerParams& P, const WorkerShared& W, uin
     __syncwarp();
   }
   if (lane == 0) {
-    if (nruns) account(P, runs, nruns);
+    if (nruns) account(P, runs, nruns, &first_account);
     if (blockIdx.x < kDiagCtas) {
       P.dc->diag[blockIdx.x][DG_C_BAR] = t_wait;
       P.dc->diag[blockIdx.x][DG_C_COMPLETE] = t_acc;
@@ -262,13 +273,16 @@ __device__ void completer_loop(const WorkerParams& P, const WorkerShared& W, uin
 }
 
 // ---- dequeue warp -------------------------------------------------------------------------
-constexpr uint32_t kChunk = 4;  // tickets claimed per atomic when work is plentiful
+constexpr uint32_t kChunk = 8;  // tickets claimed per atomic when work is plentiful (dcache size)
 
 struct ProdState {
   uint64_t iter;        // items staged so far
   uint64_t ticket;      // lowest unprocessed ticket held
   uint64_t chunk_end;   // tickets [ticket, chunk_end) are claimed by this CTA
   uint64_t desc_end;    // descriptors of tickets < desc_end are in the shared cache
+  uint64_t n_ticket;    // chunk claimed ahead: tickets [n_ticket, n_end) (empty if equal)
+  uint64_t n_end;
+  uint32_t n_fetched;   // its descriptors are being loaded into the warp's registers
   uint32_t last_seq;    // flush of the last staged item (start stamp once per flush)
   uint64_t tail_cache;
   uint64_t items_done_cache;
@@ -283,8 +297,9 @@ struct ProdState {
   // leader: diagnostics
   uint64_t read_sum, read_n, read_max;
   uint64_t rounds, timeouts, work_resumes, parked_seen;
-  unsigned long long dg[6];
+  unsigned long long dg[7];  // DG_P_WAIT_EMPTY .. DG_P_ITEMS, then kDgTma
 };
+constexpr int kDgTma = 6;  // producer counter stored in slot DG_P_TMA
 
 __device__ __forceinline__ void publish_diag(const WorkerParams& P, const ProdState& st) {
   ptx::st_relaxed_sys(&P.rep->heartbeat, st.polls);
@@ -299,7 +314,7 @@ __device__ __forceinline__ void publish_diag(const WorkerParams& P, const ProdSt
 }
 
 // Wait (lane 0) until compute warps released stage use `use` (i.e. iteration use-1 done).
-__device__ bool wait_empty(const WorkerParams& P, SmemHeader& H, uint64_t iter, uint32_t S) {
+__device__ __forceinline__ bool wait_empty(const WorkerParams& P, SmemHeader& H, uint64_t iter, uint32_t S) {
   if (iter < S) return true;
   const uint32_t s = (uint32_t)iter & (S - 1);
   const uint32_t parity = (uint32_t)(((iter >> (__ffs(S) - 1)) - 1) & 1);
@@ -310,7 +325,7 @@ __device__ bool wait_empty(const WorkerParams& P, SmemHeader& H, uint64_t iter, 
     if ((++spins & 255u) == 0) {
       const uint64_t t = ptx::now_ns();
       *reinterpret_cast<volatile unsigned long long*>(&H.prod_alive) = t;
-      if (t - t0 > P.hc->wait_limit_ns) {
+      if (t - t0 > H.wait_limit_ns) {
         report_error(P, DE_WAIT_EMPTY, iter);
         return false;
       }
@@ -320,7 +335,7 @@ __device__ bool wait_empty(const WorkerParams& P, SmemHeader& H, uint64_t iter, 
 }
 
 // Wait (lane 0) until all `iter` staged items have been released by the compute warps.
-__device__ bool drain_own(const WorkerParams& P, SmemHeader& H, uint64_t iter, uint32_t S) {
+__device__ __forceinline__ bool drain_own(const WorkerParams& P, SmemHeader& H, uint64_t iter, uint32_t S) {
   const uint64_t lo = iter > S ? iter - S : 0;
   for (uint64_t u = lo; u < iter; ++u) {
     // use u was released when the empty barrier of its stage completed phase (u / S)
@@ -330,7 +345,7 @@ __device__ bool drain_own(const WorkerParams& P, SmemHeader& H, uint64_t iter, u
     const uint64_t t0 = ptx::now_ns();
     uint32_t spins = 0;
     while (!ptx::mbar_try_wait(bar, parity)) {
-      if ((++spins & 255u) == 0 && ptx::now_ns() - t0 > P.hc->wait_limit_ns) {
+      if ((++spins & 255u) == 0 && ptx::now_ns() - t0 > H.wait_limit_ns) {
         report_error(P, DE_WAIT_EMPTY, u);
         return false;
       }
@@ -353,7 +368,7 @@ __device__ __forceinline__ void park_count(DevCtl* dc, uint64_t round) {
 
 // Park protocol (lane 0 of a dequeue warp that is idle and holds an unpublished ticket).
 // Returns PV_RESUME or PV_EXIT.
-__device__ int park(const WorkerParams& P, SmemHeader& H, ProdState& st, uint64_t round, uint32_t S) {
+__device__ __forceinline__ int park(const WorkerParams& P, SmemHeader& H, ProdState& st, uint64_t round, uint32_t S) {
   DevCtl* dc = P.dc;
   st.seen_round = round;
   const bool leader = blockIdx.x == 0;
@@ -392,6 +407,7 @@ __device__ int park(const WorkerParams& P, SmemHeader& H, ProdState& st, uint64_
       }
       ptx::nanosleep(128);
     }
+    if (st.rounds == 1) tl_mark(P, TL_GATHER);
     const bool aborted = *reinterpret_cast<volatile unsigned int*>(&dc->abort) != 0;
     if (!gathered && !aborted) {
       ptx::st_release_gpu(&dc->tail_mirror, ptx::ld_acquire_sys(&P.hc->tail));
@@ -413,6 +429,7 @@ __device__ int park(const WorkerParams& P, SmemHeader& H, ProdState& st, uint64_
     }
     dc->exit_tail = pm;
     publish_diag(P, st);
+    tl_mark(P, TL_VERDICT);
     ptx::st_release_gpu(&dc->verdict, (round << 2) | PV_EXIT);
     return PV_EXIT;
   }
@@ -425,7 +442,7 @@ __device__ int park(const WorkerParams& P, SmemHeader& H, ProdState& st, uint64_
     if ((++spins & 63u) == 0) {
       const uint64_t now = ptx::now_ns();
       *reinterpret_cast<volatile unsigned long long*>(&H.prod_alive) = now;
-      if (now - t0 > P.hc->wait_limit_ns) {
+      if (now - t0 > H.wait_limit_ns) {
         report_error(P, DE_WAIT_PARK, st.ticket);
         return PV_EXIT;
       }
@@ -437,7 +454,7 @@ __device__ int park(const WorkerParams& P, SmemHeader& H, ProdState& st, uint64_
 // Copy `bytes` (multiple of 16) from mapped/global memory into shared memory with the warp.
 __device__ __forceinline__ void warp_copy16(void* dst, const void* src, uint32_t bytes, uint32_t lane) {
   for (uint32_t off = lane * 16; off < bytes; off += 32 * 16) {
-    const uint4 v = ptx::ld_volatile_v4(reinterpret_cast<const unsigned char*>(src) + off);
+    const uint4 v = ptx::ld_cg_v4(reinterpret_cast<const unsigned char*>(src) + off);
     *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(dst) + off) = v;
   }
 }
@@ -450,11 +467,12 @@ __device__ __forceinline__ void arm_exit(SmemHeader& H, uint32_t s) {
 
 // Stage one item (whole dequeue warp; stage `st.iter % S` is free).  On an error the
 // stage is armed as the exit sentinel and false is returned.
-__device__ bool stage_item(const WorkerParams& P, const WorkerShared& W, ProdState& st, uint32_t lane) {
+__device__ __forceinline__ bool stage_item(const WorkerParams& P, const WorkerShared& W, ProdState& st, uint32_t lane) {
   SmemHeader& H = *W.H;
   const uint32_t S = P.stages;
   const uint32_t s = (uint32_t)st.iter & (S - 1);
   StageMeta& m = H.meta[s];
+  if (lane == 0 && st.iter == 0) tl_mark(P, TL_STAGE);
   if (lane < 4) {
     const uint4* src = reinterpret_cast<const uint4*>(&H.dcache[st.ticket & 7]);
     reinterpret_cast<uint4*>(&m.item)[lane] = src[lane];
@@ -479,7 +497,7 @@ __device__ bool stage_item(const WorkerParams& P, const WorkerShared& W, ProdSta
         if ((++spins & 63u) == 0) {
           const uint64_t now = ptx::now_ns();
           *reinterpret_cast<volatile unsigned long long*>(&H.prod_alive) = now;
-          if (now - t0 > P.hc->wait_limit_ns) {
+          if (now - t0 > H.wait_limit_ns) {
             report_error(P, DE_WAIT_BARRIER, st.ticket);
             ok = 0;
             break;
@@ -506,6 +524,7 @@ __device__ bool stage_item(const WorkerParams& P, const WorkerShared& W, ProdSta
   }
   __syncwarp();
   if (lane == 0) {
+    const unsigned long long c_tma = clock64();
     const uint32_t full = ptx::smem_addr(&H.full[s]);
     unsigned char* buf = stage_buf(W, s);
     if (it.kind == IK_EW_CONTIG) {
@@ -567,6 +586,8 @@ __device__ bool stage_item(const WorkerParams& P, const WorkerShared& W, ProdSta
     } else {
       ptx::mbar_arrive(full);
     }
+    st.dg[kDgTma] += clock64() - c_tma;
+    if (st.iter == 0) tl_mark(P, TL_TMA);
   }
   ok = __shfl_sync(0xffffffffu, ok, 0);
   if (!ok) return false;
@@ -580,7 +601,7 @@ __device__ bool stage_item(const WorkerParams& P, const WorkerShared& W, ProdSta
   return true;
 }
 
-__device__ void push_exit(const WorkerParams& P, SmemHeader& H, ProdState& st, uint32_t lane) {
+__device__ __forceinline__ void push_exit(const WorkerParams& P, SmemHeader& H, ProdState& st, uint32_t lane) {
   const uint32_t S = P.stages;
   if (lane == 0) {
     wait_empty(P, H, st.iter, S);
@@ -589,7 +610,7 @@ __device__ void push_exit(const WorkerParams& P, SmemHeader& H, ProdState& st, u
   __syncwarp();
 }
 
-__device__ void producer_loop(const WorkerParams& P, const WorkerShared& W, uint32_t lane) {
+__device__ __forceinline__ void producer_loop(const WorkerParams& P, const WorkerShared& W, uint32_t lane) {
   SmemHeader& H = *W.H;
   DevCtl* dc = P.dc;
   const uint32_t S = P.stages;
@@ -604,16 +625,16 @@ __device__ void producer_loop(const WorkerParams& P, const WorkerShared& W, uint
   st.items_done_cache = 0;
   st.seen_round = 0;
   st.round = 0;
-  st.beat_val = P.hc->host_beat;
+  st.beat_val = leader ? P.hc->host_beat : 0;
   st.beat_t = ptx::now_ns();
   st.polls = 0;
-  st.quit_epoch = P.hc->quit_epoch;
-  st.yield_every = P.hc->yield_every;
-  st.safety_ns = P.hc->safety_idle_ns;
-  st.spin_ns = P.hc->spin_ns;
+  st.quit_epoch = ptx::ld_acquire_gpu(&dc->p_quit_epoch);
+  st.yield_every = ptx::ld_acquire_gpu(&dc->p_yield_every);
+  st.safety_ns = ptx::ld_acquire_gpu(&dc->p_safety_idle_ns);
+  st.spin_ns = (uint32_t)ptx::ld_acquire_gpu(&dc->p_spin_ns);
   st.read_sum = st.read_n = st.read_max = 0;
   st.rounds = st.timeouts = st.work_resumes = st.parked_seen = 0;
-  for (int k = 0; k < 6; ++k) st.dg[k] = 0;
+  for (int k = 0; k < 7; ++k) st.dg[k] = 0;
   struct Flush {
     const WorkerParams& P;
     uint32_t lane;
@@ -622,12 +643,22 @@ __device__ void producer_loop(const WorkerParams& P, const WorkerShared& W, uint
       if (lane == 0 && blockIdx.x < kDiagCtas) {
         unsigned long long* row = P.dc->diag[blockIdx.x];
         for (int k = 0; k < 6; ++k) row[k] = st.dg[k];
+        row[DG_P_TMA] = st.dg[kDgTma];
       }
     }
   } flush_diag{P, lane, st};
 
+  st.n_ticket = st.n_end = 0;
+  st.n_fetched = 0;
+  // Descriptors of the chunk claimed ahead, 16 bytes per lane (4 lanes per descriptor).  The
+  // loads are issued when the chunk is claimed and land in shared memory only when the chunk
+  // becomes current, so their latency (a read of mapped host memory) overlaps the staging of
+  // the current chunk.
+  uint4 pf = make_uint4(0, 0, 0, 0);
+
   while (true) {
     int action = 0;  // 0: stage ticket, 1: exit
+    uint32_t switched = 0, issue = 0;
     if (lane == 0) {
       unsigned long long c0 = clock64();
       const bool empty_ok = wait_empty(P, H, st.iter, S);
@@ -636,14 +667,37 @@ __device__ void producer_loop(const WorkerParams& P, const WorkerShared& W, uint
       if (!empty_ok) {
         action = 1;
       } else if (st.ticket == st.chunk_end) {
-        // Claim a chunk: several tickets per atomic while plenty of published work lies
-        // ahead, single tickets near the end of the published work (load balance).
+        if (st.n_end > st.n_ticket) {
+          // move on to the chunk claimed ahead
+          st.ticket = st.n_ticket;
+          st.chunk_end = st.n_end;
+          st.desc_end = st.n_fetched ? st.n_end : st.n_ticket;
+          switched = st.n_fetched;
+          st.n_ticket = st.n_end = 0;
+          st.n_fetched = 0;
+        } else {
+          // Claim a chunk: several tickets per atomic while plenty of published work lies
+          // ahead, single tickets near the end of the published work (load balance).
+          const uint64_t ahead = st.tail_cache > st.chunk_end ? st.tail_cache - st.chunk_end : 0;
+          uint64_t k = ahead / (2ull * gridDim.x);
+          k = k < 1 ? 1 : (k > kChunk ? kChunk : k);
+          if (st.iter == 0 && st.chunk_end == 0) tl_mark(P, TL_CLAIM);
+          st.ticket = atomicAdd(&dc->head, k);
+          st.chunk_end = st.ticket + k;
+          st.desc_end = st.ticket;
+        }
+        // Claim the next chunk now while at least two tickets per CTA of published work lie
+        // beyond this one; its descriptors are loaded while this chunk is staged.  A CTA
+        // that goes idle never holds a chunk ahead (this chunk would have to be published).
         const uint64_t ahead = st.tail_cache > st.chunk_end ? st.tail_cache - st.chunk_end : 0;
-        uint64_t k = ahead / (2ull * gridDim.x);
-        k = k < 1 ? 1 : (k > kChunk ? kChunk : k);
-        st.ticket = atomicAdd(&dc->head, k);
-        st.chunk_end = st.ticket + k;
-        st.desc_end = st.ticket;
+        if (st.chunk_end <= st.tail_cache && ahead >= 2ull * gridDim.x) {
+          uint64_t k = ahead / (2ull * gridDim.x);
+          k = k > kChunk ? kChunk : k;
+          st.n_ticket = atomicAdd(&dc->head, k);
+          st.n_end = st.n_ticket + k;
+          st.n_fetched = st.n_end <= st.tail_cache;
+          issue = st.n_fetched;
+        }
         c0 = clock64();
         st.dg[DG_P_CLAIM] += c0 - c1;
         c1 = c0;
@@ -692,6 +746,7 @@ __device__ void producer_loop(const WorkerParams& P, const WorkerShared& W, uint
           if (now - st.beat_t > st.safety_ns) want_exit = true;
           if (want_exit) {
             st.round = (st.round > st.seen_round ? st.round : st.seen_round) + 1;
+            if (st.rounds == 0) tl_mark(P, TL_ROUND);
             ++st.rounds;
             dc->park_min = ~0ull;
             atomicExch(&dc->park_word, (unsigned long long)st.round << 32);
@@ -718,11 +773,28 @@ __device__ void producer_loop(const WorkerParams& P, const WorkerShared& W, uint
       push_exit(P, H, st, lane);
       return;
     }
+    __syncwarp();  // orders lane 0's acquire of the tail before the other lanes' descriptor loads
     st.ticket = __shfl_sync(0xffffffffu, st.ticket, 0);
     st.chunk_end = __shfl_sync(0xffffffffu, st.chunk_end, 0);
     st.desc_end = __shfl_sync(0xffffffffu, st.desc_end, 0);
     st.tail_cache = __shfl_sync(0xffffffffu, st.tail_cache, 0);
+    switched = __shfl_sync(0xffffffffu, switched, 0);
+    issue = __shfl_sync(0xffffffffu, issue, 0);
     unsigned long long cd = clock64();
+    if (switched) {
+      // the chunk claimed ahead is current: its descriptors go to the shared cache
+      if (lane < 4 * (uint32_t)(st.chunk_end - st.ticket))
+        reinterpret_cast<uint4*>(&H.dcache[(st.ticket + (lane >> 2)) & 7])[lane & 3] = pf;
+      __syncwarp();
+    }
+    if (issue) {
+      st.n_ticket = __shfl_sync(0xffffffffu, st.n_ticket, 0);
+      st.n_end = __shfl_sync(0xffffffffu, st.n_end, 0);
+      if (lane < 4 * (uint32_t)(st.n_end - st.n_ticket)) {
+        const uint64_t t = st.n_ticket + (lane >> 2);
+        pf = ptx::ld_cg_v4(reinterpret_cast<const unsigned char*>(P.items + (t & P.item_mask)) + (lane & 3) * 16);
+      }
+    }
     if (st.ticket >= st.desc_end) {
       // one warp-wide read fetches the descriptors of every published ticket of the chunk
       const uint64_t hi = st.chunk_end < st.tail_cache ? st.chunk_end : st.tail_cache;
@@ -730,7 +802,7 @@ __device__ void producer_loop(const WorkerParams& P, const WorkerShared& W, uint
       if (lane < 4 * cnt) {
         const uint64_t t = st.ticket + (lane >> 2);
         const unsigned char* src = reinterpret_cast<const unsigned char*>(P.items + (t & P.item_mask)) + (lane & 3) * 16;
-        reinterpret_cast<uint4*>(&H.dcache[t & 7])[lane & 3] = ptx::ld_volatile_v4(src);
+        reinterpret_cast<uint4*>(&H.dcache[t & 7])[lane & 3] = ptx::ld_cg_v4(src);
       }
       __syncwarp();
       st.desc_end = hi;
@@ -763,7 +835,8 @@ __device__ void batch_worker_body(const WorkerParams& P, unsigned char* smem_raw
     }
     ptx::fence_mbar_init();
     H->prod_alive = ptx::now_ns();
-    H->full_wait_ns = P.hc->wait_limit_ns + P.hc->safety_idle_ns;
+    H->wait_limit_ns = P.wait_limit_ns;
+    H->full_wait_ns = P.wait_limit_ns;
     H->exit_flag = 0;
   }
   __syncthreads();
@@ -782,7 +855,16 @@ __device__ void batch_worker_body(const WorkerParams& P, unsigned char* smem_raw
       dc->abort = 0;
       dc->exited = 0;
       dc->yield_base = dc->items_done;
+      if (gridDim.x < kDiagCtas) {
+        for (int k = 0; k < kDiagSlots; ++k) dc->diag[gridDim.x][k] = ~0ull;
+        dc->diag[gridDim.x][TL_INIT] = ptx::now_ns();
+      }
       dc->tail_mirror = ptx::ld_acquire_sys(&P.hc->tail);
+      dc->p_wait_limit_ns = P.hc->wait_limit_ns;
+      dc->p_safety_idle_ns = P.hc->safety_idle_ns;
+      dc->p_yield_every = P.hc->yield_every;
+      dc->p_quit_epoch = P.hc->quit_epoch;
+      dc->p_spin_ns = P.hc->spin_ns;
       ptx::fence_acq_rel_gpu();
       ptx::st_release_gpu(&dc->launch_epoch, P.epoch);
       ptx::st_relaxed_sys(&P.rep->t_launch, ptx::now_ns());
@@ -792,13 +874,18 @@ __device__ void batch_worker_body(const WorkerParams& P, unsigned char* smem_raw
     } else {
       const uint64_t t0 = ptx::now_ns();
       while (ptx::ld_acquire_gpu(&dc->launch_epoch) != P.epoch) {
-        if (ptx::now_ns() - t0 > P.hc->wait_limit_ns) {
+        if (ptx::now_ns() - t0 > P.wait_limit_ns) {
           report_error(P, DE_WAIT_START, 0);
           start_ok = 0;
           break;
         }
         ptx::nanosleep(128);
       }
+    }
+    if (start_ok) {
+      const uint64_t wl = ptx::ld_acquire_gpu(&dc->p_wait_limit_ns);
+      H->wait_limit_ns = wl;
+      H->full_wait_ns = wl + ptx::ld_acquire_gpu(&dc->p_safety_idle_ns);
     }
   }
   __syncthreads();
@@ -812,9 +899,11 @@ __device__ void batch_worker_body(const WorkerParams& P, unsigned char* smem_raw
   __syncthreads();
   if (threadIdx.x == 0) {
     if (blockIdx.x < kDiagCtas) dc->diag[blockIdx.x][DG_CYCLES] = clock64() - cta_c0;
+    tl_mark(P, TL_EXIT_FIRST);
     ptx::fence_acq_rel_gpu();
     const unsigned int n = atomicAdd(&dc->exited, 1u) + 1;
     if (n == gridDim.x) {
+      if (gridDim.x < kDiagCtas) dc->diag[gridDim.x][TL_EXIT_LAST] = ptx::now_ns();
       ptx::st_relaxed_sys(&P.rep->exit_tail, dc->exit_tail);
       ptx::st_relaxed_sys(&P.rep->t_exit, ptx::now_ns());
       ptx::st_relaxed_sys(&P.rep->items_done, dc->items_done);

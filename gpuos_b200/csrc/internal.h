@@ -156,11 +156,28 @@ enum DiagSlot {
   DG_C_TILE,            // compute thread 0: tile function
   DG_C_BAR,             // compute thread 0: compute-warp barrier after the tile
   DG_C_COMPLETE,        // compute thread 0: completion accounting
-  DG_C_ITEMS,           // items computed
+  DG_P_TMA,             // dequeue warp: issuing the bulk copies of staged items
   DG_CYCLES,            // total cycles of the CTA
   kDiagSlots = 12
 };
 constexpr int kDiagCtas = 256;
+
+// Launch timeline: %globaltimer stamps of the first occurrence of each event in the last
+// worker launch, kept in diag row gridDim.x (the row after the last CTA's).
+enum TimelineSlot {
+  TL_INIT = 0,    // CTA 0 initialised the launch
+  TL_CLAIM,       // first ticket claim
+  TL_STAGE,       // first item staging began
+  TL_TMA,         // first bulk copies issued
+  TL_TILE0,       // first tile started
+  TL_TILE1,       // first tile finished
+  TL_ACCOUNT,     // first completion accounting
+  TL_ROUND,       // leader opened the first exit round
+  TL_GATHER,      // leader's first gather ended (all parked, work, or timeout)
+  TL_VERDICT,     // leader published the exit verdict
+  TL_EXIT_FIRST,  // first CTA finished
+  TL_EXIT_LAST    // last CTA finished
+};
 
 // Device-memory control block (cudaMalloc, zeroed at init).
 struct alignas(128) DevCtl {
@@ -176,7 +193,9 @@ struct alignas(128) DevCtl {
   unsigned int abort;              // a CTA hit an error: everybody exits
   unsigned int exited;             // CTAs that left the current launch
   unsigned long long yield_base;   // items_done at launch (yield accounting)
-  unsigned long long _pad[5];
+  // HostCtl words as CTA 0 read them at launch: every other CTA takes them from here, so a
+  // launch reads host memory from one thread only
+  unsigned long long p_wait_limit_ns, p_safety_idle_ns, p_yield_every, p_quit_epoch, p_spin_ns;
   unsigned int batch_done[kNumBatchSlots];
   unsigned long long batch_t0[kNumBatchSlots];
   unsigned long long diag[kDiagCtas][kDiagSlots];  // per-CTA cycle counters of the last launch
@@ -203,6 +222,7 @@ struct WorkerParams {
   uint32_t stage_bytes;   // operand buffer bytes per stage
   uint32_t compute_threads;
   uint32_t _pad;
+  uint64_t wait_limit_ns;  // bound of the launch-start wait (HostCtl::wait_limit_ns at launch)
 };
 
 // Per-stage bookkeeping in shared memory.
@@ -227,12 +247,16 @@ struct alignas(128) SmemHeader {
   unsigned long long done[kMaxStages];   // compute warps -> completer
   unsigned long long prod_alive;   // %globaltimer stamp of the dequeue warp
   unsigned long long full_wait_ns; // compute warps' bound on a silent dequeue warp
+  unsigned long long wait_limit_ns; // bound of the CTA's other waits (launch copy of HostCtl)
   unsigned int exit_flag;
   unsigned int _pad;
   StageMeta meta[kMaxStages];
   WorkItem dcache[8];              // descriptors of the claimed chunk (ticket & 7)
 };
 
+// Compute threads per worker CTA at most (plus the dequeue and completer warps): 512 threads
+// leave each thread 128 registers.
+constexpr int kMaxComputeThreads = 448;
 constexpr uint32_t kStageBytesDefault = 32768 + 128;  // two 16 KB operand halves + slack
 constexpr uint32_t kHalfBytes = 16384;                // one operand tile
 

@@ -679,6 +679,20 @@ PyObject* py_debug_counters(PyObject*, PyObject* args, PyObject* kw) {
   return rows;
 }
 
+PyObject* py_debug_timeline(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"device", nullptr};
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "|O", const_cast<char**>(kwlist), &devobj)) return nullptr;
+  gpuos_rt* rt = rt_arg(devobj, nullptr);
+  if (!rt) return nullptr;
+  std::vector<uint64_t> buf(257 * 12, ~0ull);
+  const int ctas = gpuos_rt_debug_counters(rt, buf.data(), (int)buf.size());
+  if (ctas < 0) return raise_status(-ctas);
+  PyObject* row = PyList_New(12);
+  for (int k = 0; k < 12; ++k) PyList_SET_ITEM(row, k, PyLong_FromUnsignedLongLong(buf[ctas * 12 + k]));
+  return row;
+}
+
 PyObject* py_launches(PyObject*, PyObject* args, PyObject* kw) {
   static const char* kwlist[] = {"device", nullptr};
   PyObject* devobj = Py_None;
@@ -963,6 +977,8 @@ PyMethodDef kMethods[] = {
      "raw handle of the worker kernel's stream"},
     {"launches", (PyCFunction)(void (*)(void))py_launches, METH_VARARGS | METH_KEYWORDS, "worker launches so far"},
     {"set_device_wait_ms", py_set_device_wait_ms, METH_VARARGS, "bound of the worker's in-grid waits"},
+    {"debug_timeline", (PyCFunction)(void (*)(void))py_debug_timeline, METH_VARARGS | METH_KEYWORDS,
+     "debug_timeline(device=None) -> [12 %globaltimer stamps of the last launch's first events]"},
     {"debug_counters", (PyCFunction)(void (*)(void))py_debug_counters, METH_VARARGS | METH_KEYWORDS,
      "per-CTA cycle counters of the last worker launch"},
     {"debug_inject_stall", (PyCFunction)(void (*)(void))py_debug_inject_stall, METH_VARARGS | METH_KEYWORDS,

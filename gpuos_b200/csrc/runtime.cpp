@@ -733,6 +733,7 @@ static int launch_worker_locked(gpuos_rt* rt) {
   P.stages = rt->stages;
   P.stage_bytes = rt->stage_bytes;
   P.compute_threads = (uint32_t)rt->tpb;
+  P.wait_limit_ns = rt->hc->wait_limit_ns;
   CK(cudaSetDevice(rt->device));
   // one dequeue warp + one completer warp + threads_per_block compute threads
   CK(gpuos_internal_launch_batch_worker(&P, rt->sm_count, rt->tpb + 64, rt->smem, rt->kstream));
@@ -899,8 +900,8 @@ extern "C" int gpuos_rt_init(int device, int capacity, int threads_per_block, gp
   }
   if (capacity <= 0) capacity = 4096;
   if (threads_per_block <= 0) threads_per_block = 256;
-  if (threads_per_block % 32 != 0 || threads_per_block < 64 || threads_per_block > 960)
-    return fail(GPUOS_ERR_INVALID, "threads_per_block must be a multiple of 32 in [64, 960]");
+  if (threads_per_block % 32 != 0 || threads_per_block < 64 || threads_per_block > kMaxComputeThreads)
+    return fail(GPUOS_ERR_INVALID, "threads_per_block must be a multiple of 32 in [64, %d]", kMaxComputeThreads);
   int ndev = 0;
   CK(cudaGetDeviceCount(&ndev));
   if (device < 0 || device >= ndev) return fail(GPUOS_ERR_INVALID, "device %d out of range (%d devices)", device, ndev);
@@ -1281,7 +1282,8 @@ extern "C" int gpuos_rt_set_yield_every(gpuos_rt* rt, uint64_t every) {
 extern "C" int gpuos_rt_debug_counters(gpuos_rt* rt, uint64_t* out, int n) {
   if (!rt) return -fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
   const int ctas = std::min(rt->sm_count, kDiagCtas);
-  std::vector<unsigned long long> buf((size_t)ctas * kDiagSlots);
+  const int rows = std::min(ctas + 1, kDiagCtas);  // + the launch timeline row
+  std::vector<unsigned long long> buf((size_t)rows * kDiagSlots);
   cudaError_t e = cudaSetDevice(rt->device);
   if (e == cudaSuccess)
     e = cudaMemcpyAsync(buf.data(), rt->dc->diag, buf.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost,
@@ -1297,7 +1299,9 @@ extern "C" int gpuos_rt_set_device_wait_ms(gpuos_rt* rt, int ms) {
   if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
   if (ms <= 0) return fail(GPUOS_ERR_INVALID, "device wait bound must be positive");
   rt->hc->wait_limit_ns = (uint64_t)ms * 1000000ull;
-  return GPUOS_OK;
+  // a running worker keeps the bound it was launched with: stop it so the next launch
+  // (on the next flush) takes the new one
+  return gpuos_rt_quiesce(rt, 30000);
 }
 
 // Publish one item whose dependency barrier never opens: the dequeue warp's bounded wait
@@ -1644,6 +1648,7 @@ extern "C" int gpuos_ew_batch_noalloc(const GpuosEwRequest* reqs, int nreq, int 
   P.stages = stages;
   P.stage_bytes = kStageBytesDefault;
   P.compute_threads = 256;
+  P.wait_limit_ns = hc->wait_limit_ns;
   CK(gpuos_internal_launch_batch_worker(&P, sm_count, 256 + 64, smem, stream));
   if (!(flags & GPUOS_FLUSH_SYNC)) return GPUOS_OK;
 

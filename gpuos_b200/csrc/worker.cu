@@ -58,7 +58,7 @@ __global__ void builtin_addr_kernel(int which, unsigned long long* out) {
   else *out = 0ull;
 }
 
-extern "C" __global__ void __launch_bounds__(1024, 1) gpuos_batch_worker(WorkerParams P) {
+extern "C" __global__ void __launch_bounds__(kMaxComputeThreads + 64, 1) gpuos_batch_worker(const __grid_constant__ WorkerParams P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   batch_worker_body(P, smem_raw);
 }

@@ -168,7 +168,8 @@ typedef struct gpuos_rt gpuos_rt; /* one runtime per device */
 
 /* gpuos_ext.init (pytorch_ext/gpuos_ext.cpp:448-540): allocate the ring and
  * control state on `device`, launch the persistent worker (one CTA per SM, each
- * `threads_per_block` compute threads plus one dequeue warp). */
+ * `threads_per_block` compute threads, a multiple of 32 in [64, 448], plus a dequeue
+ * warp and a completion warp). */
 int gpuos_rt_init(int device, int capacity, int threads_per_block, gpuos_rt** out);
 
 /* gpuos_ext.shutdown (gpuos_ext.cpp:542-592): drain, stop the worker, free. */
@@ -231,7 +232,9 @@ int gpuos_rt_set_debug_level(gpuos_rt* rt, int level);
 int gpuos_rt_set_yield_every(gpuos_rt* rt, uint64_t every);
 /* Host-side idle time after which the worker is stopped (0: stop after every drain). */
 int gpuos_rt_set_idle_quiesce_ms(gpuos_rt* rt, int ms);
-/* Bound (ms) of the worker's in-grid waits (default 5000, env GPUOS_DEVICE_WAIT_MS). */
+/* Bound (ms) of the worker's in-grid waits (default 5000, env GPUOS_DEVICE_WAIT_MS).  A
+ * worker reads the bound when it is launched, so a running worker is stopped first
+ * (gpuos_rt_quiesce) and the next flush launches one with the new bound. */
 int gpuos_rt_set_device_wait_ms(gpuos_rt* rt, int ms);
 /* Failure-path test hook: publish one item whose dependency barrier never opens.  The
  * worker's bounded wait expires, it reports "dependency barrier wait expired" and exits;
@@ -276,9 +279,13 @@ uint64_t gpuos_rt_launches(gpuos_rt* rt);
 
 /* Per-CTA cycle counters of the last worker launch (valid once it has exited, e.g.
  * after gpuos_rt_quiesce): rows of 12 counters (stage wait, claim, idle, descriptor
- * fetch, staging, items staged, fill wait, tile, barrier, completion, items computed,
- * total cycles), one row per CTA.  Copies min(n, ctas*12) values into out and returns
- * the number of CTAs (negative status on error). */
+ * fetch, staging, items staged, fill wait, tile, completer wait, completion, bulk-copy
+ * issue, total cycles), one row per CTA, followed by one row of %globaltimer stamps (ns)
+ * of the launch's first events: launch initialised, first claim, first staging, first bulk
+ * copies, first tile start and end, first completion accounting, first exit round, first
+ * gather, exit verdict, first and last CTA finished (~0 where an event did not happen).
+ * Copies min(n, (ctas+1)*12) values into out and returns the number of CTAs (negative
+ * status on error). */
 int gpuos_rt_debug_counters(gpuos_rt* rt, uint64_t* out, int n);
 
 /* Device-free planning hooks (no CUDA call): the 64-byte work items (and, for strided
