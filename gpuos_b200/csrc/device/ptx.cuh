@@ -96,6 +96,12 @@ __device__ __forceinline__ unsigned long long ld_acquire_gpu(const unsigned long
   return v;
 }
 
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ unsigned int ld_acquire_gpu_u32(const unsigned int* p) {
   unsigned int v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -123,6 +129,16 @@ __device__ __forceinline__ uint4 ld_cg_v4(const void* p) {
                : "memory");
   return r;
 }
+
+// Asynchronous 16-byte copy global -> shared (L2 only, weak like ld_cg_v4), completed by
+// cp_async_wait_all of the issuing thread.
+__device__ __forceinline__ void cp_async_cg16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // 16-byte load that always observes the coherent (host-written) value.
 __device__ __forceinline__ uint4 ld_volatile_v4(const void* p) {

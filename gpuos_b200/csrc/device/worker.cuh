@@ -274,50 +274,46 @@ __device__ __forceinline__ void completer_loop(const WorkerParams& P, const Work
 
 // ---- dequeue warp -------------------------------------------------------------------------
 constexpr uint32_t kChunk = 8;  // tickets claimed per atomic when work is plentiful (dcache size)
+constexpr int kDgTma = 6;       // ProdCold::dg index of the bulk-copy issue cycles (slot DG_P_TMA)
 
+// Per-item state of the dequeue warp (registers; identical in every lane after each step).
 struct ProdState {
   uint64_t iter;        // items staged so far
   uint64_t ticket;      // lowest unprocessed ticket held
   uint64_t chunk_end;   // tickets [ticket, chunk_end) are claimed by this CTA
-  uint64_t desc_end;    // descriptors of tickets < desc_end are in the shared cache
+  uint64_t desc_end;    // descriptors of tickets < desc_end are in dcache[cur]
   uint64_t n_ticket;    // chunk claimed ahead: tickets [n_ticket, n_end) (empty if equal)
   uint64_t n_end;
-  uint32_t n_fetched;   // its descriptors are being loaded into the warp's registers
-  uint32_t last_seq;    // flush of the last staged item (start stamp once per flush)
   uint64_t tail_cache;
   uint64_t items_done_cache;
-  uint64_t seen_round;  // last closing round handled
-  uint64_t round;       // leader: current closing round
-  uint64_t beat_val;    // leader: last observed host beat
-  uint64_t beat_t;      // leader: when it changed
-  uint64_t polls;
-  // leader: cached host control words (refreshed every few polls, not every poll)
-  uint64_t quit_epoch, yield_every, safety_ns;
-  uint32_t spin_ns;
-  // leader: diagnostics
-  uint64_t read_sum, read_n, read_max;
-  uint64_t rounds, timeouts, work_resumes, parked_seen;
-  unsigned long long dg[7];  // DG_P_WAIT_EMPTY .. DG_P_ITEMS, then kDgTma
+  uint32_t n_fetched;   // the ahead chunk's descriptors are being copied into dcache[cur ^ 1]
+  uint32_t cur;         // dcache buffer of the current chunk
+  uint32_t last_seq;    // flush of the last staged item (start stamp once per flush)
 };
-constexpr int kDgTma = 6;  // producer counter stored in slot DG_P_TMA
 
-__device__ __forceinline__ void publish_diag(const WorkerParams& P, const ProdState& st) {
-  ptx::st_relaxed_sys(&P.rep->heartbeat, st.polls);
+__device__ __forceinline__ void publish_diag(const WorkerParams& P, const ProdCold& C) {
+  ptx::st_relaxed_sys(&P.rep->heartbeat, C.polls);
   ptx::st_relaxed_sys(&P.rep->head_mirror, *reinterpret_cast<volatile unsigned long long*>(&P.dc->head));
   ptx::st_relaxed_sys(&P.rep->items_done, *reinterpret_cast<volatile unsigned long long*>(&P.dc->items_done));
-  ptx::st_relaxed_sys(&P.rep->park_rounds, st.rounds);
-  ptx::st_relaxed_sys(&P.rep->park_timeouts, st.timeouts);
-  ptx::st_relaxed_sys(&P.rep->park_work, st.work_resumes);
-  ptx::st_relaxed_sys(&P.rep->parked_seen, st.parked_seen);
-  ptx::st_relaxed_sys(&P.rep->host_read_ns_max, st.read_max);
-  ptx::st_relaxed_sys(&P.rep->host_read_ns_avg, st.read_n ? st.read_sum / st.read_n : 0);
+  ptx::st_relaxed_sys(&P.rep->park_rounds, C.rounds);
+  ptx::st_relaxed_sys(&P.rep->park_timeouts, C.timeouts);
+  ptx::st_relaxed_sys(&P.rep->park_work, C.work_resumes);
+  ptx::st_relaxed_sys(&P.rep->parked_seen, C.parked_seen);
+  ptx::st_relaxed_sys(&P.rep->host_read_ns_max, C.read_max);
+  ptx::st_relaxed_sys(&P.rep->host_read_ns_avg, C.read_n ? C.read_sum / C.read_n : 0);
+}
+
+// Phase parity that the empty barrier of stage use `u` (u >= S) completes once use u - S
+// has been released.
+__device__ __forceinline__ uint32_t empty_parity(uint64_t u, uint32_t S) {
+  return (uint32_t)(((u >> (__ffs(S) - 1)) - 1) & 1);
 }
 
 // Wait (lane 0) until compute warps released stage use `use` (i.e. iteration use-1 done).
 __device__ __forceinline__ bool wait_empty(const WorkerParams& P, SmemHeader& H, uint64_t iter, uint32_t S) {
   if (iter < S) return true;
   const uint32_t s = (uint32_t)iter & (S - 1);
-  const uint32_t parity = (uint32_t)(((iter >> (__ffs(S) - 1)) - 1) & 1);
+  const uint32_t parity = empty_parity(iter, S);
   const uint32_t bar = ptx::smem_addr(&H.empty[s]);
   const uint64_t t0 = ptx::now_ns();
   uint32_t spins = 0;
@@ -357,20 +353,27 @@ __device__ __forceinline__ bool drain_own(const WorkerParams& P, SmemHeader& H, 
 enum ParkVerdict { PV_RESUME = 1, PV_EXIT = 2 };
 constexpr uint64_t kGatherNs = 200ull * 1000;  // leader gathers parked CTAs this long, then retries
 
-// Count this CTA as parked in `round` (no-op if that round is no longer open).
-__device__ __forceinline__ void park_count(DevCtl* dc, uint64_t round) {
-  while (true) {
-    const unsigned long long w = ptx::ld_acquire_gpu(&dc->park_word);
-    if ((w >> 32) != round) return;
-    if (atomicCAS(&dc->park_word, w, w + 1) == w) return;
+// CTAs whose parked flag shows `round` (the leader's scan: independent loads, 16 in flight).
+__device__ __forceinline__ uint32_t count_parked(DevCtl* dc, uint64_t round) {
+  const uint32_t n = gridDim.x;
+  uint32_t cnt = 0;
+  for (uint32_t c0 = 0; c0 < n; c0 += 16) {
+    unsigned long long v[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) v[k] = c0 + k < n ? ptx::ld_relaxed_gpu(&dc->parked[c0 + k]) : ~0ull;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) cnt += v[k] == round ? 1u : 0u;
   }
+  return cnt;
 }
 
 // Park protocol (lane 0 of a dequeue warp that is idle and holds an unpublished ticket).
 // Returns PV_RESUME or PV_EXIT.
-__device__ __forceinline__ int park(const WorkerParams& P, SmemHeader& H, ProdState& st, uint64_t round, uint32_t S) {
+__device__ __forceinline__ int park(const WorkerParams& P, SmemHeader& H, const ProdState& st, uint64_t round,
+                                    uint32_t S) {
   DevCtl* dc = P.dc;
-  st.seen_round = round;
+  ProdCold& C = H.cold;
+  C.seen_round = round;
   const bool leader = blockIdx.x == 0;
   if (!leader) {
     const unsigned long long v = ptx::ld_acquire_gpu(&dc->verdict);
@@ -379,35 +382,35 @@ __device__ __forceinline__ int park(const WorkerParams& P, SmemHeader& H, ProdSt
   }
   if (!drain_own(P, H, st.iter, S)) return PV_EXIT;
   atomicMin(&dc->park_min, (unsigned long long)st.ticket);
-  ptx::fence_acq_rel_gpu();
-  park_count(dc, round);
+  ptx::st_release_gpu(&dc->parked[blockIdx.x], round);
   const uint64_t t0 = ptx::now_ns();
   if (leader) {
     uint32_t spins = 0;
     bool gathered = false;
     while (true) {
-      if ((ptx::ld_acquire_gpu(&dc->park_word) & 0xffffffffull) >= gridDim.x) {
+      if (count_parked(dc, round) >= gridDim.x) {
+        ptx::fence_acq_rel_gpu();  // every parked CTA's park_min update is visible from here on
         gathered = true;
         break;
       }
       if (*reinterpret_cast<volatile unsigned int*>(&dc->abort)) break;
       const uint64_t t = ptx::ld_acquire_sys(&P.hc->tail);
       if (t > *reinterpret_cast<volatile unsigned long long*>(&dc->park_min)) {  // work for a parked CTA
-        ++st.work_resumes;
+        ++C.work_resumes;
         break;
       }
       if ((++spins & 15u) == 0) {
         const uint64_t now = ptx::now_ns();
         *reinterpret_cast<volatile unsigned long long*>(&H.prod_alive) = now;
         if (now - t0 > kGatherNs) {  // someone is still busy: retry later
-          ++st.timeouts;
-          st.parked_seen = ptx::ld_acquire_gpu(&dc->park_word) & 0xffffffffull;
+          ++C.timeouts;
+          C.parked_seen = count_parked(dc, round);
           break;
         }
       }
       ptx::nanosleep(128);
     }
-    if (st.rounds == 1) tl_mark(P, TL_GATHER);
+    if (C.rounds == 1) tl_mark(P, TL_GATHER);
     const bool aborted = *reinterpret_cast<volatile unsigned int*>(&dc->abort) != 0;
     if (!gathered && !aborted) {
       ptx::st_release_gpu(&dc->tail_mirror, ptx::ld_acquire_sys(&P.hc->tail));
@@ -421,14 +424,14 @@ __device__ __forceinline__ int park(const WorkerParams& P, SmemHeader& H, ProdSt
     const uint64_t T = ptx::ld_acquire_sys(&P.hc->tail);
     const uint64_t pm = *reinterpret_cast<volatile unsigned long long*>(&dc->park_min);
     if (!aborted && T > pm) {
-      ++st.work_resumes;
+      ++C.work_resumes;
       ptx::st_relaxed_sys(&P.rep->state, (P.epoch << 8) | WS_RUNNING);
       ptx::st_release_gpu(&dc->tail_mirror, T);
       ptx::st_release_gpu(&dc->verdict, (round << 2) | PV_RESUME);
       return PV_RESUME;
     }
     dc->exit_tail = pm;
-    publish_diag(P, st);
+    publish_diag(P, C);
     tl_mark(P, TL_VERDICT);
     ptx::st_release_gpu(&dc->verdict, (round << 2) | PV_EXIT);
     return PV_EXIT;
@@ -465,8 +468,75 @@ __device__ __forceinline__ void arm_exit(SmemHeader& H, uint32_t s) {
   ptx::mbar_arrive(ptx::smem_addr(&H.full[s]));
 }
 
-// Stage one item (whole dequeue warp; stage `st.iter % S` is free).  On an error the
-// stage is armed as the exit sentinel and false is returned.
+// Items the group path stages without help: contiguous element-wise tiles and row groups.
+__device__ __forceinline__ bool group_kind(const WorkItem& it) {
+  return it.batch < kNumBatchSlots &&
+         ((it.kind == IK_EW_CONTIG && it.op < GPUOS_EW_NUM_OPS) || it.kind == IK_ROW_REDUCE);
+}
+
+// Issue the operand copies of a contiguous element-wise tile or a row group into stage s
+// and arrive on its full barrier (one thread).  m.item is already written.
+__device__ __forceinline__ void stage_copies(const WorkerShared& W, StageMeta& m, uint32_t s, const WorkItem& it) {
+  const uint32_t full = ptx::smem_addr(&W.H->full[s]);
+  unsigned char* buf = stage_buf(W, s);
+  uint32_t staged = 0;
+  if (it.kind == IK_EW_CONTIG) {
+    uint32_t tx = 0;
+    uint64_t a0 = 0, a1 = 0, b0 = 0, b1 = 0;
+    const uint32_t half = W.stage_bytes >> 1;
+    if (!(it.flags & IF_A_BCAST)) {
+      const uint64_t bytes = (uint64_t)it.count * dtype_size(it.dt_a);
+      a0 = it.a & ~15ull;
+      a1 = (it.a + bytes + 15) & ~15ull;
+      if (a1 - a0 <= half) {
+        m.a_off = (uint32_t)(it.a - a0);
+        staged |= 1;
+        tx += (uint32_t)(a1 - a0);
+      }
+    }
+    if ((it.flags & IF_B_PRESENT) && !(it.flags & (IF_B_SCALAR | IF_B_BCAST))) {
+      const uint64_t bytes = (uint64_t)it.count * dtype_size(it.dt_b);
+      b0 = it.b & ~15ull;
+      b1 = (it.b + bytes + 15) & ~15ull;
+      if (b1 - b0 <= half) {
+        m.b_off = (uint32_t)(it.b - b0);
+        staged |= 2;
+        tx += (uint32_t)(b1 - b0);
+      }
+    }
+    m.staged = staged;
+    if (tx) {
+      ptx::mbar_arrive_expect_tx(full, tx);
+      if (staged & 1) ptx::bulk_g2s(ptx::smem_addr(buf), reinterpret_cast<const void*>(a0), (uint32_t)(a1 - a0), full);
+      if (staged & 2)
+        ptx::bulk_g2s(ptx::smem_addr(buf + half), reinterpret_cast<const void*>(b0), (uint32_t)(b1 - b0), full);
+    } else {
+      ptx::mbar_arrive(full);
+    }
+  } else if (it.kind == IK_ROW_REDUCE && !(it.flags & IF_UNSTAGED)) {
+    const int es = dtype_size(it.dt_a);
+    const int64_t rows = it.count, C = it.aux, rs = (int64_t)it.x, is = (int64_t)it.b;
+    const uint64_t span = (uint64_t)(((rows - 1) * rs + (C - 1) * is + 1) * es);
+    const uint64_t a0 = it.a & ~15ull;
+    const uint64_t a1 = (it.a + span + 15) & ~15ull;
+    if (a1 - a0 <= W.stage_bytes) {
+      m.a_off = (uint32_t)(it.a - a0);
+      m.staged = 1;
+      ptx::mbar_arrive_expect_tx(full, (uint32_t)(a1 - a0));
+      ptx::bulk_g2s(ptx::smem_addr(buf), reinterpret_cast<const void*>(a0), (uint32_t)(a1 - a0), full);
+    } else {
+      m.staged = 0;
+      ptx::mbar_arrive(full);
+    }
+  } else {
+    m.staged = 0;
+    ptx::mbar_arrive(full);
+  }
+}
+
+// Stage the item of st.ticket alone (whole dequeue warp; stage `st.iter % S` is free): every
+// kind, dependency barriers, malformed items.  On an error the stage is armed as the exit
+// sentinel and false is returned.
 __device__ __forceinline__ bool stage_item(const WorkerParams& P, const WorkerShared& W, ProdState& st, uint32_t lane) {
   SmemHeader& H = *W.H;
   const uint32_t S = P.stages;
@@ -474,7 +544,7 @@ __device__ __forceinline__ bool stage_item(const WorkerParams& P, const WorkerSh
   StageMeta& m = H.meta[s];
   if (lane == 0 && st.iter == 0) tl_mark(P, TL_STAGE);
   if (lane < 4) {
-    const uint4* src = reinterpret_cast<const uint4*>(&H.dcache[st.ticket & 7]);
+    const uint4* src = reinterpret_cast<const uint4*>(&H.dcache[st.cur][st.ticket & 7]);
     reinterpret_cast<uint4*>(&m.item)[lane] = src[lane];
   }
   __syncwarp();
@@ -514,9 +584,10 @@ __device__ __forceinline__ bool stage_item(const WorkerParams& P, const WorkerSh
     if (!ok) arm_exit(H, s);
   }
   ok = __shfl_sync(0xffffffffu, ok, 0);
+  st.items_done_cache = __shfl_sync(0xffffffffu, st.items_done_cache, 0);
+  st.last_seq = __shfl_sync(0xffffffffu, st.last_seq, 0);
   if (!ok) return false;
 
-  m.staged = 0;
   if (it.kind == IK_EW_GENERIC || it.kind == IK_RED_GENERIC) {
     warp_copy16(&m.ext.layout, P.layouts + (it.aux & P.layout_mask), sizeof(Layout), lane);
   } else if (it.kind == IK_TASK) {
@@ -525,55 +596,8 @@ __device__ __forceinline__ bool stage_item(const WorkerParams& P, const WorkerSh
   __syncwarp();
   if (lane == 0) {
     const unsigned long long c_tma = clock64();
-    const uint32_t full = ptx::smem_addr(&H.full[s]);
-    unsigned char* buf = stage_buf(W, s);
-    if (it.kind == IK_EW_CONTIG) {
-      uint32_t tx = 0;
-      uint64_t a0 = 0, a1 = 0, b0 = 0, b1 = 0;
-      const uint32_t half = W.stage_bytes >> 1;
-      if (!(it.flags & IF_A_BCAST)) {
-        const uint64_t bytes = (uint64_t)it.count * dtype_size(it.dt_a);
-        a0 = it.a & ~15ull;
-        a1 = (it.a + bytes + 15) & ~15ull;
-        if (a1 - a0 <= half) {
-          m.a_off = (uint32_t)(it.a - a0);
-          m.staged |= 1;
-          tx += (uint32_t)(a1 - a0);
-        }
-      }
-      if ((it.flags & IF_B_PRESENT) && !(it.flags & (IF_B_SCALAR | IF_B_BCAST))) {
-        const uint64_t bytes = (uint64_t)it.count * dtype_size(it.dt_b);
-        b0 = it.b & ~15ull;
-        b1 = (it.b + bytes + 15) & ~15ull;
-        if (b1 - b0 <= half) {
-          m.b_off = (uint32_t)(it.b - b0);
-          m.staged |= 2;
-          tx += (uint32_t)(b1 - b0);
-        }
-      }
-      if (tx) {
-        ptx::mbar_arrive_expect_tx(full, tx);
-        if (m.staged & 1) ptx::bulk_g2s(ptx::smem_addr(buf), reinterpret_cast<const void*>(a0), (uint32_t)(a1 - a0), full);
-        if (m.staged & 2)
-          ptx::bulk_g2s(ptx::smem_addr(buf + half), reinterpret_cast<const void*>(b0), (uint32_t)(b1 - b0), full);
-      } else {
-        ptx::mbar_arrive(full);
-      }
-    } else if (it.kind == IK_ROW_REDUCE && !(it.flags & IF_UNSTAGED)) {
-      const int es = dtype_size(it.dt_a);
-      const int64_t rows = it.count, C = it.aux, rs = (int64_t)it.x, is = (int64_t)it.b;
-      const uint64_t span = (uint64_t)(((rows - 1) * rs + (C - 1) * is + 1) * es);
-      const uint64_t a0 = it.a & ~15ull;
-      const uint64_t a1 = (it.a + span + 15) & ~15ull;
-      if (a1 - a0 <= W.stage_bytes) {
-        m.a_off = (uint32_t)(it.a - a0);
-        m.staged = 1;
-        ptx::mbar_arrive_expect_tx(full, (uint32_t)(a1 - a0));
-        ptx::bulk_g2s(ptx::smem_addr(buf), reinterpret_cast<const void*>(a0), (uint32_t)(a1 - a0), full);
-      } else {
-        ptx::mbar_arrive(full);
-      }
-    } else if (it.kind == IK_TASK) {
+    if (it.kind == IK_TASK) {
+      m.staged = 0;
       const OpFn fn = resolve_op(P, m.ext.task.op);
       if (fn == nullptr) {
         report_error(P, DE_NULL_OP, st.ticket);
@@ -581,12 +605,12 @@ __device__ __forceinline__ bool stage_item(const WorkerParams& P, const WorkerSh
         arm_exit(H, s);
       } else {
         m.item.x = reinterpret_cast<uint64_t>(fn);
-        ptx::mbar_arrive(full);
+        ptx::mbar_arrive(ptx::smem_addr(&H.full[s]));
       }
     } else {
-      ptx::mbar_arrive(full);
+      stage_copies(W, m, s, it);
     }
-    st.dg[kDgTma] += clock64() - c_tma;
+    H.cold.dg[kDgTma] += clock64() - c_tma;
     if (st.iter == 0) tl_mark(P, TL_TMA);
   }
   ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -598,20 +622,59 @@ __device__ __forceinline__ bool stage_item(const WorkerParams& P, const WorkerSh
     fn(m.ext.task);
     ptx::named_bar_sync(kBarTask, blockDim.x);
   }
+  st.iter += 1;
+  st.ticket += 1;
   return true;
 }
 
-__device__ __forceinline__ void push_exit(const WorkerParams& P, SmemHeader& H, ProdState& st, uint32_t lane) {
+// Stage up to S items of the current chunk at once, one lane per item: the items whose
+// descriptors are here, that the group path handles, need no dependency wait, and whose
+// stages are already free (stage st.iter is).  Returns the number staged (0: the item of
+// st.ticket needs stage_item).
+__device__ __forceinline__ uint32_t stage_group(const WorkerParams& P, const WorkerShared& W, ProdState& st,
+                                                uint32_t lane) {
+  SmemHeader& H = *W.H;
   const uint32_t S = P.stages;
-  if (lane == 0) {
-    wait_empty(P, H, st.iter, S);
-    arm_exit(H, (uint32_t)st.iter & (S - 1));
+  const uint64_t have = st.desc_end - st.ticket;
+  const uint32_t navail = (uint32_t)(have < S ? have : S);
+  WorkItem it;
+  bool ok = false;
+  if (lane < navail) {
+    it = H.dcache[st.cur][(st.ticket + lane) & 7];
+    const uint64_t u = st.iter + lane;
+    const bool free = lane == 0 || u < S ||
+                      ptx::mbar_test_wait(ptx::smem_addr(&H.empty[(uint32_t)u & (S - 1)]), empty_parity(u, S));
+    ok = free && group_kind(it) && it.wait_items <= st.items_done_cache;
+  } else {
+    it.batch_seq = 0;
+  }
+  const uint32_t mask = __ballot_sync(0xffffffffu, ok);
+  const uint32_t g = (uint32_t)__ffs(~mask) - 1;  // leading lanes that can stage
+  if (g == 0) return 0;
+  const uint32_t prev_seq = __shfl_up_sync(0xffffffffu, it.batch_seq, 1);
+  if (lane < g) {
+    const uint32_t s = (uint32_t)(st.iter + lane) & (S - 1);
+    StageMeta& m = H.meta[s];
+    m.item = it;
+    // start stamp of the flush: the first item each CTA stages from it is enough
+    if (it.batch_seq != (lane == 0 ? st.last_seq : prev_seq))
+      atomicMin(&P.dc->batch_t0[it.batch], (unsigned long long)ptx::now_ns());
+    stage_copies(W, m, s, it);
+  }
+  st.last_seq = __shfl_sync(0xffffffffu, it.batch_seq, g - 1);
+  if (lane == 0 && st.iter == 0) {
+    tl_mark(P, TL_STAGE);
+    tl_mark(P, TL_TMA);
   }
   __syncwarp();
+  st.iter += g;
+  st.ticket += g;
+  return g;
 }
 
 __device__ __forceinline__ void producer_loop(const WorkerParams& P, const WorkerShared& W, uint32_t lane) {
   SmemHeader& H = *W.H;
+  ProdCold& C = H.cold;
   DevCtl* dc = P.dc;
   const uint32_t S = P.stages;
   const bool leader = blockIdx.x == 0;
@@ -620,50 +683,36 @@ __device__ __forceinline__ void producer_loop(const WorkerParams& P, const Worke
   st.ticket = 0;
   st.chunk_end = 0;
   st.desc_end = 0;
+  st.n_ticket = st.n_end = 0;
+  st.n_fetched = 0;
+  st.cur = 0;
   st.last_seq = 0;
   st.tail_cache = ptx::ld_acquire_gpu(&dc->tail_mirror);
   st.items_done_cache = 0;
-  st.seen_round = 0;
-  st.round = 0;
-  st.beat_val = leader ? P.hc->host_beat : 0;
-  st.beat_t = ptx::now_ns();
-  st.polls = 0;
-  st.quit_epoch = ptx::ld_acquire_gpu(&dc->p_quit_epoch);
-  st.yield_every = ptx::ld_acquire_gpu(&dc->p_yield_every);
-  st.safety_ns = ptx::ld_acquire_gpu(&dc->p_safety_idle_ns);
-  st.spin_ns = (uint32_t)ptx::ld_acquire_gpu(&dc->p_spin_ns);
-  st.read_sum = st.read_n = st.read_max = 0;
-  st.rounds = st.timeouts = st.work_resumes = st.parked_seen = 0;
-  for (int k = 0; k < 7; ++k) st.dg[k] = 0;
-  struct Flush {
-    const WorkerParams& P;
-    uint32_t lane;
-    ProdState& st;
-    __device__ ~Flush() {
-      if (lane == 0 && blockIdx.x < kDiagCtas) {
-        unsigned long long* row = P.dc->diag[blockIdx.x];
-        for (int k = 0; k < 6; ++k) row[k] = st.dg[k];
-        row[DG_P_TMA] = st.dg[kDgTma];
-      }
-    }
-  } flush_diag{P, lane, st};
-
-  st.n_ticket = st.n_end = 0;
-  st.n_fetched = 0;
-  // Descriptors of the chunk claimed ahead, 16 bytes per lane (4 lanes per descriptor).  The
-  // loads are issued when the chunk is claimed and land in shared memory only when the chunk
-  // becomes current, so their latency (a read of mapped host memory) overlaps the staging of
-  // the current chunk.
-  uint4 pf = make_uint4(0, 0, 0, 0);
+  if (lane == 0) {
+    C.seen_round = 0;
+    C.round = 0;
+    C.beat_val = leader ? P.hc->host_beat : 0;
+    C.beat_t = ptx::now_ns();
+    C.polls = 0;
+    C.quit_epoch = ptx::ld_acquire_gpu(&dc->p_quit_epoch);
+    C.yield_every = ptx::ld_acquire_gpu(&dc->p_yield_every);
+    C.safety_ns = ptx::ld_acquire_gpu(&dc->p_safety_idle_ns);
+    C.spin_ns = ptx::ld_acquire_gpu(&dc->p_spin_ns);
+    C.read_sum = C.read_n = C.read_max = 0;
+    C.rounds = C.timeouts = C.work_resumes = C.parked_seen = 0;
+    for (int k = 0; k < 7; ++k) C.dg[k] = 0;
+  }
+  __syncwarp();
 
   while (true) {
-    int action = 0;  // 0: stage ticket, 1: exit
+    int action = 0;  // 0: stage, 1: exit, 2: error after staging began
     uint32_t switched = 0, issue = 0;
     if (lane == 0) {
       unsigned long long c0 = clock64();
       const bool empty_ok = wait_empty(P, H, st.iter, S);
       unsigned long long c1 = clock64();
-      st.dg[DG_P_WAIT_EMPTY] += c1 - c0;
+      C.dg[DG_P_WAIT_EMPTY] += c1 - c0;
       if (!empty_ok) {
         action = 1;
       } else if (st.ticket == st.chunk_end) {
@@ -687,7 +736,7 @@ __device__ __forceinline__ void producer_loop(const WorkerParams& P, const Worke
           st.desc_end = st.ticket;
         }
         // Claim the next chunk now while at least two tickets per CTA of published work lie
-        // beyond this one; its descriptors are loaded while this chunk is staged.  A CTA
+        // beyond this one; its descriptors are copied while this chunk is staged.  A CTA
         // that goes idle never holds a chunk ahead (this chunk would have to be published).
         const uint64_t ahead = st.tail_cache > st.chunk_end ? st.tail_cache - st.chunk_end : 0;
         if (st.chunk_end <= st.tail_cache && ahead >= 2ull * gridDim.x) {
@@ -699,21 +748,21 @@ __device__ __forceinline__ void producer_loop(const WorkerParams& P, const Worke
           issue = st.n_fetched;
         }
         c0 = clock64();
-        st.dg[DG_P_CLAIM] += c0 - c1;
+        C.dg[DG_P_CLAIM] += c0 - c1;
         c1 = c0;
       }
       while (action == 0 && st.ticket >= st.tail_cache) {
         // idle: poll for publication, watch for exit conditions
-        ++st.polls;
+        ++C.polls;
         uint64_t t;
         if (leader) {
           // only the leader reads host memory; everybody else polls its device mirror
           const uint64_t r0 = ptx::now_ns();
           t = ptx::ld_acquire_sys(&P.hc->tail);
           const uint64_t dr = ptx::now_ns() - r0;
-          st.read_sum += dr;
-          ++st.read_n;
-          if (dr > st.read_max) st.read_max = dr;
+          C.read_sum += dr;
+          ++C.read_n;
+          if (dr > C.read_max) C.read_max = dr;
           if (t > *reinterpret_cast<volatile unsigned long long*>(&dc->tail_mirror)) ptx::st_release_gpu(&dc->tail_mirror, t);
         } else {
           t = ptx::ld_acquire_gpu(&dc->tail_mirror);
@@ -728,34 +777,35 @@ __device__ __forceinline__ void producer_loop(const WorkerParams& P, const Worke
           action = 1;
           break;
         }
-        if (leader && (st.polls & 7u) == 0) {
-          st.quit_epoch = P.hc->quit_epoch;
-          const uint64_t beat = P.hc->host_beat;
-          if (beat != st.beat_val) {
-            st.beat_val = beat;
-            st.beat_t = now;
+        if (leader) {
+          if ((C.polls & 7u) == 0) {  // host control words: refreshed every few polls
+            C.quit_epoch = P.hc->quit_epoch;
+            const uint64_t beat = P.hc->host_beat;
+            if (beat != C.beat_val) {
+              C.beat_val = beat;
+              C.beat_t = now;
+            }
+            if ((C.polls & 63u) == 0) {
+              C.yield_every = P.hc->yield_every;
+              C.safety_ns = P.hc->safety_idle_ns;
+              C.spin_ns = P.hc->spin_ns;
+              publish_diag(P, C);
+            }
           }
-          if ((st.polls & 63u) == 0) {
-            st.yield_every = P.hc->yield_every;
-            st.safety_ns = P.hc->safety_idle_ns;
-            st.spin_ns = P.hc->spin_ns;
-            publish_diag(P, st);
-          }
-          bool want_exit = st.quit_epoch >= P.epoch;
-          if (st.yield_every && ptx::ld_acquire_gpu(&dc->items_done) - dc->yield_base >= st.yield_every) want_exit = true;
-          if (now - st.beat_t > st.safety_ns) want_exit = true;
+          bool want_exit = C.quit_epoch >= P.epoch;
+          if (C.yield_every && ptx::ld_acquire_gpu(&dc->items_done) - dc->yield_base >= C.yield_every) want_exit = true;
+          if (now - C.beat_t > C.safety_ns) want_exit = true;
           if (want_exit) {
-            st.round = (st.round > st.seen_round ? st.round : st.seen_round) + 1;
-            if (st.rounds == 0) tl_mark(P, TL_ROUND);
-            ++st.rounds;
-            dc->park_min = ~0ull;
-            atomicExch(&dc->park_word, (unsigned long long)st.round << 32);
+            C.round = (C.round > C.seen_round ? C.round : C.seen_round) + 1;
+            if (C.rounds == 0) tl_mark(P, TL_ROUND);
+            ++C.rounds;
+            atomicExch(&dc->park_min, ~0ull);
             ptx::fence_acq_rel_gpu();
-            ptx::st_release_gpu(&dc->closing, st.round);
+            ptx::st_release_gpu(&dc->closing, C.round);
           }
         }
         const unsigned long long cl = ptx::ld_acquire_gpu(&dc->closing);
-        if (cl > st.seen_round) {
+        if (cl > C.seen_round) {
           const int v = park(P, H, st, cl, S);
           if (v == PV_EXIT) {
             action = 1;
@@ -764,16 +814,19 @@ __device__ __forceinline__ void producer_loop(const WorkerParams& P, const Worke
           st.tail_cache = ptx::ld_acquire_gpu(&dc->tail_mirror);
           continue;
         }
-        ptx::nanosleep(leader ? st.spin_ns : 256);
+        ptx::nanosleep(leader ? (uint32_t)C.spin_ns : 256);
       }
-      st.dg[DG_P_IDLE] += clock64() - c1;
+      C.dg[DG_P_IDLE] += clock64() - c1;
     }
     action = __shfl_sync(0xffffffffu, action, 0);
     if (action == 1) {
-      push_exit(P, H, st, lane);
-      return;
+      if (lane == 0) {
+        wait_empty(P, H, st.iter, S);
+        arm_exit(H, (uint32_t)st.iter & (S - 1));
+      }
+      break;
     }
-    __syncwarp();  // orders lane 0's acquire of the tail before the other lanes' descriptor loads
+    __syncwarp();  // orders lane 0's acquire of the tail before the other lanes' descriptor reads
     st.ticket = __shfl_sync(0xffffffffu, st.ticket, 0);
     st.chunk_end = __shfl_sync(0xffffffffu, st.chunk_end, 0);
     st.desc_end = __shfl_sync(0xffffffffu, st.desc_end, 0);
@@ -782,18 +835,21 @@ __device__ __forceinline__ void producer_loop(const WorkerParams& P, const Worke
     issue = __shfl_sync(0xffffffffu, issue, 0);
     unsigned long long cd = clock64();
     if (switched) {
-      // the chunk claimed ahead is current: its descriptors go to the shared cache
-      if (lane < 4 * (uint32_t)(st.chunk_end - st.ticket))
-        reinterpret_cast<uint4*>(&H.dcache[(st.ticket + (lane >> 2)) & 7])[lane & 3] = pf;
+      // the chunk claimed ahead is current: wait for the copies of its descriptors
+      ptx::cp_async_wait_all();
       __syncwarp();
+      st.cur ^= 1u;
     }
     if (issue) {
       st.n_ticket = __shfl_sync(0xffffffffu, st.n_ticket, 0);
       st.n_end = __shfl_sync(0xffffffffu, st.n_end, 0);
+      st.n_fetched = 1;
       if (lane < 4 * (uint32_t)(st.n_end - st.n_ticket)) {
         const uint64_t t = st.n_ticket + (lane >> 2);
-        pf = ptx::ld_cg_v4(reinterpret_cast<const unsigned char*>(P.items + (t & P.item_mask)) + (lane & 3) * 16);
+        ptx::cp_async_cg16(ptx::smem_addr(&H.dcache[st.cur ^ 1u][t & 7]) + (lane & 3) * 16,
+                           reinterpret_cast<const unsigned char*>(P.items + (t & P.item_mask)) + (lane & 3) * 16);
       }
+      ptx::cp_async_commit();
     }
     if (st.ticket >= st.desc_end) {
       // one warp-wide read fetches the descriptors of every published ticket of the chunk
@@ -802,18 +858,30 @@ __device__ __forceinline__ void producer_loop(const WorkerParams& P, const Worke
       if (lane < 4 * cnt) {
         const uint64_t t = st.ticket + (lane >> 2);
         const unsigned char* src = reinterpret_cast<const unsigned char*>(P.items + (t & P.item_mask)) + (lane & 3) * 16;
-        reinterpret_cast<uint4*>(&H.dcache[t & 7])[lane & 3] = ptx::ld_cg_v4(src);
+        reinterpret_cast<uint4*>(&H.dcache[st.cur][t & 7])[lane & 3] = ptx::ld_cg_v4(src);
       }
       __syncwarp();
       st.desc_end = hi;
     }
     unsigned long long ce = clock64();
-    st.dg[DG_P_DESC] += ce - cd;
-    if (!stage_item(P, W, st, lane)) return;
-    st.dg[DG_P_STAGE] += clock64() - ce;
-    st.dg[DG_P_ITEMS] += 1;
-    st.iter = __shfl_sync(0xffffffffu, st.iter, 0) + 1;
-    st.ticket += 1;
+    if (lane == 0) C.dg[DG_P_DESC] += ce - cd;
+    uint32_t g = stage_group(P, W, st, lane);
+    if (g == 0) {
+      if (!stage_item(P, W, st, lane)) break;
+      g = 1;
+    }
+    if (lane == 0) {
+      C.dg[DG_P_STAGE] += clock64() - ce;
+      C.dg[DG_P_ITEMS] += g;
+    }
+  }
+  // no descriptor copy may still be landing in shared memory when the warp leaves
+  ptx::cp_async_wait_all();
+  __syncwarp();
+  if (lane == 0 && blockIdx.x < kDiagCtas) {
+    unsigned long long* row = dc->diag[blockIdx.x];
+    for (int k = 0; k < 6; ++k) row[k] = C.dg[k];
+    row[DG_P_TMA] = C.dg[kDgTma];
   }
 }
 
@@ -850,7 +918,7 @@ __device__ void batch_worker_body(const WorkerParams& P, unsigned char* smem_raw
       dc->head = dc->exit_tail;
       dc->closing = 0;
       dc->verdict = 0;
-      dc->park_word = 0;
+      for (uint32_t c = 0; c < gridDim.x && c < (uint32_t)kDiagCtas; ++c) dc->parked[c] = 0;
       dc->park_min = ~0ull;
       dc->abort = 0;
       dc->exited = 0;

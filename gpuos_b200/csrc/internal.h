@@ -189,13 +189,14 @@ struct alignas(128) DevCtl {
   unsigned long long closing;      // leader requests grid exit (round number)
   unsigned long long verdict;      // (round << 2) | 1 resume | 2 exit
   unsigned long long park_min;     // lowest held ticket among parked CTAs
-  unsigned long long park_word;    // (round << 32) | CTAs parked in that round
+  unsigned long long _reserved;
   unsigned int abort;              // a CTA hit an error: everybody exits
   unsigned int exited;             // CTAs that left the current launch
   unsigned long long yield_base;   // items_done at launch (yield accounting)
   // HostCtl words as CTA 0 read them at launch: every other CTA takes them from here, so a
   // launch reads host memory from one thread only
   unsigned long long p_wait_limit_ns, p_safety_idle_ns, p_yield_every, p_quit_epoch, p_spin_ns;
+  unsigned long long parked[kDiagCtas];  // per CTA: the exit round it last parked in
   unsigned int batch_done[kNumBatchSlots];
   unsigned long long batch_t0[kNumBatchSlots];
   unsigned long long diag[kDiagCtas][kDiagSlots];  // per-CTA cycle counters of the last launch
@@ -226,7 +227,7 @@ struct WorkerParams {
 };
 
 // Per-stage bookkeeping in shared memory.
-struct alignas(16) StageMeta {
+struct alignas(64) StageMeta {
   WorkItem item;
   uint32_t a_off;       // byte offset of the first a element inside the staged buffer
   uint32_t b_off;
@@ -241,6 +242,21 @@ struct alignas(16) StageMeta {
 
 // Worker shared-memory header (stage buffers follow, 128-byte aligned).
 constexpr int kMaxStages = 8;
+// Dequeue-warp state used off the per-item path (leader polling, exit rounds, diagnostics);
+// kept in shared memory so the per-item state stays in registers.
+struct ProdCold {
+  uint64_t seen_round;  // last closing round handled
+  uint64_t round;       // leader: current closing round
+  uint64_t beat_val;    // leader: last observed host beat
+  uint64_t beat_t;      // leader: when it changed
+  uint64_t polls;
+  uint64_t quit_epoch, yield_every, safety_ns;  // leader: host control words (refreshed while idle)
+  uint64_t spin_ns;
+  uint64_t read_sum, read_n, read_max;          // leader: host tail read latency
+  uint64_t rounds, timeouts, work_resumes, parked_seen;
+  unsigned long long dg[7];  // DG_P_WAIT_EMPTY .. DG_P_ITEMS, then the bulk-copy issue cycles
+};
+
 struct alignas(128) SmemHeader {
   unsigned long long full[kMaxStages];   // dequeue warp -> compute warps (+ TMA bytes)
   unsigned long long empty[kMaxStages];  // completer -> dequeue warp
@@ -251,7 +267,8 @@ struct alignas(128) SmemHeader {
   unsigned int exit_flag;
   unsigned int _pad;
   StageMeta meta[kMaxStages];
-  WorkItem dcache[8];              // descriptors of the claimed chunk (ticket & 7)
+  WorkItem dcache[2][8];           // descriptors of the current / next chunk (ticket & 7)
+  ProdCold cold;
 };
 
 // Compute threads per worker CTA at most (plus the dequeue and completer warps): 512 threads

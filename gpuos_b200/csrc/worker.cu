@@ -274,7 +274,7 @@ extern "C" size_t gpuos_internal_smem_header_bytes() { return (sizeof(SmemHeader
 // words, ticket, layouts and tile descriptors of its one-shot worker launch live in this array,
 // which every device that loads the library holds until the process exits.  In host code the
 // name stands in for the array only; its device address comes from cudaGetSymbolAddress.
-static_assert(StaticScratch::kBytes == 1113856, "the documented scratch size has changed");
+static_assert(StaticScratch::kBytes == 1115904, "the documented scratch size has changed");
 static __device__ __align__(256) unsigned char g_noalloc_scratch[StaticScratch::kBytes];
 
 namespace {
