@@ -14,7 +14,8 @@ Printed JSON line (rank 0):
             D2H of out inside every step
   roofline  the worker kernel: algorithmic bytes (12 B per element) / launch duration,
             launches timed with CUDA events on the worker's stream in drain mode (one launch
-            per flush), against MEASURED_PEAKS.json hbm_gbs
+            per step, from launch to grid exit), against MEASURED_PEAKS.json hbm_gbs; traffic
+            is the DRAM bytes of one such launch from the committed ncu summary
   baselines GPU per-op torch eager (same stream of requests as individual launches) and
             the CPU path (PyTorch CPU eager over the same requests on the host cores)
   latency   p50/p99 submit->done of single 4096-element requests (sync flush each)
@@ -30,7 +31,6 @@ import datetime
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -73,6 +73,16 @@ def peaks():
         return 6650.0, "fallback"
 
 
+def profiled_traffic():
+    """DRAM bytes (read + write) of one worker launch on this workload, from the committed ncu
+    summary (profiles/gpuos_batch_worker_c1_drain.json), or None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "gpuos_batch_worker_c1_drain.json")) as f:
+            return float(json.load(f)["dram_bytes_per_launch"])
+    except Exception:
+        return None
+
+
 def workload(rank: int, R: int, N: int):
     g = torch.Generator().manual_seed(1234 + 1 + rank)
     A = torch.rand(R, N, generator=g) * 2 - 1
@@ -82,51 +92,62 @@ def workload(rank: int, R: int, N: int):
 
 
 class Clocks:
-    """nvidia-smi samples during the timed region."""
+    """SM clock and clock-event reasons sampled through NVML every 20 ms while a timed region
+    runs."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksThrottleReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksThrottleReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksThrottleReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksThrottleReasonSwPowerCap"),
+               ("hw_power_brake", "nvmlClocksThrottleReasonHwPowerBrakeSlowdown"))
 
     def __init__(self, index: int):
         self.index = index
-        self.samples = []
-        self.proc = None
+        self.samples = []  # (sm_mhz, reasons bitmask)
+        self.sm_max = None
+        self.stop_evt = threading.Event()
         self.thread = None
+        self.nvml = None
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            import pynvml
+            pynvml.nvmlInit()
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            phys = int(vis.split(",")[self.index]) if vis else self.index
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(phys)
+            self.sm_max = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            self.nvml = pynvml
         except Exception:
-            self.proc = None
+            self.nvml = None
             return
-        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread = threading.Thread(target=self._run, daemon=True)
         self.thread.start()
 
-    def _read(self):
-        for line in self.proc.stdout:
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) >= 9:
-                self.samples.append(parts)
+    def _run(self):
+        nv = self.nvml
+        while not self.stop_evt.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                try:
+                    r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                except Exception:
+                    r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.handle)
+                self.samples.append((sm, r))
+            except Exception:
+                pass
+            self.stop_evt.wait(0.02)
 
     def stop(self):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self.stop_evt.set()
         if self.thread is not None:
             self.thread.join(timeout=2)
         if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
-        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
-        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[k] for s in self.samples for k in range(4) if s[5 + k].lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+            return {"sm_mhz": None, "sm_max_mhz": self.sm_max, "reasons": ["clock sampling unavailable"], "samples": 0}
+        nv = self.nvml
+        reasons = sorted({name for _, r in self.samples for name, attr in self.REASONS
+                          if hasattr(nv, attr) and r & getattr(nv, attr)})
+        return {"sm_mhz": statistics.median(sm for sm, _ in self.samples), "sm_max_mhz": self.sm_max,
                 "reasons": reasons, "samples": len(self.samples)}
 
 
@@ -312,12 +333,15 @@ def main():
     }
 
     if not args.no_extras:
-        # ---- roofline: worker launches timed with CUDA events on the worker's stream ----
+        # ---- roofline: the worker launched once per step (drain mode), each launch timed
+        # with CUDA events on the worker's own stream ----
         g.set_idle_quiesce_ms(0)
         g.quiesce()
         ks = torch.cuda.ExternalStream(g.kernel_stream())
+        rclocks = Clocks(dev)
+        rclocks.start()
         durs = []
-        for k in range(max(5, args.steps // 2)):
+        for k in range(max(6, args.steps)):
             for i in range(R):
                 subs[i](a_rows[i], b_rows[i], o_rows[i])
             ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -327,13 +351,18 @@ def main():
             eb.synchronize()
             if k > 0:
                 durs.append(ea.elapsed_time(eb))
+        rclk = rclocks.stop()
         g.set_idle_quiesce_ms(200 if args.worker_mode == "persistent" else 0)
         kms = statistics.mean(durs)
-        achieved = R * N * BYTES_PER_ELEM / (kms * 1e-3) / 1e9
+        alg = R * N * BYTES_PER_ELEM
+        achieved = alg / (kms * 1e-3) / 1e9
         line["roofline"] = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                            "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
-                            "kernel": "gpuos_batch_worker", "launch_ms": kms,
-                            "algorithmic_bytes_per_launch": R * N * BYTES_PER_ELEM}
+                            "frac": achieved / peak, "traffic": profiled_traffic(), "peak_kind": peak_kind,
+                            "kernel": "gpuos_batch_worker", "launch_ms": kms, "launches": len(durs),
+                            "algorithmic_bytes_per_launch": alg,
+                            "what": "one launch per step: 4096 tiles of 4096 fp32 (read a, b; write out), "
+                                    "from the launch to the grid's exit",
+                            "clocks": rclk}
 
         # ---- e2e: host buffers, H2D + D2H inside every step ----
         hA, hB = A.pin_memory(), B.pin_memory()

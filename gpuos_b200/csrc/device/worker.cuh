@@ -166,10 +166,12 @@ __device__ __forceinline__ void compute_loop(const WorkerParams& P, const Worker
       ctx.sb = stage_buf(W, s) + (W.stage_bytes >> 1);
       ctx.tid = ctid;
       ctx.nt = nct;
-      const uint32_t fi = (kind == IK_EW_CONTIG || kind == IK_EW_GENERIC) ? m.item.op : GPUOS_EW_NUM_OPS;
-      TileFn fn = g_tile_fns[fi];
       if (iter == 0 && ctid == 0) tl_mark(P, TL_TILE0);
-      fn(ctx);
+      if (kind != IK_EW_CONTIG || !f32_staged_tile(m, ctx.sa, ctx.sb, ctid, nct)) {
+        const uint32_t fi = (kind == IK_EW_CONTIG || kind == IK_EW_GENERIC) ? m.item.op : GPUOS_EW_NUM_OPS;
+        TileFn fn = g_tile_fns[fi];
+        fn(ctx);
+      }
       if (iter == 0 && ctid == 0) tl_mark(P, TL_TILE1);
     }
     // this warp is done with the stage; no CTA-wide barrier between tiles
