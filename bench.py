@@ -258,6 +258,9 @@ def main():
     else:
         torch.cuda.set_device(0)
     dev = torch.cuda.current_device()
+    if args.worker_mode == "drain":
+        # every launch (the one at init included) exits as soon as its work is done
+        os.environ["GPUOS_IDLE_QUIESCE_MS"] = "0"
     from gpuos_b200 import gpuos_ext as g
 
     R, N = args.requests, args.numel
@@ -333,35 +336,34 @@ def main():
     }
 
     if not args.no_extras:
-        # ---- roofline: the worker launched once per step (drain mode), each launch timed
-        # with CUDA events on the worker's own stream ----
+        # ---- roofline: the worker launched once per step (drain mode); the runtime brackets
+        # each launch with CUDA events on the worker's own stream ----
         g.set_idle_quiesce_ms(0)
         g.quiesce()
-        ks = torch.cuda.ExternalStream(g.kernel_stream())
+        g.launch_times()
+        g.set_launch_timing(True)
         rclocks = Clocks(dev)
         rclocks.start()
-        durs = []
-        for k in range(max(6, args.steps)):
+        nsteps = max(6, args.steps)
+        for k in range(nsteps + 1):
             for i in range(R):
                 subs[i](a_rows[i], b_rows[i], o_rows[i])
-            ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            ea.record(ks)
             g.flush(sync=True)
-            eb.record(ks)
-            eb.synchronize()
-            if k > 0:
-                durs.append(ea.elapsed_time(eb))
+        g.quiesce()
+        torch.cuda.synchronize()
         rclk = rclocks.stop()
+        durs = g.launch_times()[1:]  # the first launch of the series is not timed
+        g.set_launch_timing(False)
         g.set_idle_quiesce_ms(200 if args.worker_mode == "persistent" else 0)
-        kms = statistics.mean(durs)
         alg = R * N * BYTES_PER_ELEM
+        kms = sum(durs) / nsteps  # launch time per step (a launch may serve more than one step)
         achieved = alg / (kms * 1e-3) / 1e9
         line["roofline"] = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                             "frac": achieved / peak, "traffic": profiled_traffic(), "peak_kind": peak_kind,
                             "kernel": "gpuos_batch_worker", "launch_ms": kms, "launches": len(durs),
                             "algorithmic_bytes_per_launch": alg,
-                            "what": "one launch per step: 4096 tiles of 4096 fp32 (read a, b; write out), "
-                                    "from the launch to the grid's exit",
+                            "what": "one launch per step (drain mode): 4096 tiles of 4096 fp32 (read a, b; "
+                                    "write out), CUDA events on the worker stream around each launch",
                             "clocks": rclk}
 
         # ---- e2e: host buffers, H2D + D2H inside every step ----

@@ -693,6 +693,35 @@ PyObject* py_debug_timeline(PyObject*, PyObject* args, PyObject* kw) {
   return row;
 }
 
+PyObject* py_set_launch_timing(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"on", "device", nullptr};
+  int on = 1;
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "p|O", const_cast<char**>(kwlist), &on, &devobj)) return nullptr;
+  gpuos_rt* rt = rt_arg(devobj, nullptr);
+  if (!rt) return nullptr;
+  const int st = gpuos_rt_set_launch_timing(rt, on);
+  if (st) return raise_status(st);
+  Py_RETURN_NONE;
+}
+
+PyObject* py_launch_times(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"device", nullptr};
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "|O", const_cast<char**>(kwlist), &devobj)) return nullptr;
+  gpuos_rt* rt = rt_arg(devobj, nullptr);
+  if (!rt) return nullptr;
+  std::vector<float> buf(4096);
+  int n;
+  Py_BEGIN_ALLOW_THREADS
+  n = gpuos_rt_launch_times(rt, buf.data(), (int)buf.size());
+  Py_END_ALLOW_THREADS
+  if (n < 0) return raise_status(-n);
+  PyObject* out = PyList_New(n);
+  for (int i = 0; i < n; ++i) PyList_SET_ITEM(out, i, PyFloat_FromDouble(buf[i]));
+  return out;
+}
+
 PyObject* py_launches(PyObject*, PyObject* args, PyObject* kw) {
   static const char* kwlist[] = {"device", nullptr};
   PyObject* devobj = Py_None;
@@ -979,6 +1008,10 @@ PyMethodDef kMethods[] = {
     {"set_device_wait_ms", py_set_device_wait_ms, METH_VARARGS, "bound of the worker's in-grid waits"},
     {"debug_timeline", (PyCFunction)(void (*)(void))py_debug_timeline, METH_VARARGS | METH_KEYWORDS,
      "debug_timeline(device=None) -> [12 %globaltimer stamps of the last launch's first events]"},
+    {"set_launch_timing", (PyCFunction)(void (*)(void))py_set_launch_timing, METH_VARARGS | METH_KEYWORDS,
+     "set_launch_timing(on, device=None): bracket every worker launch with CUDA events"},
+    {"launch_times", (PyCFunction)(void (*)(void))py_launch_times, METH_VARARGS | METH_KEYWORDS,
+     "launch_times(device=None) -> [ms of each finished timed launch, oldest first]"},
     {"debug_counters", (PyCFunction)(void (*)(void))py_debug_counters, METH_VARARGS | METH_KEYWORDS,
      "per-CTA cycle counters of the last worker launch"},
     {"debug_inject_stall", (PyCFunction)(void (*)(void))py_debug_inject_stall, METH_VARARGS | METH_KEYWORDS,

@@ -608,6 +608,10 @@ struct gpuos_rt {
   uint32_t stage_bytes = kStageBytesDefault;
   size_t smem = 0;
   cudaStream_t kstream = nullptr, cstream = nullptr;
+  // CUDA events around worker launches (gpuos_rt_set_launch_timing): pairs in launch order
+  bool time_launches = false;
+  std::deque<std::pair<cudaEvent_t, cudaEvent_t>> launch_events;
+  std::vector<cudaEvent_t> spare_events;
 
   // mapped pinned block
   void* host_block = nullptr;
@@ -735,8 +739,24 @@ static int launch_worker_locked(gpuos_rt* rt) {
   P.compute_threads = (uint32_t)rt->tpb;
   P.wait_limit_ns = rt->hc->wait_limit_ns;
   CK(cudaSetDevice(rt->device));
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  if (rt->time_launches) {
+    for (cudaEvent_t* ev : {&ev0, &ev1}) {
+      if (!rt->spare_events.empty()) {
+        *ev = rt->spare_events.back();
+        rt->spare_events.pop_back();
+      } else {
+        CK(cudaEventCreate(ev));
+      }
+    }
+    CK(cudaEventRecord(ev0, rt->kstream));
+  }
   // one dequeue warp + one completer warp + threads_per_block compute threads
   CK(gpuos_internal_launch_batch_worker(&P, rt->sm_count, rt->tpb + 64, rt->smem, rt->kstream));
+  if (rt->time_launches) {
+    CK(cudaEventRecord(ev1, rt->kstream));
+    rt->launch_events.emplace_back(ev0, ev1);
+  }
   rt->launched = true;
   return GPUOS_OK;
 }
@@ -1027,6 +1047,11 @@ extern "C" int gpuos_rt_shutdown(gpuos_rt* rt) {
   cudaError_t e = cudaStreamSynchronize(rt->kstream);
   if (e != cudaSuccess && !status) status = fail(GPUOS_ERR_CUDA, "worker: %s", cudaGetErrorString(e));
   cudaStreamSynchronize(rt->cstream);
+  for (auto& pr : rt->launch_events) {
+    cudaEventDestroy(pr.first);
+    cudaEventDestroy(pr.second);
+  }
+  for (cudaEvent_t ev : rt->spare_events) cudaEventDestroy(ev);
   cudaStreamDestroy(rt->kstream);
   cudaStreamDestroy(rt->cstream);
   cudaFree(rt->dc);
@@ -1182,6 +1207,34 @@ extern "C" int gpuos_rt_flush_times(gpuos_rt* rt, uint64_t seq, uint64_t* t_star
 }
 
 extern "C" cudaStream_t gpuos_rt_kernel_stream(gpuos_rt* rt) { return rt ? rt->kstream : nullptr; }
+
+extern "C" int gpuos_rt_set_launch_timing(gpuos_rt* rt, int on) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  std::lock_guard<std::mutex> lk(rt->mu);
+  rt->time_launches = on != 0;
+  return GPUOS_OK;
+}
+
+extern "C" int gpuos_rt_launch_times(gpuos_rt* rt, float* ms_out, int max) {
+  if (!rt) return -fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  std::lock_guard<std::mutex> lk(rt->mu);
+  int n = 0;
+  while (!rt->launch_events.empty() && n < max) {
+    auto pr = rt->launch_events.front();
+    const cudaError_t q = cudaEventQuery(pr.second);
+    if (q == cudaErrorNotReady) break;
+    if (q != cudaSuccess) return -fail(GPUOS_ERR_CUDA, "launch timing: %s", cudaGetErrorString(q));
+    float ms = 0.f;
+    const cudaError_t e = cudaEventElapsedTime(&ms, pr.first, pr.second);
+    if (e != cudaSuccess) return -fail(GPUOS_ERR_CUDA, "launch timing: %s", cudaGetErrorString(e));
+    if (ms_out) ms_out[n] = ms;
+    ++n;
+    rt->launch_events.pop_front();
+    rt->spare_events.push_back(pr.first);
+    rt->spare_events.push_back(pr.second);
+  }
+  return n;
+}
 
 extern "C" uint64_t gpuos_rt_launches(gpuos_rt* rt) {
   if (!rt) return 0;

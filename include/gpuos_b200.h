@@ -277,6 +277,13 @@ int gpuos_rt_flush_times(gpuos_rt* rt, uint64_t seq, uint64_t* t_start, uint64_t
 cudaStream_t gpuos_rt_kernel_stream(gpuos_rt* rt);
 uint64_t gpuos_rt_launches(gpuos_rt* rt);
 
+/* Launch timing: while on, every worker launch is bracketed by two CUDA events recorded on
+ * the worker's stream right before and after the launch.  gpuos_rt_launch_times writes the
+ * durations (ms) of up to `max` finished launches, oldest first, drops them, and returns
+ * their number (negative status on error). */
+int gpuos_rt_set_launch_timing(gpuos_rt* rt, int on);
+int gpuos_rt_launch_times(gpuos_rt* rt, float* ms_out, int max);
+
 /* Per-CTA cycle counters of the last worker launch (valid once it has exited, e.g.
  * after gpuos_rt_quiesce): rows of 12 counters (stage wait, claim, idle, descriptor
  * fetch, staging, items staged, fill wait, tile, completer wait, completion, bulk-copy
