@@ -73,6 +73,21 @@ def peaks():
         return 6650.0, "fallback"
 
 
+def rank_max(dist, x: float, device: str) -> float:
+    """Max of a per-rank timing over all ranks (identity without a process group)."""
+    if dist is None:
+        return x
+    t = torch.tensor([x], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def job_rate(units_per_rank: float, world: int, elapsed_ms: float) -> float:
+    """Whole-job rate under weak scaling: every rank processed `units_per_rank` units, and the job
+    took the slowest rank's time."""
+    return units_per_rank * world / (elapsed_ms / 1e3)
+
+
 def profiled_traffic():
     """DRAM bytes (read + write) of one worker launch on this workload, from the committed ncu
     summary (profiles/gpuos_batch_worker_c1_drain.json), or None."""
@@ -289,10 +304,8 @@ def main():
     def max_over_ranks(x: float) -> float:
         if dist is None:
             return x
-        g.quiesce()
-        t = torch.tensor([x], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        g.quiesce()  # the collective needs SMs that a running worker holds
+        return rank_max(dist, x, "cuda")
 
     for _ in range(max(3, args.warmup)):
         step()
@@ -314,7 +327,7 @@ def main():
     clk = clocks.stop()
     launches = g.launches() - n_launch0
     elapsed_ms = max_over_ranks(e0.elapsed_time(e1))
-    value = R * args.steps * world / (elapsed_ms / 1e3)
+    value = job_rate(R * args.steps, world, elapsed_ms)
     dev_ns = []
     for s in seqs:
         try:
@@ -383,7 +396,7 @@ def main():
         f1.record()
         f1.synchronize()
         e2e_ms = max_over_ranks(f0.elapsed_time(f1))
-        line["e2e"] = {"value": R * args.steps * world / (e2e_ms / 1e3), "unit": UNIT,
+        line["e2e"] = {"value": job_rate(R * args.steps, world, e2e_ms), "unit": UNIT,
                        "h2d_bytes_per_step": 2 * R * N * 4, "d2h_bytes_per_step": R * N * 4,
                        "correct": bool(torch.equal(hO, ref))}
 
