@@ -60,6 +60,15 @@ def _worker_obj(force: bool, verbose: bool) -> str:
     return out
 
 
+def _expr_obj(force: bool, verbose: bool) -> str:
+    src = os.path.join(CSRC, "expr.cpp")
+    out = os.path.join(BUILD, "expr.o")
+    if force or _newer(out, [src, os.path.join(CSRC, "internal.h"), os.path.join(INCLUDE, "gpuos_b200.h")]):
+        _run(["g++", "-O2", "-std=c++17", "-fPIC", "-Wall", "-I" + INCLUDE, "-I" + CSRC,
+              "-I" + os.path.join(CUDA_HOME, "include"), "-c", src, "-o", out], verbose)
+    return out
+
+
 def _runtime_obj(force: bool, verbose: bool) -> str:
     src = os.path.join(CSRC, "runtime.cpp")
     out = os.path.join(BUILD, "runtime.o")
@@ -99,7 +108,8 @@ def build(force: bool = False, verbose: bool = False) -> None:
     with cf.ThreadPoolExecutor(max_workers=3) as ex:
         fw = ex.submit(_worker_obj, force, verbose)
         fr = ex.submit(_runtime_obj, force, verbose)
-        objs = [fw.result(), fr.result()]
+        fx = ex.submit(_expr_obj, force, verbose)
+        objs = [fw.result(), fr.result(), fx.result()]
     if force or _newer(LIB, objs):
         _run([NVCC, *ARCH, "-shared", "-Xcompiler", "-fPIC", "-cudart", "static", *objs, "-o", LIB,
               "-lpthread", "-ldl", "-lrt"], verbose)

@@ -795,6 +795,11 @@ __device__ __forceinline__ void producer_loop(const WorkerParams& P, const Worke
             }
           }
           bool want_exit = C.quit_epoch >= P.epoch;
+          if (want_exit) {
+            // the host withdraws an idle stop when it publishes work: confirm before exiting
+            C.quit_epoch = P.hc->quit_epoch;
+            want_exit = C.quit_epoch >= P.epoch;
+          }
           if (C.yield_every && ptx::ld_acquire_gpu(&dc->items_done) - dc->yield_base >= C.yield_every) want_exit = true;
           if (now - C.beat_t > C.safety_ns) want_exit = true;
           if (want_exit) {

@@ -144,6 +144,37 @@ struct alignas(32) Ticket {
 
 constexpr int kNumBatchSlots = 1024;
 
+// ---- registered expression operators ------------------------------------------------
+// register_elementwise(key, expr, arity) compiles `expr` (a C float expression in A and B)
+// on the host into a postfix program for a small stack machine; the worker evaluates it per
+// element.  Installing an operator writes a program into a device table: no module is
+// loaded while the persistent worker runs.
+constexpr int kExprMaxCode = 64;   // instructions per program
+constexpr int kExprMaxStack = 16;  // evaluation stack depth
+constexpr int kExprPrograms = 32;  // programs per device (each gets its own operator address)
+enum ExprOp : uint8_t {
+  XO_END = 0,
+  XO_A, XO_B, XO_CONST,                                        // push A, B, imm[pc]
+  XO_NEG, XO_NOT,                                              // unary operators
+  XO_ADD, XO_SUB, XO_MUL, XO_DIV,                              // arithmetic
+  XO_LT, XO_LE, XO_GT, XO_GE, XO_EQ, XO_NE, XO_AND, XO_OR,     // comparisons, logic (1 / 0)
+  XO_SELECT,                                                   // c ? x : y  (pops y, x, c)
+  XO_EXP, XO_LOG, XO_LOG1P, XO_EXPM1, XO_SQRT, XO_RSQRT, XO_ABS, XO_TANH, XO_SIN, XO_COS,
+  XO_TAN, XO_ERF, XO_FLOOR, XO_CEIL, XO_TRUNC, XO_ROUND, XO_EXP2, XO_LOG2, XO_LOG10,
+  XO_SINH, XO_COSH, XO_ASIN, XO_ACOS, XO_ATAN,                 // one-argument functions
+  XO_MIN, XO_MAX, XO_POW, XO_FMOD, XO_ATAN2, XO_COPYSIGN,      // two-argument functions
+  XO_NUM
+};
+struct ExprProg {
+  uint8_t code[kExprMaxCode];
+  float imm[kExprMaxCode];  // constant of an XO_CONST at the same index
+  int32_t len;
+  int32_t arity;
+  int32_t depth;            // stack slots the program needs
+  int32_t _pad;
+};
+static_assert(sizeof(ExprProg) == 336, "ExprProg layout");
+
 // Per-CTA cycle counters (clock64) of one launch, written when the CTA exits.
 enum DiagSlot {
   DG_P_WAIT_EMPTY = 0,  // dequeue warp: waiting for a free stage

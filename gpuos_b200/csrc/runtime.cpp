@@ -40,6 +40,10 @@ extern "C" cudaError_t gpuos_internal_launch_batch_worker(const WorkerParams* p,
 extern "C" cudaError_t gpuos_internal_set_worker_smem(size_t smem);
 extern "C" cudaError_t gpuos_internal_table_ptrs(void** table, void** alias);
 extern "C" cudaError_t gpuos_internal_preload_kernels();
+extern "C" cudaError_t gpuos_internal_set_expr_prog(int k, const void* prog, cudaStream_t s);
+namespace gpuos {
+int expr_compile(const char* expr, int arity, ExprProg* out, std::string* err);
+}
 extern "C" size_t gpuos_internal_smem_header_bytes();
 
 // ---- errors -----------------------------------------------------------------------------
@@ -653,6 +657,7 @@ struct gpuos_rt {
   std::thread keeper;
   std::atomic<bool> stop{false};
   int next_slot = 20;
+  int next_expr = 0;  // expression programs installed on this device
   int verbose = 0;
 };
 
@@ -1498,15 +1503,48 @@ extern "C" int gpuos_rt_register_builtin_ew(gpuos_rt* rt, int ew_op, int* slot) 
   return register_builtin_code(rt, 100 + ew_op, slot);
 }
 
+// register_elementwise for an expression that is not a built-in operator
+// (gpuos_ext.cpp:814-881): compile it into a program, write the program into the next free
+// device program entry, then point `slot` at that entry's operator.  Nothing is loaded while
+// the worker runs, so no worker needs to stop (the reference's module load waits for it).
 extern "C" int gpuos_rt_register_expr(gpuos_rt* rt, const char* key, const char* expr, int arity, int slot,
                                       int* slot_out) {
-  (void)key;
-  (void)expr;
-  (void)arity;
-  (void)slot;
-  (void)slot_out;
+  (void)key;  // the key -> slot registry lives with the caller (the Python module caches it)
   if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
-  return fail(GPUOS_ERR_UNSUPPORTED, "NVRTC operator injection is not available in this build");
+  if (slot >= GPUOS_MAX_OPS) return fail(GPUOS_ERR_INVALID, "slot %d out of range", slot);
+  ExprProg prog;
+  std::string err;
+  int e = expr_compile(expr, arity, &prog, &err);
+  if (e) return fail(e, "expression '%s': %s", expr ? expr : "", err.c_str());
+  int k, s;
+  {
+    std::lock_guard<std::mutex> lk(rt->mu);
+    if (rt->next_expr >= kExprPrograms)
+      return fail(GPUOS_ERR_FULL, "all %d expression operators of this device are in use", kExprPrograms);
+    if (slot < 0 && rt->next_slot >= GPUOS_MAX_OPS) return fail(GPUOS_ERR_FULL, "op table full (%d slots)", GPUOS_MAX_OPS);
+    k = rt->next_expr++;
+    s = slot >= 0 ? slot : rt->next_slot++;
+  }
+  CK(cudaSetDevice(rt->device));
+  CK(gpuos_internal_set_expr_prog(k, &prog, rt->cstream));
+  OpPtrInt addr = 0;
+  CK(gpu_get_builtin_op_async(200 + k, &addr, rt->cstream));
+  CK(cudaStreamSynchronize(rt->cstream));
+  if (!addr) return fail(GPUOS_ERR_CUDA, "expression operator %d has no address", k);
+  e = gpuos_rt_set_slot(rt, s, addr);
+  if (e) return e;
+  if (slot_out) *slot_out = s;
+  return GPUOS_OK;
+}
+
+extern "C" int gpuos_expr_compile(const char* expr, int arity, void* prog_out, int prog_bytes) {
+  if (prog_out && prog_bytes < (int)sizeof(ExprProg)) return fail(GPUOS_ERR_INVALID, "program buffer smaller than %zu bytes", sizeof(ExprProg));
+  ExprProg prog;
+  std::string err;
+  const int e = expr_compile(expr, arity, &prog, &err);
+  if (e) return fail(e, "expression '%s': %s", expr ? expr : "", err.c_str());
+  if (prog_out) std::memcpy(prog_out, &prog, sizeof(prog));
+  return GPUOS_OK;
 }
 
 // ---- planning hooks -----------------------------------------------------------------------

@@ -12,6 +12,7 @@
 #include "device/ops.cuh"
 #include "device/tiles.cuh"
 #include "device/refops.cuh"
+#include "device/expr.cuh"
 #include "device/worker.cuh"
 
 namespace gpuos {
@@ -49,12 +50,21 @@ __global__ void init_builtin_ops_kernel() {
   if (idx == kBatchSlot) g_op_table[kBatchSlot] = op_batch;
 }
 
+// Operator addresses of the expression programs (one per program index).
+__device__ OpFn g_expr_fns[kExprPrograms] = {
+    op_expr<0>,  op_expr<1>,  op_expr<2>,  op_expr<3>,  op_expr<4>,  op_expr<5>,  op_expr<6>,  op_expr<7>,
+    op_expr<8>,  op_expr<9>,  op_expr<10>, op_expr<11>, op_expr<12>, op_expr<13>, op_expr<14>, op_expr<15>,
+    op_expr<16>, op_expr<17>, op_expr<18>, op_expr<19>, op_expr<20>, op_expr<21>, op_expr<22>, op_expr<23>,
+    op_expr<24>, op_expr<25>, op_expr<26>, op_expr<27>, op_expr<28>, op_expr<29>, op_expr<30>, op_expr<31>};
+
 __global__ void builtin_addr_kernel(int which, unsigned long long* out) {
   if (which == -1) *out = reinterpret_cast<unsigned long long>(&op_add);
   else if (which == -2) *out = reinterpret_cast<unsigned long long>(&op_mul);
   else if (which == -3) *out = reinterpret_cast<unsigned long long>(&op_batch);
   else if (which >= 0 && which < GPUOS_EW_NUM_OPS + 2)
     *out = reinterpret_cast<unsigned long long>(g_builtin_ref_ops[which]);
+  else if (which >= 1000 && which < 1000 + kExprPrograms)
+    *out = reinterpret_cast<unsigned long long>(g_expr_fns[which - 1000]);
   else *out = 0ull;
 }
 
@@ -239,6 +249,7 @@ extern "C" cudaError_t gpu_get_builtin_op_async(int slot, OpPtrInt* out, cudaStr
   else if (slot == 1) which = -2;
   else if (slot == kBatchSlot) which = -3;
   else if (slot >= 100 && slot < 100 + GPUOS_EW_NUM_OPS + 2) which = slot - 100;
+  else if (slot >= 200 && slot < 200 + kExprPrograms) which = 1000 + (slot - 200);
   else which = -100;
   unsigned long long* d = nullptr;
   cudaError_t e = cudaMallocAsync(&d, sizeof(*d), s);
@@ -265,6 +276,13 @@ extern "C" cudaError_t gpuos_internal_table_ptrs(void** table, void** alias) {
   cudaError_t e = cudaGetSymbolAddress(table, g_op_table);
   if (e != cudaSuccess) return e;
   return cudaGetSymbolAddress(alias, g_op_alias);
+}
+
+// Write expression program k (host copy) into the device table, stream-ordered on s.
+extern "C" cudaError_t gpuos_internal_set_expr_prog(int k, const void* prog, cudaStream_t s) {
+  if (k < 0 || k >= kExprPrograms) return cudaErrorInvalidValue;
+  return cudaMemcpyToSymbolAsync(g_expr_progs, prog, sizeof(ExprProg), (size_t)k * sizeof(ExprProg),
+                                 cudaMemcpyHostToDevice, s);
 }
 
 extern "C" size_t gpuos_internal_smem_header_bytes() { return (sizeof(SmemHeader) + 127) & ~size_t(127); }

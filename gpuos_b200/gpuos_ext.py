@@ -7,11 +7,14 @@ adds the registry-style calls that the reference implements next to them:
 
 * ``register_elementwise(key, expr, arity)`` (gpuos_ext.cpp:870-881): expressions with
   the exact semantics of a built-in operator map to that operator's reference-ABI device
-  function; any other expression is compiled by NVRTC for sm_100a (``register_expr``).
+  function; any other C float expression is compiled on the host into a program for the
+  worker's expression interpreter (``register_expr``), so registering never loads a module
+  next to the running worker.
 * ``register_reduce(key, op_name)`` (gpuos_ext.cpp:1003-1014): built-in sum/mean.
 * ``register_topk`` / ``submit_topk`` (gpuos_ext.cpp:1050-1071): slot 42; values are
   produced by ``torch.topk`` as in the reference (top-k is not on the batched path).
-* ``load_and_register_custom(ptx, entry_name, slot)`` (gpuos_ext.cpp:1079-1088).
+* ``load_and_register_custom(ptx, entry_name, slot)`` (gpuos_ext.cpp:1079-1088): not
+  provided; raises NotImplementedError.
 
 Importing this module without the compiled extension raises ImportError: there is no CPU
 or PyTorch fallback for the runtime itself.
@@ -111,9 +114,11 @@ def submit_topk(slot: int, x, values, indices, k: int, dim: int, largest: bool, 
 
 
 def load_and_register_custom(ptx: str, entry_name: str, slot: int) -> None:
-    """Load PTX that defines ``extern "C" __device__ void <entry_name>(const Task&)`` and
-    place it in ``slot``."""
-    raise NotImplementedError("custom PTX injection is not available in this build")
+    """Not provided.  Calling an operator of a separately loaded module from the persistent
+    worker hung the worker on B200 in this build's tests, so operators are not injected as
+    machine code; use ``register_elementwise`` with an expression instead."""
+    raise NotImplementedError("custom PTX operators are not supported; register an expression with "
+                              "register_elementwise instead")
 
 
 def reset_registry() -> None:

@@ -112,10 +112,12 @@ cudaError_t gpu_set_debug_level_async(int level, cudaStream_t s);
 /* persistent_kernel.cu:267-269 — ring worker exits after every `every` Tasks. */
 cudaError_t gpu_set_yield_every_async(unsigned long long every, cudaStream_t s);
 
-/* Device address of the built-in operator installed in `slot` by
- * launch_init_builtin_ops (0 if none).  The reference tests obtain such
- * addresses through NVRTC modules (test/dual_slot_switch.cpp:78-102); this
- * returns the built-in ones so a slot can be refilled after a swap. */
+/* Device address of a built-in operator (0 if none): codes 0, 1, 10 are the operators
+ * launch_init_builtin_ops installs (add, mul, batch); 100+k the reference-ABI element-wise
+ * operator k, then sum and mean; 200+k the operator of expression program k.  The
+ * reference tests obtain such addresses through NVRTC modules
+ * (test/dual_slot_switch.cpp:78-102); this returns the built-in ones so a slot can be
+ * refilled after a swap. */
 cudaError_t gpu_get_builtin_op_async(int slot, OpPtrInt* out, cudaStream_t s);
 
 /* Bound for the ring worker's idle wait (reference worker: unbounded,
@@ -260,12 +262,24 @@ int gpuos_rt_get_alias(gpuos_rt* rt, int logical, int* physical);
 int gpuos_rt_register_builtin_reduce(gpuos_rt* rt, int red_op, int* slot);
 int gpuos_rt_register_builtin_ew(gpuos_rt* rt, int ew_op, int* slot);
 
-/* NVRTC operator injection for sm_100a (gpuos_ext.cpp:814-881): `expr` is a C
- * float expression in A (and B when arity == 2).  The worker is quiesced, a new
- * worker module containing the operator is compiled and loaded, and the operator is
- * placed in `slot` (slot < 0: next free slot >= 20).  *slot_out receives the slot. */
+/* register_elementwise for expressions that are not a built-in operator
+ * (gpuos_ext.cpp:814-881, there NVRTC): `expr` is a C float expression in A (and B when
+ * arity == 2) — literals, + - * /, comparisons, ! && ||, ?:, (float) casts and the float
+ * functions exp log log1p expm1 sqrt rsqrt fabs tanh sin cos tan erf floor ceil trunc round
+ * exp2 log2 log10 sinh cosh asin acos atan fmin fmax pow fmod atan2 copysign (with or
+ * without the f suffix).  It is compiled on the host into a program for the worker's stack
+ * machine (at most 64 steps, 16 stack slots) and becomes a reference-ABI operator: element i
+ * of out = expr of element i of in0/in1 under the Task's broadcast strides, computed in float
+ * and stored as out's dtype.  Up to 32 expressions per device; the operator goes to `slot`
+ * (< 0: next free slot >= 20), *slot_out receives the slot.  No module is loaded, so a
+ * running worker keeps running. */
 int gpuos_rt_register_expr(gpuos_rt* rt, const char* key, const char* expr, int arity,
                            int slot, int* slot_out);
+
+/* Compile-only check of a gpuos_rt_register_expr expression (no device needed).  With
+ * prog_out non-NULL (prog_bytes >= 336) the program is copied out: code[64] (uint8 opcodes),
+ * imm[64] (float constants), then int32 len, arity, depth. */
+int gpuos_expr_compile(const char* expr, int arity, void* prog_out, int prog_bytes);
 
 /* Device %globaltimer stamps of a completed flush: start of its first item and end
  * of its last item (ns).  Returns GPUOS_ERR_INVALID if `seq` is not complete or has
