@@ -140,11 +140,9 @@ __device__ __forceinline__ void compute_loop(const WorkerParams& P, const Worker
       }
     }
   } flush_diag{P, ctid, dg, &n_items};
-  const uint32_t shift = __ffs(S) - 1;  // S is a power of two
-  for (uint64_t iter = 0;; ++iter) {
+  uint32_t s = 0, parity = 0;  // stage and phase parity of use `iter` (stages are used in order)
+  for (uint64_t iter = 0;; ++iter, s = s + 1 == S ? 0 : s + 1, parity ^= s == 0 ? 1u : 0u) {
     unsigned long long c0 = clock64();
-    const uint32_t s = (uint32_t)iter & (S - 1);
-    const uint32_t parity = (uint32_t)(iter >> shift) & 1;
     if (!wait_phase(ptx::smem_addr(&H.full[s]), parity, &H.prod_alive, H.full_wait_ns)) {
       report_error(P, DE_WAIT_FULL, iter);
       return;
@@ -192,15 +190,13 @@ __device__ __forceinline__ void compute_loop(const WorkerParams& P, const Worker
 __device__ __forceinline__ void completer_loop(const WorkerParams& P, const WorkerShared& W, uint32_t lane) {
   SmemHeader& H = *W.H;
   const uint32_t S = P.stages;
-  const uint32_t shift = __ffs(S) - 1;
   DoneRun runs[kMaxRuns];
   int nruns = 0;
   bool first_account = true;
   uint32_t pending = 0;
   unsigned long long t_wait = 0, t_acc = 0, n_items = 0;
-  for (uint64_t iter = 0;; ++iter) {
-    const uint32_t s = (uint32_t)iter & (S - 1);
-    const uint32_t parity = (uint32_t)(iter >> shift) & 1;
+  uint32_t s = 0, parity = 0;  // stage and phase parity of use `iter`
+  for (uint64_t iter = 0;; ++iter, s = s + 1 == S ? 0 : s + 1, parity ^= s == 0 ? 1u : 0u) {
     int kind = 0;
     uint32_t batch = 0, batch_items = 0, batch_seq = 0;
     if (lane == 0) {
@@ -291,7 +287,19 @@ struct ProdState {
   uint32_t n_fetched;   // the ahead chunk's descriptors are being copied into dcache[cur ^ 1]
   uint32_t cur;         // dcache buffer of the current chunk
   uint32_t last_seq;    // flush of the last staged item (start stamp once per flush)
+  uint32_t stage;       // stage of use `iter`
+  uint32_t phase;       // phase parity of use `iter` ((iter / S) & 1)
 };
+
+// Advance the stage cursor of the dequeue warp by n uses (n <= S).
+__device__ __forceinline__ void advance(ProdState& st, uint32_t n, uint32_t S) {
+  st.iter += n;
+  st.stage += n;
+  if (st.stage >= S) {
+    st.stage -= S;
+    st.phase ^= 1u;
+  }
+}
 
 __device__ __forceinline__ void publish_diag(const WorkerParams& P, const ProdCold& C) {
   ptx::st_relaxed_sys(&P.rep->heartbeat, C.polls);
@@ -305,17 +313,12 @@ __device__ __forceinline__ void publish_diag(const WorkerParams& P, const ProdCo
   ptx::st_relaxed_sys(&P.rep->host_read_ns_avg, C.read_n ? C.read_sum / C.read_n : 0);
 }
 
-// Phase parity that the empty barrier of stage use `u` (u >= S) completes once use u - S
-// has been released.
-__device__ __forceinline__ uint32_t empty_parity(uint64_t u, uint32_t S) {
-  return (uint32_t)(((u >> (__ffs(S) - 1)) - 1) & 1);
-}
-
-// Wait (lane 0) until compute warps released stage use `use` (i.e. iteration use-1 done).
-__device__ __forceinline__ bool wait_empty(const WorkerParams& P, SmemHeader& H, uint64_t iter, uint32_t S) {
+// Wait (lane 0) until stage `s` is free for use `iter` (whose phase parity is `phase`): the
+// empty barrier of the stage completes phase (iter / S - 1) once use iter - S is released.
+__device__ __forceinline__ bool wait_empty(const WorkerParams& P, SmemHeader& H, uint64_t iter, uint32_t s,
+                                           uint32_t phase, uint32_t S) {
   if (iter < S) return true;
-  const uint32_t s = (uint32_t)iter & (S - 1);
-  const uint32_t parity = empty_parity(iter, S);
+  const uint32_t parity = phase ^ 1u;
   const uint32_t bar = ptx::smem_addr(&H.empty[s]);
   const uint64_t t0 = ptx::now_ns();
   uint32_t spins = 0;
@@ -337,8 +340,8 @@ __device__ __forceinline__ bool drain_own(const WorkerParams& P, SmemHeader& H, 
   const uint64_t lo = iter > S ? iter - S : 0;
   for (uint64_t u = lo; u < iter; ++u) {
     // use u was released when the empty barrier of its stage completed phase (u / S)
-    const uint32_t s = (uint32_t)u & (S - 1);
-    const uint32_t parity = (uint32_t)((u >> (__ffs(S) - 1)) & 1);
+    const uint32_t s = (uint32_t)(u % S);
+    const uint32_t parity = (uint32_t)((u / S) & 1);
     const uint32_t bar = ptx::smem_addr(&H.empty[s]);
     const uint64_t t0 = ptx::now_ns();
     uint32_t spins = 0;
@@ -542,7 +545,7 @@ __device__ __forceinline__ void stage_copies(const WorkerShared& W, StageMeta& m
 __device__ __forceinline__ bool stage_item(const WorkerParams& P, const WorkerShared& W, ProdState& st, uint32_t lane) {
   SmemHeader& H = *W.H;
   const uint32_t S = P.stages;
-  const uint32_t s = (uint32_t)st.iter & (S - 1);
+  const uint32_t s = st.stage;
   StageMeta& m = H.meta[s];
   if (lane == 0 && st.iter == 0) tl_mark(P, TL_STAGE);
   if (lane < 4) {
@@ -624,7 +627,7 @@ __device__ __forceinline__ bool stage_item(const WorkerParams& P, const WorkerSh
     fn(m.ext.task);
     ptx::named_bar_sync(kBarTask, blockDim.x);
   }
-  st.iter += 1;
+  advance(st, 1, S);
   st.ticket += 1;
   return true;
 }
@@ -644,8 +647,12 @@ __device__ __forceinline__ uint32_t stage_group(const WorkerParams& P, const Wor
   if (lane < navail) {
     it = H.dcache[st.cur][(st.ticket + lane) & 7];
     const uint64_t u = st.iter + lane;
-    const bool free = lane == 0 || u < S ||
-                      ptx::mbar_test_wait(ptx::smem_addr(&H.empty[(uint32_t)u & (S - 1)]), empty_parity(u, S));
+    uint32_t su = st.stage + lane, ph = st.phase;
+    if (su >= S) {
+      su -= S;
+      ph ^= 1u;
+    }
+    const bool free = lane == 0 || u < S || ptx::mbar_test_wait(ptx::smem_addr(&H.empty[su]), ph ^ 1u);
     ok = free && group_kind(it) && it.wait_items <= st.items_done_cache;
   } else {
     it.batch_seq = 0;
@@ -655,7 +662,7 @@ __device__ __forceinline__ uint32_t stage_group(const WorkerParams& P, const Wor
   if (g == 0) return 0;
   const uint32_t prev_seq = __shfl_up_sync(0xffffffffu, it.batch_seq, 1);
   if (lane < g) {
-    const uint32_t s = (uint32_t)(st.iter + lane) & (S - 1);
+    const uint32_t s = st.stage + lane < S ? st.stage + lane : st.stage + lane - S;
     StageMeta& m = H.meta[s];
     m.item = it;
     // start stamp of the flush: the first item each CTA stages from it is enough
@@ -669,7 +676,7 @@ __device__ __forceinline__ uint32_t stage_group(const WorkerParams& P, const Wor
     tl_mark(P, TL_TMA);
   }
   __syncwarp();
-  st.iter += g;
+  advance(st, g, S);
   st.ticket += g;
   return g;
 }
@@ -689,6 +696,8 @@ __device__ __forceinline__ void producer_loop(const WorkerParams& P, const Worke
   st.n_fetched = 0;
   st.cur = 0;
   st.last_seq = 0;
+  st.stage = 0;
+  st.phase = 0;
   st.tail_cache = ptx::ld_acquire_gpu(&dc->tail_mirror);
   st.items_done_cache = 0;
   if (lane == 0) {
@@ -712,7 +721,7 @@ __device__ __forceinline__ void producer_loop(const WorkerParams& P, const Worke
     uint32_t switched = 0, issue = 0;
     if (lane == 0) {
       unsigned long long c0 = clock64();
-      const bool empty_ok = wait_empty(P, H, st.iter, S);
+      const bool empty_ok = wait_empty(P, H, st.iter, st.stage, st.phase, S);
       unsigned long long c1 = clock64();
       C.dg[DG_P_WAIT_EMPTY] += c1 - c0;
       if (!empty_ok) {
@@ -828,8 +837,8 @@ __device__ __forceinline__ void producer_loop(const WorkerParams& P, const Worke
     action = __shfl_sync(0xffffffffu, action, 0);
     if (action == 1) {
       if (lane == 0) {
-        wait_empty(P, H, st.iter, S);
-        arm_exit(H, (uint32_t)st.iter & (S - 1));
+        wait_empty(P, H, st.iter, st.stage, st.phase, S);
+        arm_exit(H, st.stage);
       }
       break;
     }

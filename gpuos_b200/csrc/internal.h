@@ -191,7 +191,7 @@ enum DiagSlot {
   DG_CYCLES,            // total cycles of the CTA
   kDiagSlots = 12
 };
-constexpr int kDiagCtas = 256;
+constexpr int kDiagCtas = 512;  // worker CTAs per launch stay below this (one row per CTA + timeline)
 
 // Launch timeline: %globaltimer stamps of the first occurrence of each event in the last
 // worker launch, kept in diag row gridDim.x (the row after the last CTA's).

@@ -40,6 +40,7 @@ extern "C" cudaError_t gpuos_internal_launch_batch_worker(const WorkerParams* p,
 extern "C" cudaError_t gpuos_internal_set_worker_smem(size_t smem);
 extern "C" cudaError_t gpuos_internal_table_ptrs(void** table, void** alias);
 extern "C" cudaError_t gpuos_internal_preload_kernels();
+extern "C" cudaError_t gpuos_internal_worker_occupancy(int threads, size_t smem, int* blocks);
 extern "C" cudaError_t gpuos_internal_set_expr_prog(int k, const void* prog, cudaStream_t s);
 namespace gpuos {
 int expr_compile(const char* expr, int arity, ExprProg* out, std::string* err);
@@ -658,8 +659,21 @@ struct gpuos_rt {
   std::atomic<bool> stop{false};
   int next_slot = 20;
   int next_expr = 0;  // expression programs installed on this device
+  int ctas_per_sm = 1;  // worker CTAs resident per SM (each with its own dequeue warp)
+  int grid = 0;         // worker CTAs per launch
+  int cta_threads = 0;  // compute threads per worker CTA
   int verbose = 0;
 };
+
+// Stages of the worker's ring: as many as shared memory holds (GPUOS_STAGES caps it), 2 to
+// kMaxStages.  Every staged item keeps its operand loads in flight, so more stages keep more
+// bytes in flight per SM.
+static uint32_t pick_stages(size_t smem_cap, size_t stage_bytes) {
+  const int want = std::max(2, std::min(kMaxStages, env_int("GPUOS_STAGES", kMaxStages)));
+  uint32_t S = (uint32_t)want;
+  while (S > 2 && gpuos_internal_smem_header_bytes() + S * stage_bytes > smem_cap) --S;
+  return S;
+}
 
 static std::mutex g_rt_mu;
 static std::map<int, gpuos_rt*> g_rts;
@@ -741,7 +755,7 @@ static int launch_worker_locked(gpuos_rt* rt) {
   P.epoch = ep;
   P.stages = rt->stages;
   P.stage_bytes = rt->stage_bytes;
-  P.compute_threads = (uint32_t)rt->tpb;
+  P.compute_threads = (uint32_t)rt->cta_threads;
   P.wait_limit_ns = rt->hc->wait_limit_ns;
   CK(cudaSetDevice(rt->device));
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
@@ -757,7 +771,7 @@ static int launch_worker_locked(gpuos_rt* rt) {
     CK(cudaEventRecord(ev0, rt->kstream));
   }
   // one dequeue warp + one completer warp + threads_per_block compute threads
-  CK(gpuos_internal_launch_batch_worker(&P, rt->sm_count, rt->tpb + 64, rt->smem, rt->kstream));
+  CK(gpuos_internal_launch_batch_worker(&P, rt->grid, rt->cta_threads + 64, rt->smem, rt->kstream));
   if (rt->time_launches) {
     CK(cudaEventRecord(ev1, rt->kstream));
     rt->launch_events.emplace_back(ev0, ev1);
@@ -938,12 +952,6 @@ extern "C" int gpuos_rt_init(int device, int capacity, int threads_per_block, gp
   rt->tpb = threads_per_block;
   rt->verbose = env_int("GPUOS_VERBOSE", 0);
   rt->idle_quiesce_ms = env_int("GPUOS_IDLE_QUIESCE_MS", 200);
-  {
-    // stage count: a power of two in [2, kMaxStages]
-    const int want = std::max(2, std::min(kMaxStages, env_int("GPUOS_STAGES", 4)));
-    rt->stages = 2;
-    while ((int)rt->stages * 2 <= want) rt->stages *= 2;
-  }
   auto cleanup = [&](int code) {
     if (rt->host_block) cudaFreeHost(rt->host_block);
     if (rt->dc) cudaFree(rt->dc);
@@ -954,13 +962,21 @@ extern "C" int gpuos_rt_init(int device, int capacity, int threads_per_block, gp
   };
   cudaError_t e = cudaDeviceGetAttribute(&rt->sm_count, cudaDevAttrMultiProcessorCount, device);
   if (e != cudaSuccess) return cleanup(fail(GPUOS_ERR_CUDA, "cudaDeviceGetAttribute: %s", cudaGetErrorString(e)));
-  int smem_optin = 0;
+  int smem_optin = 0, smem_sm = 0, smem_reserved = 0;
   cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+  cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, device);
+  cudaDeviceGetAttribute(&smem_reserved, cudaDevAttrReservedSharedMemoryPerBlock, device);
+  // Worker CTAs per SM (GPUOS_CTAS_PER_SM, 1 or 2): with 2, each CTA gets half of the compute
+  // threads and half of the shared memory, and every SM runs two dequeue warps.
+  rt->ctas_per_sm = std::max(1, std::min(2, env_int("GPUOS_CTAS_PER_SM", 1)));
+  if (rt->ctas_per_sm == 2 && (threads_per_block / 2) % 32 != 0) rt->ctas_per_sm = 1;
+  rt->cta_threads = threads_per_block / rt->ctas_per_sm;
+  rt->grid = rt->sm_count * rt->ctas_per_sm;
+  if (rt->grid >= kDiagCtas) return cleanup(fail(GPUOS_ERR_UNSUPPORTED, "%d worker CTAs exceed %d", rt->grid, kDiagCtas - 1));
+  const size_t smem_cap = std::min<size_t>((size_t)smem_optin, (size_t)smem_sm / rt->ctas_per_sm - smem_reserved);
+  rt->stages = pick_stages(smem_cap, rt->stage_bytes);
   rt->smem = gpuos_internal_smem_header_bytes() + (size_t)rt->stages * rt->stage_bytes;
-  while (rt->smem > (size_t)smem_optin && rt->stages > 2) {
-    rt->stages /= 2;
-    rt->smem = gpuos_internal_smem_header_bytes() + (size_t)rt->stages * rt->stage_bytes;
-  }
+  if (rt->smem > smem_cap) return cleanup(fail(GPUOS_ERR_UNSUPPORTED, "worker needs %zu bytes of shared memory", rt->smem));
   rt->item_cap = pow2_at_least(std::max<uint64_t>((uint64_t)capacity * 8, 1u << 16));
   rt->task_cap = pow2_at_least(std::max<uint64_t>((uint64_t)capacity, 1024));
   rt->layout_cap = pow2_at_least(std::max<uint64_t>((uint64_t)capacity, 1024));
@@ -999,7 +1015,12 @@ extern "C" int gpuos_rt_init(int device, int capacity, int threads_per_block, gp
   if (e == cudaSuccess) e = gpuos_internal_table_ptrs(&rt->op_table, &rt->op_alias);
   if (e == cudaSuccess) e = gpuos_internal_set_worker_smem(rt->smem);
   if (e == cudaSuccess) e = gpuos_internal_preload_kernels();
+  int resident = 0;
+  if (e == cudaSuccess) e = gpuos_internal_worker_occupancy(rt->cta_threads + 64, rt->smem, &resident);
   if (e != cudaSuccess) return cleanup(fail(GPUOS_ERR_CUDA, "runtime setup: %s", cudaGetErrorString(e)));
+  // every worker CTA must be resident at once (the grid coordinates its exit)
+  if (resident < rt->ctas_per_sm)
+    return cleanup(fail(GPUOS_ERR_UNSUPPORTED, "%d worker CTAs per SM requested, %d fit", rt->ctas_per_sm, resident));
   rt->last_activity_ns = mono_ns();
   {
     std::lock_guard<std::mutex> lk(rt->mu);
@@ -1339,7 +1360,7 @@ extern "C" int gpuos_rt_set_yield_every(gpuos_rt* rt, uint64_t every) {
 
 extern "C" int gpuos_rt_debug_counters(gpuos_rt* rt, uint64_t* out, int n) {
   if (!rt) return -fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
-  const int ctas = std::min(rt->sm_count, kDiagCtas);
+  const int ctas = std::min(rt->grid, kDiagCtas);
   const int rows = std::min(ctas + 1, kDiagCtas);  // + the launch timeline row
   std::vector<unsigned long long> buf((size_t)rows * kDiagSlots);
   cudaError_t e = cudaSetDevice(rt->device);
@@ -1678,15 +1699,9 @@ extern "C" int gpuos_ew_batch_noalloc(const GpuosEwRequest* reqs, int nreq, int 
   CK(cudaGetDevice(&dev));
   CK(cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev));
   CK(cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
-  // same stage rule as gpuos_rt_init, so both entry points set the same shared-memory limit
-  const int want = std::max(2, std::min(kMaxStages, env_int("GPUOS_STAGES", 4)));
-  uint32_t stages = 2;
-  while ((int)stages * 2 <= want) stages *= 2;
-  size_t smem = gpuos_internal_smem_header_bytes() + (size_t)stages * kStageBytesDefault;
-  while (smem > (size_t)smem_optin && stages > 2) {
-    stages /= 2;
-    smem = gpuos_internal_smem_header_bytes() + (size_t)stages * kStageBytesDefault;
-  }
+  // same stage rule as gpuos_rt_init with one worker CTA per SM
+  const uint32_t stages = pick_stages((size_t)smem_optin, kStageBytesDefault);
+  const size_t smem = gpuos_internal_smem_header_bytes() + (size_t)stages * kStageBytesDefault;
   void* scratch = nullptr;
   size_t scratch_bytes = 0;
   CK(gpuos_internal_noalloc_scratch(smem, &scratch, &scratch_bytes));

@@ -268,8 +268,24 @@ extern "C" cudaError_t gpuos_internal_launch_batch_worker(const WorkerParams* p,
   return cudaGetLastError();
 }
 
+// Raise (never lower) the worker's dynamic shared-memory limit on the current device: the
+// runtime and the no-allocation entry point may size their launches differently.
 extern "C" cudaError_t gpuos_internal_set_worker_smem(size_t smem) {
-  return cudaFuncSetAttribute(gpuos_batch_worker, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  static std::mutex mu;
+  static size_t limit[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lk(mu);
+  if (dev >= 0 && dev < 64 && limit[dev] >= smem) return cudaSuccess;
+  e = cudaFuncSetAttribute(gpuos_batch_worker, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e == cudaSuccess && dev >= 0 && dev < 64) limit[dev] = smem;
+  return e;
+}
+
+// Worker CTAs of `threads` threads and `smem` dynamic shared memory that fit on one SM.
+extern "C" cudaError_t gpuos_internal_worker_occupancy(int threads, size_t smem, int* blocks) {
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, gpuos_batch_worker, threads, smem);
 }
 
 extern "C" cudaError_t gpuos_internal_table_ptrs(void** table, void** alias) {
@@ -292,7 +308,7 @@ extern "C" size_t gpuos_internal_smem_header_bytes() { return (sizeof(SmemHeader
 // words, ticket, layouts and tile descriptors of its one-shot worker launch live in this array,
 // which every device that loads the library holds until the process exits.  In host code the
 // name stands in for the array only; its device address comes from cudaGetSymbolAddress.
-static_assert(StaticScratch::kBytes == 1115904, "the documented scratch size has changed");
+static_assert(StaticScratch::kBytes == 1142528, "the documented scratch size has changed");
 static __device__ __align__(256) unsigned char g_noalloc_scratch[StaticScratch::kBytes];
 
 namespace {

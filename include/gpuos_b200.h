@@ -328,8 +328,8 @@ int gpuos_plan_reduce(int red_op, const GpuosOperand* x, const GpuosOperand* out
  * implicit device synchronisation.  gpuos_ew_batch_noalloc runs the same worker kernel as
  * gpuos_rt_submit_ew + gpuos_rt_flush, once, on `stream`, over `nreq` element-wise requests,
  * with all of its scratch (control words, completion ticket, tile descriptors, strided
- * layouts) in one fixed array of device memory that is part of this library: 1,115,904 bytes
- * (1.06 MiB) per device, held by every device that loads the library until the process exits.  It calls
+ * layouts) in one fixed array of device memory that is part of this library: 1,142,528 bytes
+ * (1.09 MiB) per device, held by every device that loads the library until the process exits.  It calls
  * no cudaMalloc, cudaFree or other allocating routine.
  *
  * Limits: the requests together may be split into at most GPUOS_NOALLOC_MAX_TILES tiles
