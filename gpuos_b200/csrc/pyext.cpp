@@ -22,6 +22,9 @@
 #include <deque>
 #include <string>
 #include <utility>
+#include <atomic>
+#include <chrono>
+#include <thread>
 #include <vector>
 
 #include "gpuos_b200.h"
@@ -36,6 +39,13 @@ struct DevRefs {
 };
 
 gpuos_rt* g_rt[kMaxDev] = {nullptr};
+// Calls that run with the GIL released while they use a runtime; shutdown waits for them.
+std::atomic<int> g_busy[kMaxDev];
+struct Busy {
+  int d;
+  explicit Busy(int dev) : d(dev) { g_busy[d].fetch_add(1); }
+  ~Busy() { g_busy[d].fetch_sub(1); }
+};
 DevRefs g_refs[kMaxDev];
 int g_verbose = 0;
 
@@ -49,9 +59,11 @@ PyObject* raise_status(int st) {
   return nullptr;
 }
 
-void release_list(std::vector<PyObject*>& v) {
+// Dropping a reference can run arbitrary Python code (finalizers, weakref callbacks, the
+// garbage collector) and let another thread run, which may flush and touch g_refs.  So the
+// references are first taken out of the shared lists, and dropped afterwards.
+void drop_refs(std::vector<PyObject*>& v) {
   for (PyObject* o : v) Py_DECREF(o);
-  v.clear();
 }
 
 void release_completed(int dev) {
@@ -59,19 +71,25 @@ void release_completed(int dev) {
   DevRefs& R = g_refs[dev];
   if (R.inflight.empty()) return;
   const uint64_t done = rt ? gpuos_rt_completed(rt) : ~0ull;
+  std::vector<PyObject*> dead;
   while (!R.inflight.empty() && R.inflight.front().first <= done) {
-    release_list(R.inflight.front().second);
+    auto& v = R.inflight.front().second;
+    dead.insert(dead.end(), v.begin(), v.end());
     R.inflight.pop_front();
   }
+  drop_refs(dead);
 }
 
 void release_all(int dev) {
   DevRefs& R = g_refs[dev];
-  release_list(R.pending);
+  std::vector<PyObject*> dead;
+  dead.swap(R.pending);
   while (!R.inflight.empty()) {
-    release_list(R.inflight.front().second);
+    auto& v = R.inflight.front().second;
+    dead.insert(dead.end(), v.begin(), v.end());
     R.inflight.pop_front();
   }
+  drop_refs(dead);
 }
 
 int dtype_code(c10::ScalarType st) {
@@ -301,6 +319,7 @@ int flush_device(int dev, bool sync, uint64_t* seq_out) {
   if (st) return st;
   move_pending(dev, seq);
   if (sync && seq) {
+    Busy busy(dev);
     Py_BEGIN_ALLOW_THREADS st = gpuos_rt_wait(rt, seq, 30000);
     Py_END_ALLOW_THREADS
   }
@@ -380,11 +399,13 @@ PyObject* py_init(PyObject*, PyObject* args, PyObject* kw) {
 int shutdown_device(int dev) {
   gpuos_rt* rt = g_rt[dev];
   if (!rt) return 0;
+  g_rt[dev] = nullptr;  // later calls see "not initialized"; calls in flight finish first
   move_pending(dev, 0);
   int st;
-  Py_BEGIN_ALLOW_THREADS st = gpuos_rt_shutdown(rt);
+  Py_BEGIN_ALLOW_THREADS
+  while (g_busy[dev].load() > 0) std::this_thread::sleep_for(std::chrono::microseconds(50));
+  st = gpuos_rt_shutdown(rt);
   Py_END_ALLOW_THREADS
-  g_rt[dev] = nullptr;
   release_all(dev);
   return st;
 }
@@ -497,7 +518,9 @@ PyObject* py_quiesce(PyObject*, PyObject* args, PyObject* kw) {
       if (dev != d) continue;
     }
     int st;
-    Py_BEGIN_ALLOW_THREADS st = gpuos_rt_quiesce(g_rt[d], timeout_ms);
+    gpuos_rt* rt = g_rt[d];
+    Busy busy(d);
+    Py_BEGIN_ALLOW_THREADS st = gpuos_rt_quiesce(rt, timeout_ms);
     Py_END_ALLOW_THREADS
     if (st) return raise_status(st);
   }
@@ -578,9 +601,11 @@ PyObject* py_sync_wait(PyObject*, PyObject* args, PyObject* kw) {
   unsigned long long target;
   int timeout_ms = 30000;
   if (!PyArg_ParseTupleAndKeywords(args, kw, "K|i", const_cast<char**>(kwlist), &target, &timeout_ms)) return nullptr;
-  gpuos_rt* rt = rt_arg(nullptr, nullptr);
+  int dev = 0;
+  gpuos_rt* rt = rt_arg(nullptr, &dev);
   if (!rt) return nullptr;
   int st;
+  Busy busy(dev);
   Py_BEGIN_ALLOW_THREADS st = gpuos_rt_sync_wait(rt, target, timeout_ms);
   Py_END_ALLOW_THREADS
   if (st) return raise_status(st);
@@ -598,6 +623,7 @@ PyObject* py_wait(PyObject*, PyObject* args, PyObject* kw) {
   gpuos_rt* rt = rt_arg(devobj, &dev);
   if (!rt) return nullptr;
   int st;
+  Busy busy(dev);
   Py_BEGIN_ALLOW_THREADS st = gpuos_rt_wait(rt, seq, timeout_ms);
   Py_END_ALLOW_THREADS
   if (st) return raise_status(st);
@@ -709,10 +735,12 @@ PyObject* py_launch_times(PyObject*, PyObject* args, PyObject* kw) {
   static const char* kwlist[] = {"device", nullptr};
   PyObject* devobj = Py_None;
   if (!PyArg_ParseTupleAndKeywords(args, kw, "|O", const_cast<char**>(kwlist), &devobj)) return nullptr;
-  gpuos_rt* rt = rt_arg(devobj, nullptr);
+  int dev = 0;
+  gpuos_rt* rt = rt_arg(devobj, &dev);
   if (!rt) return nullptr;
   std::vector<float> buf(4096);
   int n;
+  Busy busy(dev);
   Py_BEGIN_ALLOW_THREADS
   n = gpuos_rt_launch_times(rt, buf.data(), (int)buf.size());
   Py_END_ALLOW_THREADS
@@ -824,9 +852,11 @@ PyObject* py_register_expr(PyObject*, PyObject* args, PyObject* kw) {
   PyObject* devobj = Py_None;
   if (!PyArg_ParseTupleAndKeywords(args, kw, "ssi|iO", const_cast<char**>(kwlist), &key, &expr, &arity, &slot, &devobj))
     return nullptr;
-  gpuos_rt* rt = rt_arg(devobj, nullptr);
+  int dev = 0;
+  gpuos_rt* rt = rt_arg(devobj, &dev);
   if (!rt) return nullptr;
   int out = -1, st;
+  Busy busy(dev);
   Py_BEGIN_ALLOW_THREADS st = gpuos_rt_register_expr(rt, key, expr, arity, slot, &out);
   Py_END_ALLOW_THREADS
   if (st) return raise_status(st);

@@ -216,8 +216,24 @@ struct Plan {
 
 constexpr uint32_t kGenericTile = 8192;
 
+// Row-major dense (every size > 1 dim has the contiguous stride).
+static bool dense(const GpuosOperand& t) {
+  int64_t expect = 1;
+  for (int d = t.ndim - 1; d >= 0; --d) {
+    if (t.sizes[d] != 1 && t.strides[d] != expect) return false;
+    expect *= t.sizes[d];
+  }
+  return true;
+}
+
+static bool same_shape(const GpuosOperand& x, const GpuosOperand& y) {
+  if (x.ndim != y.ndim) return false;
+  for (int d = 0; d < x.ndim; ++d)
+    if (x.sizes[d] != y.sizes[d]) return false;
+  return true;
+}
+
 int plan_ew(const EwReq& r, uint32_t half_bytes, Plan* p) {
-  std::string err;
   if (r.op < 0 || r.op >= GPUOS_EW_NUM_OPS) return fail(GPUOS_ERR_INVALID, "unknown element-wise op %d", r.op);
   const GpuosOperand& out = *r.out;
   if (!r.a || !dtype_ok(r.a->dtype) || !dtype_ok(out.dtype))
@@ -238,6 +254,50 @@ int plan_ew(const EwReq& r, uint32_t half_bytes, Plan* p) {
   if (n == 0) return GPUOS_OK;
   if (!out.data || !r.a->data || (b && !b->data)) return fail(GPUOS_ERR_INVALID, "null data pointer");
 
+  const int esa = dtype_size(r.a->dtype), eso = dtype_size(out.dtype);
+  const int esb = b ? dtype_size(b->dtype) : 4;
+  uint8_t base_flags = 0;
+  if (binary) base_flags |= IF_B_PRESENT;
+  if (binary && r.b_imm && !b) base_flags |= IF_B_SCALAR;
+  uint32_t bimm_u;
+  std::memcpy(&bimm_u, &r.b_val, 4);
+  const uint64_t bimm_bits = bimm_u;
+  WorkItem proto;
+  std::memset(&proto, 0, sizeof(proto));
+  proto.op = (uint8_t)r.op;
+  proto.dt_a = (uint8_t)r.a->dtype;
+  proto.dt_b = (uint8_t)(b ? b->dtype : kF32);
+  proto.dt_o = (uint8_t)out.dtype;
+  proto.aux = 0xffffffffu;
+
+  // Fast path: operands of the output's shape, all dense (the common case): one 1-D
+  // contiguous run, no broadcast, no dimension bookkeeping.
+  if (same_shape(*r.a, out) && dense(*r.a) && dense(out) && (!b || (same_shape(*b, out) && dense(*b)))) {
+    const int es_max = std::max(esa, b ? esb : 1);
+    const uint32_t tile = half_bytes / (uint32_t)es_max;
+    uint32_t p0u, p1u;
+    std::memcpy(&p0u, &r.params[0], 4);
+    std::memcpy(&p1u, &r.params[1], 4);
+    proto.kind = IK_EW_CONTIG;
+    proto.x = (uint64_t)p0u | ((uint64_t)p1u << 32);
+    proto.flags = base_flags;
+    const uint64_t A = (uint64_t)(uintptr_t)r.a->data, O = (uint64_t)(uintptr_t)out.data;
+    const uint64_t B = b ? (uint64_t)(uintptr_t)b->data : (r.b_imm ? bimm_bits : 0);
+    p->reads[p->nreads++] = Range{A, A + (uint64_t)n * esa};
+    if (b) p->reads[p->nreads++] = Range{B, B + (uint64_t)n * esb};
+    p->write = Range{O, O + (uint64_t)n * eso};
+    for (int64_t s = 0; s < n; s += tile) {
+      WorkItem it = proto;
+      it.count = (uint32_t)std::min<int64_t>(tile, n - s);
+      it.a = A + (uint64_t)s * esa;
+      it.b = b ? B + (uint64_t)s * esb : B;
+      it.o = O + (uint64_t)s * eso;
+      p->items.push_back(it);
+    }
+    return GPUOS_OK;
+  }
+
+  std::string err;
   Dims d;
   d.nd = out.ndim;
   for (int i = 0; i < out.ndim; ++i) {
@@ -265,26 +325,8 @@ int plan_ew(const EwReq& r, uint32_t half_bytes, Plan* p) {
   if (b) p->reads[p->nreads++] = operand_range(*b);
   p->write = operand_range(out);
 
-  const int esa = dtype_size(r.a->dtype), eso = dtype_size(out.dtype);
-  const int esb = b ? dtype_size(b->dtype) : 4;
-  uint8_t base_flags = 0;
-  if (binary) base_flags |= IF_B_PRESENT;
-  if (binary && r.b_imm && !b) base_flags |= IF_B_SCALAR;
-  const uint64_t bimm_bits = [&] {
-    uint32_t u;
-    std::memcpy(&u, &r.b_val, 4);
-    return (uint64_t)u;
-  }();
-
   const bool contig = d.nd == 1 && d.st[2][0] == 1 && (d.st[0][0] == 1 || d.st[0][0] == 0) &&
                       (!b || d.st[1][0] == 1 || d.st[1][0] == 0);
-  WorkItem proto;
-  std::memset(&proto, 0, sizeof(proto));
-  proto.op = (uint8_t)r.op;
-  proto.dt_a = (uint8_t)r.a->dtype;
-  proto.dt_b = (uint8_t)(b ? b->dtype : kF32);
-  proto.dt_o = (uint8_t)out.dtype;
-  proto.aux = 0xffffffffu;
   if (contig) {
     const bool a_vec = d.st[0][0] == 1;
     const bool b_vec = b && d.st[1][0] == 1;
@@ -484,12 +526,19 @@ class HazardMap {
     ++gen_;
     pool_.clear();
     large_.clear();
+    pending_.clear();
+    rbox_ = wbox_ = Range();
   }
-  size_t size() const { return pool_.size() + large_.size(); }
+  size_t size() const { return pool_.size() + large_.size() + pending_.size(); }
 
-  // true if r (read when !write) conflicts with the segment
-  bool conflicts(const Range& r, bool write) const {
+  // true if r (read when !write) conflicts with the segment.  The bounding boxes of the
+  // segment's reads and writes answer most queries; the ranges are hashed into 64 KiB
+  // buckets only once a query falls inside a box.
+  bool conflicts(const Range& r, bool write) {
     if (r.empty()) return false;
+    const bool in_w = box_overlap(wbox_, r), in_r = write && box_overlap(rbox_, r);
+    if (!in_w && !in_r) return false;
+    index_pending();
     for (const Ent& e : large_)
       if ((write || e.write) && overlap(e, r)) return true;
     const uint64_t b0 = r.lo >> kShift, b1 = (r.hi - 1) >> kShift;
@@ -510,6 +559,24 @@ class HazardMap {
 
   void insert(const Range& r, bool write) {
     if (r.empty()) return;
+    Range& box = write ? wbox_ : rbox_;
+    if (box.empty()) {
+      box = r;
+    } else {
+      box.lo = std::min(box.lo, r.lo);
+      box.hi = std::max(box.hi, r.hi);
+    }
+    pending_.push_back(Ent{r.lo, r.hi, write, -1});
+  }
+
+ private:
+  void index_pending() {
+    for (const Ent& e : pending_) index(Range{e.lo, e.hi}, e.write);
+    pending_.clear();
+  }
+  static bool box_overlap(const Range& box, const Range& r) { return !box.empty() && box.lo < r.hi && r.lo < box.hi; }
+
+  void index(const Range& r, bool write) {
     const uint64_t b0 = r.lo >> kShift, b1 = (r.hi - 1) >> kShift;
     if (b1 - b0 > kMaxBlocks) {
       large_.push_back(Ent{r.lo, r.hi, write, -1});
@@ -522,7 +589,6 @@ class HazardMap {
     }
   }
 
- private:
   static constexpr int kShift = 16;
   static constexpr uint64_t kMaxBlocks = 64;
   struct Ent {
@@ -586,6 +652,8 @@ class HazardMap {
   std::vector<Slot> table_;
   std::vector<Ent> pool_;
   std::vector<Ent> large_;
+  std::vector<Ent> pending_;  // inserted since the last query that needed the index
+  Range rbox_, wbox_;         // bounding boxes of the segment's reads and writes
   uint32_t gen_ = 1;
   uint32_t used_gen_ = 0;
   size_t used_ = 0;
@@ -1145,15 +1213,9 @@ static int wait_seq_locked(gpuos_rt* rt, std::unique_lock<std::mutex>& lk, uint6
   const uint64_t limit = (uint64_t)(timeout_ms < 0 ? 30000 : timeout_ms) * 1000000ull;
   uint32_t spins = 0;
   while (true) {
+    // flushes may finish out of order; the wait ends once `seq` and every earlier flush are done
     reap_locked(rt);
     if (rt->completed_seq >= seq) return GPUOS_OK;
-    bool seq_done = false;
-    for (const BatchInfo& b : rt->inflight)
-      if (b.seq == seq) {
-        seq_done = b.done;
-        break;
-      }
-    if (seq_done) return GPUOS_OK;
     int e = check_device_error_locked(rt);
     if (e) return e;
     if ((++spins & 1023u) == 0) {

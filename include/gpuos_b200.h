@@ -207,7 +207,8 @@ int gpuos_rt_submit_task(gpuos_rt* rt, const Task* task);
  * the flush ticket (0 when nothing was pending). */
 int gpuos_rt_flush(gpuos_rt* rt, int flags, cudaStream_t dep_stream, uint64_t* seq_out);
 
-/* Wait until flush ticket `seq` has completed, at most timeout_ms. */
+/* Wait until flush ticket `seq` and every earlier flush have completed, at most timeout_ms
+ * (flushes can finish out of order on the device). */
 int gpuos_rt_wait(gpuos_rt* rt, uint64_t seq, int timeout_ms);
 
 /* Highest ticket t such that every flush with ticket <= t has completed. */
