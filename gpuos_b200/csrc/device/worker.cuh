@@ -79,29 +79,46 @@ struct DoneRun {
 constexpr int kMaxRuns = 4;
 constexpr uint32_t kAccountEvery = 8;  // items per fence when completions stream in
 
+// A flush is complete: its ticket goes out first (the host waits on it), its time stamps
+// after.  The system-scope fence before the ticket orders every item of the flush (this
+// CTA's stores, and the other CTAs' through the per-flush counter read before it) and the
+// slot resets; `tseq` marks the stamps of that flush as written.
+__device__ __forceinline__ void finish_flush(const WorkerParams& P, const DoneRun& d) {
+  const unsigned long long t_end = ptx::now_ns();
+  const unsigned long long t0 = atomicExch(&P.dc->batch_t0[d.batch], ~0ull);
+  Ticket& tk = P.tickets[d.batch];
+  ptx::fence_acq_rel_sys();
+  ptx::st_relaxed_sys(&tk.seq, d.batch_seq);
+  ptx::st_relaxed_sys(&tk.t_start, t0);
+  ptx::st_relaxed_sys(&tk.t_end, t_end);
+  ptx::fence_acq_rel_sys();
+  ptx::st_relaxed_sys(&tk.tseq, d.batch_seq);
+}
+
 // One gpu-scope fence covers every item of the runs (their compute warps' stores were
 // ordered before the completer by the per-stage done barriers); then the per-flush
-// counters; the last item of a flush writes the flush's ticket into mapped memory.
+// counters; the last item of a flush writes the flush's ticket into mapped memory.  A run
+// that holds every item of its flush is complete without the counter.
 __device__ void account(const WorkerParams& P, const DoneRun* runs, int nruns, bool* first) {
   if (*first) {
     tl_mark(P, TL_ACCOUNT);
     *first = false;
   }
-  ptx::fence_acq_rel_gpu();
+  // a single whole flush needs no gpu-scope release of its own: finish_flush fences at
+  // system scope before anything else is written
+  if (nruns != 1 || runs[0].n != runs[0].batch_items) ptx::fence_acq_rel_gpu();
   unsigned long long total = 0;
   for (int r = 0; r < nruns; ++r) {
     const DoneRun& d = runs[r];
     total += d.n;
+    if (d.n == d.batch_items) {
+      finish_flush(P, d);
+      continue;
+    }
     const unsigned int prev = atomicAdd(&P.dc->batch_done[d.batch], d.n);
     if (prev + d.n == d.batch_items) {
-      ptx::fence_acq_rel_gpu();
       P.dc->batch_done[d.batch] = 0u;
-      const unsigned long long t0 = atomicExch(&P.dc->batch_t0[d.batch], ~0ull);
-      Ticket& tk = P.tickets[d.batch];
-      ptx::st_relaxed_sys(&tk.t_start, t0);
-      ptx::st_relaxed_sys(&tk.t_end, ptx::now_ns());
-      ptx::fence_sc_sys();
-      ptx::st_relaxed_sys(&tk.seq, d.batch_seq);
+      finish_flush(P, d);
     }
   }
   atomicAdd(&P.dc->items_done, total);
@@ -418,7 +435,8 @@ __device__ __forceinline__ int park(const WorkerParams& P, SmemHeader& H, const 
     if (C.rounds == 1) tl_mark(P, TL_GATHER);
     const bool aborted = *reinterpret_cast<volatile unsigned int*>(&dc->abort) != 0;
     if (!gathered && !aborted) {
-      ptx::st_release_gpu(&dc->tail_mirror, ptx::ld_acquire_sys(&P.hc->tail));
+      C.mirrored = ptx::ld_acquire_sys(&P.hc->tail);
+      ptx::st_release_gpu(&dc->tail_mirror, C.mirrored);
       ptx::st_release_gpu(&dc->verdict, (round << 2) | PV_RESUME);
       return PV_RESUME;
     }
@@ -432,6 +450,7 @@ __device__ __forceinline__ int park(const WorkerParams& P, SmemHeader& H, const 
       ++C.work_resumes;
       ptx::st_relaxed_sys(&P.rep->state, (P.epoch << 8) | WS_RUNNING);
       ptx::st_release_gpu(&dc->tail_mirror, T);
+      C.mirrored = T;
       ptx::st_release_gpu(&dc->verdict, (round << 2) | PV_RESUME);
       return PV_RESUME;
     }
@@ -711,6 +730,7 @@ __device__ __forceinline__ void producer_loop(const WorkerParams& P, const Worke
     C.safety_ns = ptx::ld_acquire_gpu(&dc->p_safety_idle_ns);
     C.spin_ns = ptx::ld_acquire_gpu(&dc->p_spin_ns);
     C.read_sum = C.read_n = C.read_max = 0;
+    C.mirrored = st.tail_cache;
     C.rounds = C.timeouts = C.work_resumes = C.parked_seen = 0;
     for (int k = 0; k < 7; ++k) C.dg[k] = 0;
   }
@@ -763,8 +783,17 @@ __device__ __forceinline__ void producer_loop(const WorkerParams& P, const Worke
         c1 = c0;
       }
       while (action == 0 && st.ticket >= st.tail_cache) {
-        // idle: poll for publication, watch for exit conditions
+        // idle: poll for publication, watch for exit conditions.  The control words are
+        // loaded first and the tail (acquire) last, so one poll costs one round trip.
         ++C.polls;
+        const unsigned int ab = *reinterpret_cast<volatile unsigned int*>(&dc->abort);
+        unsigned long long cl = ptx::ld_relaxed_gpu(&dc->closing);
+        const bool ctl = leader && (C.polls & 7u) == 0;  // host control words: every few polls
+        uint64_t q = 0, beat = 0;
+        if (ctl) {
+          q = ptx::ld_relaxed_sys(&P.hc->quit_epoch);
+          beat = ptx::ld_relaxed_sys(&P.hc->host_beat);
+        }
         uint64_t t;
         if (leader) {
           // only the leader reads host memory; everybody else polls its device mirror
@@ -774,7 +803,10 @@ __device__ __forceinline__ void producer_loop(const WorkerParams& P, const Worke
           C.read_sum += dr;
           ++C.read_n;
           if (dr > C.read_max) C.read_max = dr;
-          if (t > *reinterpret_cast<volatile unsigned long long*>(&dc->tail_mirror)) ptx::st_release_gpu(&dc->tail_mirror, t);
+          if (t > C.mirrored) {
+            ptx::st_release_gpu(&dc->tail_mirror, t);
+            C.mirrored = t;
+          }
         } else {
           t = ptx::ld_acquire_gpu(&dc->tail_mirror);
         }
@@ -784,14 +816,13 @@ __device__ __forceinline__ void producer_loop(const WorkerParams& P, const Worke
         }
         const uint64_t now = ptx::now_ns();
         *reinterpret_cast<volatile unsigned long long*>(&H.prod_alive) = now;
-        if (*reinterpret_cast<volatile unsigned int*>(&dc->abort)) {
+        if (ab) {
           action = 1;
           break;
         }
         if (leader) {
-          if ((C.polls & 7u) == 0) {  // host control words: refreshed every few polls
-            C.quit_epoch = P.hc->quit_epoch;
-            const uint64_t beat = P.hc->host_beat;
+          if (ctl) {
+            C.quit_epoch = q;
             if (beat != C.beat_val) {
               C.beat_val = beat;
               C.beat_t = now;
@@ -818,10 +849,11 @@ __device__ __forceinline__ void producer_loop(const WorkerParams& P, const Worke
             atomicExch(&dc->park_min, ~0ull);
             ptx::fence_acq_rel_gpu();
             ptx::st_release_gpu(&dc->closing, C.round);
+            cl = C.round;  // the leader joins its own round at once
           }
         }
-        const unsigned long long cl = ptx::ld_acquire_gpu(&dc->closing);
         if (cl > C.seen_round) {
+          ptx::fence_acq_rel_gpu();  // with the relaxed load of `closing`: acquire of the round
           const int v = park(P, H, st, cl, S);
           if (v == PV_EXIT) {
             action = 1;
@@ -830,7 +862,7 @@ __device__ __forceinline__ void producer_loop(const WorkerParams& P, const Worke
           st.tail_cache = ptx::ld_acquire_gpu(&dc->tail_mirror);
           continue;
         }
-        ptx::nanosleep(leader ? (uint32_t)C.spin_ns : 256);
+        ptx::nanosleep(leader ? (uint32_t)C.spin_ns : 128);
       }
       C.dg[DG_P_IDLE] += clock64() - c1;
     }

@@ -139,7 +139,7 @@ struct alignas(32) Ticket {
   volatile uint64_t seq;       // flush ticket once complete
   volatile uint64_t t_start;   // %globaltimer when its first item started
   volatile uint64_t t_end;     // %globaltimer when its last item completed
-  volatile uint64_t _pad;
+  volatile uint64_t tseq;      // flush whose t_start/t_end are written (after seq)
 };
 
 constexpr int kNumBatchSlots = 1024;
@@ -284,6 +284,7 @@ struct ProdCold {
   uint64_t quit_epoch, yield_every, safety_ns;  // leader: host control words (refreshed while idle)
   uint64_t spin_ns;
   uint64_t read_sum, read_n, read_max;          // leader: host tail read latency
+  uint64_t mirrored;                            // leader: last value stored to DevCtl::tail_mirror
   uint64_t rounds, timeouts, work_resumes, parked_seen;
   unsigned long long dg[7];  // DG_P_WAIT_EMPTY .. DG_P_ITEMS, then the bulk-copy issue cycles
 };

@@ -1289,6 +1289,13 @@ extern "C" int gpuos_rt_flush_times(gpuos_rt* rt, uint64_t seq, uint64_t* t_star
   const Ticket& tk = rt->tickets[seq % kNumBatchSlots];
   if (seq == 0 || seq > rt->last_seq || seq + kNumBatchSlots <= rt->last_seq || tk.seq != (uint32_t)seq)
     return fail(GPUOS_ERR_INVALID, "flush %llu not complete or recycled", (unsigned long long)seq);
+  // the worker writes the stamps just after the ticket
+  const uint64_t t0 = mono_ns();
+  while (tk.tseq != (uint32_t)seq) {
+    if (mono_ns() - t0 > 100ull * 1000 * 1000)
+      return fail(GPUOS_ERR_TIMEOUT, "time stamps of flush %llu not written", (unsigned long long)seq);
+    cpu_relax();
+  }
   if (t_start) *t_start = tk.t_start;
   if (t_end) *t_end = tk.t_end;
   return GPUOS_OK;
