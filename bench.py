@@ -63,6 +63,9 @@ def parse():
     p.add_argument("--no-extras", action="store_true", help="skip baselines, latency, e2e (profiling runs)")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--latency-samples", type=int, default=2000)
+    p.add_argument("--workload", choices=["c1", "c2", "c3", "c4"], default="c1",
+                   help="c1: the headline workload (default).  c2-c4: the mixed-op, strided/broadcast "
+                        "mixed-dtype and reduction streams, one GPU, measured for the kernel's roofline")
     return p.parse_args()
 
 
@@ -255,8 +258,297 @@ def run_reference(args, rank, world):
     return line
 
 
+# ---- secondary workloads (one GPU): the request streams of the other configurations ----------
+def ulp_distance(got: torch.Tensor, ref: torch.Tensor) -> torch.Tensor:
+    """|ulp distance| between two float32 tensors (same sign ordering as the integers)."""
+    def key(t):
+        i = t.float().contiguous().view(torch.int32).to(torch.int64)
+        return torch.where(i < 0, -(i & 0x7FFFFFFF), i)
+    return (key(got) - key(ref)).abs()
+
+
+def log_uniform(g, lo: float, hi: float) -> int:
+    import math
+    return int(math.exp(math.log(lo) + torch.rand(1, generator=g).item() * (math.log(hi) - math.log(lo))))
+
+
+def aligned(n: int, es: int) -> int:
+    """Elements of a slice of n elements rounded up to 512 bytes: requests sit in one buffer
+    at the alignment separate allocations would have."""
+    per = 512 // es
+    return (n + per - 1) // per * per
+
+
+def _c2_ops():
+    """name, op-code attribute, binary, (p0, p1), bit-exact against PyTorch CPU, PyTorch op"""
+    import torch.nn.functional as F
+    return [
+        ("relu", "EW_RELU", False, (), True, lambda x, y: torch.relu(x)),
+        ("sigmoid", "EW_SIGMOID", False, (), False, lambda x, y: torch.sigmoid(x)),
+        ("tanh", "EW_TANH", False, (), False, lambda x, y: torch.tanh(x)),
+        ("exp", "EW_EXP", False, (), False, lambda x, y: torch.exp(x)),
+        ("log", "EW_LOG", False, (), False, lambda x, y: torch.log(x)),
+        ("sqrt", "EW_SQRT", False, (), False, lambda x, y: torch.sqrt(x)),
+        ("gelu", "EW_GELU", False, (), False, lambda x, y: F.gelu(x)),
+        ("hardswish", "EW_HARDSWISH", False, (), True, lambda x, y: F.hardswish(x)),
+        ("leaky_relu", "EW_LEAKY_RELU", False, (0.01,), True, lambda x, y: F.leaky_relu(x, 0.01)),
+        ("elu", "EW_ELU", False, (1.0,), False, lambda x, y: F.elu(x)),
+        ("softplus", "EW_SOFTPLUS", False, (1.0, 20.0), False, lambda x, y: F.softplus(x)),
+        ("clamp", "EW_CLAMP", False, (-0.5, 0.5), True, lambda x, y: torch.clamp(x, -0.5, 0.5)),
+        ("add", "EW_ADD", True, (), True, lambda x, y: x + y),
+        ("sub", "EW_SUB", True, (), True, lambda x, y: x - y),
+        ("mul", "EW_MUL", True, (), True, lambda x, y: x * y),
+        ("div", "EW_DIV", True, (), True, lambda x, y: x / y),
+        ("maximum", "EW_MAXIMUM", True, (), True, lambda x, y: torch.maximum(x, y)),
+        ("minimum", "EW_MINIMUM", True, (), True, lambda x, y: torch.minimum(x, y)),
+        ("pow", "EW_POW", True, (), False, lambda x, y: torch.pow(x, y)),
+    ]
+
+
+def _within(got, ref, exact, x, name) -> bool:
+    if exact:
+        return bool(torch.equal(got.float().view(torch.int32), ref.float().contiguous().view(torch.int32)))
+    d = ulp_distance(got, ref)
+    if name == "gelu":  # PyTorch CPU's own GELU error reaches ~6 |x| 2**-24
+        d = torch.where((got.float() - ref.float()).abs() <= 8 * x.abs() * 2.0 ** -24, torch.zeros_like(d), d)
+    return int(d.max()) <= 2
+
+
+def build_c2(g_ext, seed=1234 + 2, n_req=16384):
+    """16384 fp32 requests, numel log-uniform 256..32768, ops uniform over the 19 operators,
+    inputs in each operator's domain; 512-byte-aligned slices of one buffer per operand."""
+    ops = _c2_ops()
+    g = torch.Generator().manual_seed(seed)
+    sizes = [log_uniform(g, 256, 32768) for _ in range(n_req)]
+    kinds = torch.randint(0, len(ops), (n_req,), generator=g).tolist()
+    offs, o = [], 0
+    for n in sizes:
+        offs.append(o)
+        o += aligned(n, 4)
+    X = torch.rand(o, generator=g) * 8 - 4
+    Y = torch.rand(o, generator=g) * 8 - 4
+    for k, (n, off) in enumerate(zip(sizes, offs)):
+        name = ops[kinds[k]][0]
+        x, y = X[off:off + n], Y[off:off + n]
+        if name in ("log", "sqrt"):
+            x.abs_().add_(1e-3)
+        elif name == "div":
+            y.copy_(torch.rand(n, generator=g) * 1.5 + 0.5)
+        elif name == "pow":
+            x.copy_(torch.rand(n, generator=g) * 1.9 + 0.1)
+            y.copy_(torch.rand(n, generator=g) * 1.5 + 0.5)
+    Xd, Yd = X.cuda(), Y.cuda()
+    Od = torch.empty_like(Xd)
+    reqs, nbytes = [], 0
+    for k, (n, off) in enumerate(zip(sizes, offs)):
+        name, code, binary, params, exact, fn = ops[kinds[k]]
+        reqs.append((getattr(g_ext, code), Xd[off:off + n], Yd[off:off + n] if binary else None,
+                     Od[off:off + n], params))
+        nbytes += (12 if binary else 8) * n
+
+    def check(sample):
+        ok = True
+        for k in sample:
+            n, off = sizes[k], offs[k]
+            name, code, binary, params, exact, fn = ops[kinds[k]]
+            x, y = X[off:off + n], Y[off:off + n]
+            ok &= _within(Od[off:off + n].cpu(), fn(x, y), exact, x, name)
+        return ok
+    desc = ("16384 fp32 requests, numel log-uniform 256..32768, ops uniform over 19 (12 unary, 7 binary), "
+            "x ~ U(-4,4) (log/sqrt on |x|+1e-3, pow base U(0.1,2) exponent U(0.5,2), divisor U(0.5,2))")
+    extra = {"ops": ops, "kinds": kinds, "X": Xd, "Y": Yd, "sizes": sizes, "offs": offs}
+    return reqs, nbytes, check, desc, extra
+
+
+def build_c3(g_ext, seed=1234 + 3, n_req=8192):
+    """8192 requests over 32 shape pairs: a = [C,R] fp16 viewed transposed as [R,C], b = [C]
+    bf16 broadcast along dim 0, out [R,C] fp32 contiguous; op add/mul/maximum/gelu(a)."""
+    import torch.nn.functional as F
+    g = torch.Generator().manual_seed(seed)
+    pairs = [(int(torch.randint(1, 257, (1,), generator=g)), int(torch.randint(32, 2049, (1,), generator=g)))
+             for _ in range(32)]
+    opk = torch.randint(0, 4, (n_req,), generator=g).tolist()
+    shapes = [pairs[k % 32] for k in range(n_req)]
+    na = sum(aligned(R * C, 2) for R, C in shapes)
+    nb = sum(aligned(C, 2) for R, C in shapes)
+    no = sum(aligned(R * C, 4) for R, C in shapes)
+    gd = torch.Generator(device="cuda").manual_seed(seed)
+    Ad = torch.randn(na, generator=gd, device="cuda").half()
+    Bd = torch.randn(nb, generator=gd, device="cuda").bfloat16()
+    Od = torch.empty(no, device="cuda")
+    codes = [g_ext.EW_ADD, g_ext.EW_MUL, g_ext.EW_MAXIMUM, g_ext.EW_GELU]
+    reqs, views, nbytes = [], [], 0
+    oa = ob = oo = 0
+    for k, (R, C) in enumerate(shapes):
+        a = Ad[oa:oa + R * C].view(C, R).t()
+        b = Bd[ob:ob + C]
+        o = Od[oo:oo + R * C].view(R, C)
+        op = opk[k]
+        reqs.append((codes[op], a, b if op < 3 else None, o, ()))
+        views.append((op, a, b, o))
+        nbytes += R * C * 6 + (2 * C if op < 3 else 0)
+        oa += aligned(R * C, 2)
+        ob += aligned(C, 2)
+        oo += aligned(R * C, 4)
+
+    def check(sample):
+        ok = True
+        for k in sample:
+            op, a, b, o = views[k]
+            ac, bc = a.cpu().float(), b.cpu().float()
+            ref = [lambda: ac + bc, lambda: ac * bc, lambda: torch.maximum(ac, bc), lambda: F.gelu(ac)][op]()
+            ok &= _within(o.cpu(), ref, op < 3, ac, "gelu")
+        return ok
+    desc = ("8192 requests over 32 shape pairs R 1..256, C 32..2048: a = [C,R] fp16 viewed transposed, "
+            "b = [C] bf16 broadcast along dim 0, out [R,C] fp32; op add/mul/maximum/gelu(a); N(0,1)")
+    return reqs, nbytes, check, desc, {}
+
+
+def build_c4(g_ext, seed=1234 + 4, n_req=8192):
+    """8192 sum/mean reductions over the last axis of [R,C]: R log-uniform 1..1024, C log-uniform
+    32..4096, fp32 and bf16, half of them stride-2 views of [R,2C], keepdim at random; the output
+    has the input's dtype."""
+    g = torch.Generator().manual_seed(seed)
+    cases = []
+    for k in range(n_req):
+        R = log_uniform(g, 1, 1024)
+        C = log_uniform(g, 32, 4096)
+        dt = torch.float32 if k % 2 == 0 else torch.bfloat16
+        keep = bool(torch.randint(0, 2, (1,), generator=g))
+        mean = bool(torch.randint(0, 2, (1,), generator=g))
+        cases.append((R, C, dt, keep, mean, (k // 2) % 2 == 0))
+    es = {torch.float32: 4, torch.bfloat16: 2}
+    n_in = {torch.float32: 0, torch.bfloat16: 0}
+    n_out = {torch.float32: 0, torch.bfloat16: 0}
+    for R, C, dt, keep, mean, strided in cases:
+        n_in[dt] += aligned(R * (2 * C if strided else C), es[dt])
+        n_out[dt] += aligned(R, es[dt])
+    gd = torch.Generator(device="cuda").manual_seed(seed)
+    IN = {dt: torch.randn(n, generator=gd, device="cuda").to(dt) for dt, n in n_in.items()}
+    OUT = {dt: torch.empty(n, device="cuda", dtype=dt) for dt, n in n_out.items()}
+    oi = {torch.float32: 0, torch.bfloat16: 0}
+    oo = {torch.float32: 0, torch.bfloat16: 0}
+    reqs, views, nbytes = [], [], 0
+    for R, C, dt, keep, mean, strided in cases:
+        w = 2 * C if strided else C
+        buf = IN[dt][oi[dt]:oi[dt] + R * w].view(R, w)
+        x = buf[:, ::2] if strided else buf
+        o = OUT[dt][oo[dt]:oo[dt] + R]
+        o = o.view(R, 1) if keep else o.view(R)
+        oi[dt] += aligned(R * w, es[dt])
+        oo[dt] += aligned(R, es[dt])
+        reqs.append(("reduce", g_ext.RED_MEAN if mean else g_ext.RED_SUM, x, o, keep))
+        views.append((x, o, keep, mean, dt, C))
+        nbytes += R * C * es[dt] + R * es[dt]
+
+    def check(sample):
+        ok = True
+        for k in sample:
+            x, o, keep, mean, dt, C = views[k]
+            xc = x.cpu().float()
+            ref = xc.mean(-1, keepdim=keep) if mean else xc.sum(-1, keepdim=keep)
+            scale = xc.abs().sum(-1, keepdim=keep) / (C if mean else 1)
+            tol = 1e-5 if dt == torch.float32 else 1e-2
+            ok &= bool(((o.cpu().float() - ref).abs() <= tol * torch.maximum(scale, ref.abs()) + 1e-6).all())
+        return ok
+    desc = ("8192 sum/mean over the last axis of [R,C], R log-uniform 1..1024, C log-uniform 32..4096, "
+            "fp32/bf16 N(0,1), half stride-2 views of [R,2C], keepdim at random, fp32 accumulation")
+    return reqs, nbytes, check, desc, {}
+
+
+def run_config(args):
+    """One GPU: every request of the configuration submitted through the runtime's calls, then
+    one flush(sync=True) per step.  `value` is requests/s with the submit calls; `device` is the
+    span of the step's flushes on the GPU (first tile staged to last tile accounted, from the
+    %globaltimer stamps of their tickets)."""
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        raise SystemExit("--workload c2..c4 runs on one GPU")
+    torch.cuda.set_device(0)
+    from gpuos_b200 import gpuos_ext as g
+    # a ring large enough for a whole step (a strided request is many tiles): one flush per step
+    g.init(capacity=65536, threads_per_block=256)
+    build = {"c2": build_c2, "c3": build_c3, "c4": build_c4}[args.workload]
+    reqs, nbytes, check, desc, extra = build(g)
+    torch.cuda.synchronize()
+    sub_ew, sub_red = g.submit_elementwise, g.submit_reduction
+
+    def step():
+        first = g.completed() + 1  # every earlier flush is complete (sync flushes)
+        for r in reqs:
+            if r[0] == "reduce":
+                sub_red(r[1], r[2], r[3], [-1], r[4])
+            else:
+                sub_ew(r[0], r[1], r[2], r[3], *r[4])
+        return first, g.flush(sync=True)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    n_req = len(reqs)
+    sample = torch.randperm(n_req, generator=torch.Generator().manual_seed(99))[:96].tolist()
+    correct = check(sample)
+    clocks = Clocks(torch.cuda.current_device())
+    clocks.start()
+    l0 = g.launches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    seqs = [step() for _ in range(args.steps)]
+    e1.record()
+    e1.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    dev_ms, nflush = [], []
+    for first, last in seqs:
+        ts = [g.flush_times(sq) for sq in range(first, last + 1)]
+        dev_ms.append((max(t1 for _, t1 in ts) - min(t0 for t0, _ in ts)) / 1e6)
+        nflush.append(last - first + 1)
+    dmed = statistics.median(dev_ms)
+    peak, peak_kind = peaks()
+    gbs = nbytes / (dmed * 1e-3) / 1e9
+    line = {
+        "metric": METRIC, "value": n_req / (ms * 1e-3), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 compute", "data": "synthetic (seeded)",
+        "config": {"workload": desc, "requests": n_req, "algorithmic_bytes_per_step": nbytes,
+                   "l2": "inputs larger than L2" if nbytes > 126e6 else "fits in L2"},
+        "device": {"flush_ms": dmed, "hbm_gbs": gbs, "frac": gbs / peak, "peak": peak, "peak_kind": peak_kind,
+                   "what": "every request of a step: first tile staged to last tile accounted "
+                           "(%globaltimer ticket stamps), persistent worker"},
+        "flushes_per_step": max(nflush),
+        "gpu_launches": g.launches() - l0, "clocks": clk, "correct": bool(correct),
+        "correct_sample": f"{len(sample)} requests against PyTorch CPU eager",
+    }
+    g.shutdown()
+    if args.workload == "c2":
+        line["scheduler_e2e"] = c2_scheduler(args, extra)
+    print(json.dumps(line), flush=True)
+
+
+def c2_scheduler(args, extra):
+    """The same 16384 requests as PyTorch calls under scheduler_context(size_threshold=1<<15,
+    auto_flush_ms=2.0), then flush(sync=True): requests/s through the dispatch plugin."""
+    from gpuos_b200.scheduler import scheduler_context
+    ops, kinds, X, Y, sizes, offs = (extra[k] for k in ("ops", "kinds", "X", "Y", "sizes", "offs"))
+    calls = [(ops[kinds[k]][5], X[off:off + n], Y[off:off + n]) for k, (n, off) in enumerate(zip(sizes, offs))]
+    times = []
+    with torch.no_grad(), scheduler_context(size_threshold=1 << 15, auto_flush_ms=2.0) as s:
+        for _ in range(1 + max(1, args.steps // 4)):
+            t0 = time.perf_counter()
+            outs = [fn(x, y) for fn, x, y in calls]
+            s.flush(sync=True)
+            times.append(time.perf_counter() - t0)
+            del outs
+        stats = dict(s.stats)
+    dt = statistics.median(times[1:])
+    return {"value": len(calls) / dt, "unit": UNIT, "ms_per_step": dt * 1e3,
+            "scheduled": stats.get("scheduled"), "fallbacks": stats.get("fallbacks"),
+            "what": "same requests as PyTorch calls under scheduler_context, host wall clock per pass"}
+
+
 def main():
     args = parse()
+    if args.workload != "c1":
+        run_config(args)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

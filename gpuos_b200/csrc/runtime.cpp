@@ -216,6 +216,13 @@ struct Plan {
 
 constexpr uint32_t kGenericTile = 8192;
 
+// Elements per contiguous tile.  A tile is staged as the 16-byte-aligned span around its
+// bytes, so an operand that starts off a 16-byte boundary gets tiles 32 bytes shorter than
+// the stage half (a multiple of 16 bytes, so every tile keeps the operand's misalignment).
+static uint32_t stage_tile(uint32_t half_bytes, int es, bool misaligned) {
+  return (misaligned ? half_bytes - 32 : half_bytes) / (uint32_t)es;
+}
+
 // Row-major dense (every size > 1 dim has the contiguous stride).
 static bool dense(const GpuosOperand& t) {
   int64_t expect = 1;
@@ -274,7 +281,8 @@ int plan_ew(const EwReq& r, uint32_t half_bytes, Plan* p) {
   // contiguous run, no broadcast, no dimension bookkeeping.
   if (same_shape(*r.a, out) && dense(*r.a) && dense(out) && (!b || (same_shape(*b, out) && dense(*b)))) {
     const int es_max = std::max(esa, b ? esb : 1);
-    const uint32_t tile = half_bytes / (uint32_t)es_max;
+    const bool misaligned = (((uintptr_t)r.a->data | (b ? (uintptr_t)b->data : 0)) & 15) != 0;
+    const uint32_t tile = stage_tile(half_bytes, es_max, misaligned);
     uint32_t p0u, p1u;
     std::memcpy(&p0u, &r.params[0], 4);
     std::memcpy(&p1u, &r.params[1], 4);
@@ -334,7 +342,9 @@ int plan_ew(const EwReq& r, uint32_t half_bytes, Plan* p) {
     if (a_vec) es_max = std::max(es_max, esa);
     if (b_vec) es_max = std::max(es_max, esb);
     if (!a_vec && !b_vec) es_max = 4;
-    const uint32_t tile = half_bytes / (uint32_t)es_max;
+    const bool misaligned =
+        (((a_vec ? (uintptr_t)r.a->data : 0) | (b_vec ? (uintptr_t)b->data : 0)) & 15) != 0;
+    const uint32_t tile = stage_tile(half_bytes, es_max, misaligned);
     uint32_t p0u, p1u;
     std::memcpy(&p0u, &r.params[0], 4);
     std::memcpy(&p1u, &r.params[1], 4);

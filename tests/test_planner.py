@@ -40,6 +40,21 @@ def test_large_request_is_tiled():
     assert len(items) == -(-100_003 // 8192)
 
 
+@pytest.mark.parametrize("dt,shift", [(torch.float32, 1), (torch.float32, 3), (torch.float16, 5), (torch.bfloat16, 1)])
+def test_misaligned_operand_tiles_fit_a_stage_half(dt, shift):
+    # a view that starts off a 16-byte boundary: every tile's 16-byte-aligned span must fit
+    # the 16 KB stage half, or the tile would not be staged
+    base = torch.randn(30_001 + shift).to(dt)
+    a, b = base[shift:], torch.randn(30_001).to(dt)
+    items = check_ew(EW["ADD"], a, b, dt)
+    es = base.element_size()
+    for it in items:
+        for addr in (int(it["a"]), int(it["b"])):
+            span = ((addr + int(it["count"]) * es + 15) & ~15) - (addr & ~15)
+            assert span <= 16384
+    assert int(items[0]["count"]) == (16384 - 32) // es
+
+
 def test_transposed_fp16_with_broadcast_bf16_is_generic():
     # C3: a = transpose of [512,64] fp16 viewed [64,512]; b = [512] bf16; out fp32
     a = torch.randn(512, 64).half().t()
