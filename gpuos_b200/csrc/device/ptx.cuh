@@ -173,6 +173,10 @@ __device__ __forceinline__ float4 ld_shared_v4f(uint32_t addr) {
   return v;
 }
 
+__device__ __forceinline__ void st_shared_f(uint32_t addr, float v) {
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
 __device__ __forceinline__ float ld_shared_f(uint32_t addr) {
   float v;
   asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));

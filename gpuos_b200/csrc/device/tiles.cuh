@@ -260,9 +260,141 @@ __device__ __noinline__ void ew_generic(const TileCtx& c) {
   }
 }
 
+// ---- EW_2D: a block of a 2-D strided / broadcast layout ------------------------------
+// The layout is [rows, cols] with the output's inner dimension last.  An item covers rows
+// [r0, r0 + nr) x columns [c0, c0 + nc) (x = r0 | c0 << 32, count = nr << 16 | nc); offsets
+// are row * stride0 + col * stride1 in 32 bits, so no element index is ever divided.
+//   row mode: warp w takes rows w, w + nwarps, ...; lanes take consecutive columns.
+//   transpose mode (IF_A_T / IF_B_T, nr <= 16, nc <= 256): an operand that is contiguous
+//   along rows is first read 16 rows per column (coalesced in its own memory order) into
+//   the stage buffer, which these blocks do not use for staging, as float [16][256] with
+//   the column index XOR 2*row (no bank conflicts in either phase); then thread j computes
+//   column j for every row, so the output is written coalesced along its columns.
+constexpr uint32_t kBarBlock = 1;  // named barrier of the compute warps (transpose mode)
+static_assert(k2dBlockRows == 16 && k2dBlockCols == 256, "the transpose tile below is float [16][256]");
+static_assert(16 * 256 * 4 <= kStageBytesDefault / 2, "a transpose tile fills at most one stage half");
+
+// Loads of a batch of kBatch elements go into registers before any store: a store through a
+// generic pointer may alias the next load, so a load-compute-store loop would wait a full
+// memory latency per element.
+constexpr uint32_t kBatch = 8;
+
+// Storage type <-> float, and f(T{}) called with the storage type of a dtype code, so a loop
+// is compiled once per dtype instead of branching on the dtype for every element.
+template <typename T> __device__ __forceinline__ float to_f(T v);
+template <> __device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <typename T> __device__ __forceinline__ T from_f(float v);
+template <> __device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+template <typename F>
+__device__ __forceinline__ void with_dtype(int dt, F&& f) {
+  if (dt == kF16) f(__half{});
+  else if (dt == kBF16) f(__nv_bfloat16{});
+  else f(float{});
+}
+
+template <int OP>
+__device__ __noinline__ void ew_2d(const TileCtx& c) {
+  const WorkItem& it = c.m->item;
+  const Layout& L = c.m->ext.layout;
+  const uint32_t nr = it.count >> 16, nc = it.count & 0xffffu;
+  const int64_t r0 = (int64_t)(uint32_t)it.x, c0 = (int64_t)(it.x >> 32);
+  const int32_t a0s = (int32_t)L.sa[0], a1s = (int32_t)L.sa[1], b0s = (int32_t)L.sb[0], b1s = (int32_t)L.sb[1];
+  const int32_t o0s = (int32_t)L.so[0], o1s = (int32_t)L.so[1];
+  const float p0 = L.params[0], p1 = L.params[1];
+  const int dta = it.dt_a, dtb = it.dt_b, dto = it.dt_o;
+  const uint32_t flags = it.flags;
+  const bool has_b = (flags & IF_B_PRESENT) != 0;
+  const bool b_imm = (flags & IF_B_SCALAR) != 0;
+  const bool b_mem = has_b && !b_imm;
+  const float bscal = b_imm ? __uint_as_float((uint32_t)it.b) : 0.f;
+  const unsigned char* A =
+      reinterpret_cast<const unsigned char*>(it.a) + (r0 * L.sa[0] + c0 * L.sa[1]) * dtype_size(dta);
+  const unsigned char* B =
+      b_mem ? reinterpret_cast<const unsigned char*>(it.b) + (r0 * L.sb[0] + c0 * L.sb[1]) * dtype_size(dtb) : nullptr;
+  unsigned char* O = reinterpret_cast<unsigned char*>(it.o) + (r0 * L.so[0] + c0 * L.so[1]) * dtype_size(dto);
+  const bool a_t = (flags & IF_A_T) != 0, b_t = b_mem && (flags & IF_B_T) != 0;
+
+  if (!a_t && !b_t) {
+    // row mode: warp w takes rows w, w + nw, ...; lane l takes columns l, l + 32, ...; each
+    // step loads kBatch columns of one row before it stores them
+    const uint32_t warp = c.tid >> 5, lane = c.tid & 31, nw = c.nt >> 5;
+    with_dtype(dto, [&](auto otag) {
+      using TO = decltype(otag);
+      for (uint32_t r = warp; r < nr; r += nw) {
+        const unsigned char* Ar = A + (int64_t)((int32_t)r * a0s) * dtype_size(dta);
+        const unsigned char* Br = b_mem ? B + (int64_t)((int32_t)r * b0s) * dtype_size(dtb) : nullptr;
+        TO* Or = reinterpret_cast<TO*>(O) + (int32_t)r * o0s;
+        for (uint32_t j0 = lane; j0 < nc; j0 += 32 * kBatch) {
+          float va[kBatch], vb[kBatch];
+#pragma unroll
+          for (uint32_t u = 0; u < kBatch; ++u) {
+            const uint32_t j = j0 + 32 * u;
+            va[u] = j < nc ? ld_elem(Ar, dta, (int32_t)j * a1s) : 0.f;
+            vb[u] = (b_mem && j < nc) ? ld_elem(Br, dtb, (int32_t)j * b1s) : bscal;
+          }
+#pragma unroll
+          for (uint32_t u = 0; u < kBatch; ++u) {
+            const uint32_t j = j0 + 32 * u;
+            if (j < nc) Or[(int32_t)j * o1s] = from_f<TO>(ew_apply<OP>(va[u], vb[u], p0, p1));
+          }
+        }
+      }
+    });
+    return;
+  }
+  // transpose mode
+  const uint32_t sta = ptx::smem_addr(c.sa), stb = ptx::smem_addr(c.sb);
+  const uint32_t total = 16u * nc;
+  auto fill = [&](auto tag, const unsigned char* X, int32_t x0, int32_t x1, uint32_t dst) {
+    using T = decltype(tag);
+    const T* Xp = reinterpret_cast<const T*>(X);
+    for (uint32_t e0 = c.tid; e0 < total; e0 += c.nt * kBatch) {
+      float v[kBatch];
+#pragma unroll
+      for (uint32_t u = 0; u < kBatch; ++u) {
+        const uint32_t e = e0 + c.nt * u, r = e & 15u, j = e >> 4;
+        v[u] = (e < total && r < nr) ? to_f<T>(Xp[(int32_t)r * x0 + (int32_t)j * x1]) : 0.f;
+      }
+#pragma unroll
+      for (uint32_t u = 0; u < kBatch; ++u) {
+        const uint32_t e = e0 + c.nt * u, r = e & 15u, j = e >> 4;
+        if (e < total && r < nr) ptx::st_shared_f(dst + 4u * (r * 256u + (j ^ (r << 1))), v[u]);
+      }
+    }
+  };
+  if (a_t) with_dtype(dta, [&](auto t) { fill(t, A, a0s, a1s, sta); });
+  if (b_t) with_dtype(dtb, [&](auto t) { fill(t, B, b0s, b1s, stb); });
+  ptx::named_bar_sync(kBarBlock, c.nt);
+  // thread j computes column j for every row of the block
+  const bool b_col = b_mem && !b_t && b0s == 0;  // b constant down a column (row broadcast)
+  with_dtype(dto, [&](auto otag) {
+    using TO = decltype(otag);
+    for (uint32_t j = c.tid; j < nc; j += c.nt) {
+      const float bj = b_col ? ld_elem(B, dtb, (int32_t)j * b1s) : bscal;
+      TO* oc = reinterpret_cast<TO*>(O) + (int32_t)j * o1s;
+      for (uint32_t r = 0; r < nr; ++r) {
+        const uint32_t k = 4u * (r * 256u + (j ^ (r << 1)));
+        const float av = a_t ? ptx::ld_shared_f(sta + k) : ld_elem(A, dta, (int32_t)r * a0s + (int32_t)j * a1s);
+        const float bv = b_t ? ptx::ld_shared_f(stb + k)
+                             : ((b_mem && !b_col) ? ld_elem(B, dtb, (int32_t)r * b0s + (int32_t)j * b1s) : bj);
+        oc[(int32_t)r * o0s] = from_f<TO>(ew_apply<OP>(av, bv, p0, p1));
+      }
+    }
+  });
+  // the stage buffer is next filled by bulk copies (async proxy) after these generic writes
+  ptx::fence_proxy_async_smem();
+}
+
 template <int OP>
 __device__ void ew_tile(const TileCtx& c) {
-  if (c.m->item.kind == IK_EW_CONTIG) ew_contig<OP>(c);
+  const uint8_t kind = c.m->item.kind;
+  if (kind == IK_EW_CONTIG) ew_contig<OP>(c);
+  else if (kind == IK_EW_2D) ew_2d<OP>(c);
   else ew_generic(c);
 }
 

@@ -29,7 +29,6 @@ namespace gpuos {
 
 constexpr uint64_t kNoTicket = ~0ull;
 constexpr uint32_t kBarTask = 2;                            // named barrier: whole CTA
-constexpr uint32_t kBarCompute = 1;                         // named barrier: compute warps
 
 struct WorkerShared {
   SmemHeader* H;
@@ -183,7 +182,8 @@ __device__ __forceinline__ void compute_loop(const WorkerParams& P, const Worker
       ctx.nt = nct;
       if (iter == 0 && ctid == 0) tl_mark(P, TL_TILE0);
       if (kind != IK_EW_CONTIG || !f32_staged_tile(m, ctx.sa, ctx.sb, ctid, nct)) {
-        const uint32_t fi = (kind == IK_EW_CONTIG || kind == IK_EW_GENERIC) ? m.item.op : GPUOS_EW_NUM_OPS;
+        const uint32_t fi =
+            (kind == IK_EW_CONTIG || kind == IK_EW_GENERIC || kind == IK_EW_2D) ? m.item.op : GPUOS_EW_NUM_OPS;
         TileFn fn = g_tile_fns[fi];
         fn(ctx);
       }
@@ -575,7 +575,7 @@ __device__ __forceinline__ bool stage_item(const WorkerParams& P, const WorkerSh
   const WorkItem it = m.item;
   int ok = 1;
   if (lane == 0) {
-    if (it.kind == IK_NONE || it.kind > IK_TASK || it.batch >= kNumBatchSlots ||
+    if (it.kind == IK_NONE || it.kind > IK_EW_2D || it.batch >= kNumBatchSlots ||
         (it.kind != IK_TASK && it.kind != IK_ROW_REDUCE && it.kind != IK_RED_GENERIC && it.op >= GPUOS_EW_NUM_OPS)) {
       report_error(P, DE_BAD_ITEM, st.ticket);
       ok = 0;
@@ -612,7 +612,7 @@ __device__ __forceinline__ bool stage_item(const WorkerParams& P, const WorkerSh
   st.last_seq = __shfl_sync(0xffffffffu, st.last_seq, 0);
   if (!ok) return false;
 
-  if (it.kind == IK_EW_GENERIC || it.kind == IK_RED_GENERIC) {
+  if (it.kind == IK_EW_GENERIC || it.kind == IK_EW_2D || it.kind == IK_RED_GENERIC) {
     warp_copy16(&m.ext.layout, P.layouts + (it.aux & P.layout_mask), sizeof(Layout), lane);
   } else if (it.kind == IK_TASK) {
     warp_copy16(&m.ext.task, P.tasks + (it.aux & P.task_mask), sizeof(Task), lane);

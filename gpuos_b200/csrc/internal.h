@@ -27,6 +27,7 @@ enum ItemKind : uint8_t {
   IK_ROW_REDUCE = 3,  // group of rows reduced over the last (possibly strided) axis
   IK_RED_GENERIC = 4, // arbitrary-axes reduction, one output element per thread
   IK_TASK = 5,        // reference-layout Task dispatched through g_op_alias/g_op_table
+  IK_EW_2D = 6,       // element-wise block of a 2-D strided / broadcast layout (layout record)
   IK_EXIT = 255       // in-CTA sentinel (never in the ring)
 };
 
@@ -36,7 +37,9 @@ enum ItemFlags : uint8_t {
   IF_A_BCAST = 4,     // EW_CONTIG: a is one element broadcast over the tile
   IF_B_BCAST = 8,     // EW_CONTIG: b is one element (in memory) broadcast over the tile
   IF_UNSTAGED = 16,   // ROW_REDUCE: rows read directly from global memory
-  IF_MEAN = 32        // reductions: divide by the reduced extent
+  IF_MEAN = 32,       // reductions: divide by the reduced extent
+  IF_A_T = 64,        // EW_2D: a is contiguous along rows; read through a shared-memory transpose
+  IF_B_T = 128        // EW_2D: the same for b
 };
 
 // One work item (64 bytes).  Field use per kind:
@@ -308,6 +311,9 @@ struct alignas(128) SmemHeader {
 constexpr int kMaxComputeThreads = 448;
 constexpr uint32_t kStageBytesDefault = 32768 + 128;  // two 16 KB operand halves + slack
 constexpr uint32_t kHalfBytes = 16384;                // one operand tile
+// EW_2D geometry: transpose-mode blocks are 16 rows x 256 columns (a float [16][256] tile
+// per transposed operand fills one stage half); row-mode blocks hold about 8192 elements.
+constexpr int64_t k2dBlockRows = 16, k2dBlockCols = 256, k2dRowTile = 8192;
 
 // ---- fixed device scratch of gpuos_ew_batch_noalloc ----------------------------------
 // One statically sized block per device holds everything a one-shot worker launch needs

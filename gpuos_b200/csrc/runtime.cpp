@@ -363,7 +363,74 @@ int plan_ew(const EwReq& r, uint32_t half_bytes, Plan* p) {
     }
     return GPUOS_OK;
   }
-  // strided / broadcast: layout record shared by the request's tiles
+  // strided / broadcast layouts of at most two dims: row x column blocks (EW_2D).  Element
+  // offsets of every operand stay below 2^31 (the device computes them in 32 bits).
+  auto extent_ok = [&]() {
+    for (int k = 0; k < 3; ++k) {
+      int64_t e = 0;
+      for (int i = 0; i < d.nd; ++i) e += (d.size[i] - 1) * std::llabs(d.st[k][i]);
+      if (e >= (int64_t(1) << 31)) return false;
+    }
+    return true;
+  };
+  if (d.nd <= 2 && n < (int64_t(1) << 31) && extent_ok()) {
+    int64_t R = 1, C = d.size[0], st[3][2];
+    for (int k = 0; k < 3; ++k) {
+      st[k][0] = d.nd == 2 ? d.st[k][0] : 0;
+      st[k][1] = d.nd == 2 ? d.st[k][1] : d.st[k][0];
+    }
+    if (d.nd == 2) {
+      R = d.size[0];
+      C = d.size[1];
+    }
+    // walk the output in its memory order: its smaller stride is the column dimension
+    if (R > 1 && st[2][0] < st[2][1]) {
+      std::swap(R, C);
+      for (int k = 0; k < 3; ++k) std::swap(st[k][0], st[k][1]);
+    }
+    // an input that runs contiguously along rows (a transposed view) is read through shared memory
+    auto along_rows = [&](int k) {
+      return R > 1 && st[k][0] != 0 && st[k][1] != 0 && std::llabs(st[k][0]) < std::llabs(st[k][1]);
+    };
+    const bool at = along_rows(0), bt = b && along_rows(1);
+    p->has_layout = true;
+    Layout& L = p->layout;
+    std::memset(&L, 0, sizeof(L));
+    L.ndim = 2;
+    L.sizes[0] = R;
+    L.sizes[1] = C;
+    L.sa[0] = st[0][0];
+    L.sa[1] = st[0][1];
+    L.sb[0] = st[1][0];
+    L.sb[1] = st[1][1];
+    L.so[0] = st[2][0];
+    L.so[1] = st[2][1];
+    for (int i = 0; i < 4; ++i) L.params[i] = r.params[i];
+    proto.kind = IK_EW_2D;
+    proto.flags = base_flags | (at ? IF_A_T : 0) | (bt ? IF_B_T : 0);
+    proto.a = (uint64_t)(uintptr_t)r.a->data;
+    proto.b = b ? (uint64_t)(uintptr_t)b->data : (r.b_imm ? bimm_bits : 0);
+    proto.o = (uint64_t)(uintptr_t)out.data;
+    auto block = [&](int64_t r0, int64_t c0, int64_t nr, int64_t nc) {
+      WorkItem it = proto;
+      it.x = (uint64_t)r0 | ((uint64_t)c0 << 32);
+      it.count = (uint32_t)((nr << 16) | nc);
+      p->items.push_back(it);
+    };
+    if (at || bt) {
+      for (int64_t r0 = 0; r0 < R; r0 += k2dBlockRows)
+        for (int64_t c0 = 0; c0 < C; c0 += k2dBlockCols)
+          block(r0, c0, std::min<int64_t>(k2dBlockRows, R - r0), std::min<int64_t>(k2dBlockCols, C - c0));
+    } else if (C >= k2dRowTile) {
+      for (int64_t r0 = 0; r0 < R; ++r0)
+        for (int64_t c0 = 0; c0 < C; c0 += k2dRowTile) block(r0, c0, 1, std::min<int64_t>(k2dRowTile, C - c0));
+    } else {
+      const int64_t rows = std::max<int64_t>(1, k2dRowTile / C);
+      for (int64_t r0 = 0; r0 < R; r0 += rows) block(r0, 0, std::min<int64_t>(rows, R - r0), C);
+    }
+    return GPUOS_OK;
+  }
+  // strided / broadcast of more dims: layout record shared by the request's tiles
   p->has_layout = true;
   Layout& L = p->layout;
   std::memset(&L, 0, sizeof(L));

@@ -21,8 +21,9 @@ LAYOUT_DT = np.dtype([("ndim", "<i4"), ("rdim", "<i4"), ("params", "<f4", 4), ("
                       ("rsa", "<i8", 8), ("rtotal", "<i8"), ("pad", "<i8"), ("pad2", "<i8")])
 assert LAYOUT_DT.itemsize == 432
 
-IK_EW_CONTIG, IK_EW_GENERIC, IK_ROW_REDUCE, IK_RED_GENERIC, IK_TASK = 1, 2, 3, 4, 5
+IK_EW_CONTIG, IK_EW_GENERIC, IK_ROW_REDUCE, IK_RED_GENERIC, IK_TASK, IK_EW_2D = 1, 2, 3, 4, 5, 6
 IF_B_PRESENT, IF_B_SCALAR, IF_A_BCAST, IF_B_BCAST, IF_UNSTAGED, IF_MEAN = 1, 2, 4, 8, 16, 32
+IF_A_T, IF_B_T = 64, 128
 CODE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2, torch.float64: 4, torch.int32: 3}
 TDT = {0: torch.float32, 1: torch.float16, 2: torch.bfloat16}
 ES = {0: 4, 1: 2, 2: 2}
@@ -164,6 +165,25 @@ def run_items(items, layout, mem: Memory, op_fn):
                     b = None
                 r = op_fn(int(it["op"]), a, b, float(L["params"][0]), float(L["params"][1]))
                 mem.view(int(it["o"]), dto, -1)[oo] = r.to(TDT[dto])
+        elif kind == IK_EW_2D:
+            # block rows [r0, r0 + nr) x columns [c0, c0 + nc) of the 2-D layout
+            L = layout
+            r0, c0 = int(it["x"]) & 0xFFFFFFFF, int(it["x"]) >> 32
+            nr, nc = int(it["count"]) >> 16, int(it["count"]) & 0xFFFF
+            rr = (torch.arange(nr, dtype=torch.int64) + r0).unsqueeze(1)
+            cc = (torch.arange(nc, dtype=torch.int64) + c0).unsqueeze(0)
+
+            def offs(st):
+                return (rr * int(st[0]) + cc * int(st[1])).reshape(-1)
+            a = mem.view(int(it["a"]), dta, -1).float()[offs(L["sa"])]
+            if it["flags"] & IF_B_SCALAR:
+                b = float(np.uint32(it["b"] & 0xFFFFFFFF).view(np.float32))
+            elif it["flags"] & IF_B_PRESENT:
+                b = mem.view(int(it["b"]), dtb, -1).float()[offs(L["sb"])]
+            else:
+                b = None
+            r = op_fn(int(it["op"]), a, b, float(L["params"][0]), float(L["params"][1]))
+            mem.view(int(it["o"]), dto, -1)[offs(L["so"])] = r.to(TDT[dto])
         elif kind == IK_ROW_REDUCE:
             rows, C, rs, es_ = int(it["count"]), int(it["aux"]), int(it["x"]), int(it["b"])
             base = mem.view(int(it["a"]), dta, -1).float()

@@ -5,8 +5,8 @@ import pytest
 import torch
 
 from oracle.reference_semantics import EW, ew_torch, reduce_torch, same_bits
-from tests._items import (IF_A_BCAST, IF_B_BCAST, IF_B_SCALAR, IF_UNSTAGED, IK_EW_CONTIG,
-                          IK_EW_GENERIC, IK_RED_GENERIC, IK_ROW_REDUCE, Memory, plan_ew,
+from tests._items import (IF_A_BCAST, IF_A_T, IF_B_BCAST, IF_B_SCALAR, IF_B_T, IF_UNSTAGED, IK_EW_2D,
+                          IK_EW_CONTIG, IK_EW_GENERIC, IK_RED_GENERIC, IK_ROW_REDUCE, Memory, plan_ew,
                           plan_reduce, run_items)
 
 
@@ -55,14 +55,47 @@ def test_misaligned_operand_tiles_fit_a_stage_half(dt, shift):
     assert int(items[0]["count"]) == (16384 - 32) // es
 
 
-def test_transposed_fp16_with_broadcast_bf16_is_generic():
+def test_transposed_fp16_with_broadcast_bf16_is_2d_transpose_blocks():
     # C3: a = transpose of [512,64] fp16 viewed [64,512]; b = [512] bf16; out fp32
     a = torch.randn(512, 64).half().t()
     b = torch.randn(512).bfloat16()
     items = check_ew(EW["ADD"], a, b, torch.float32)
-    assert all(it["kind"] == IK_EW_GENERIC for it in items)
+    assert all(it["kind"] == IK_EW_2D and it["flags"] & IF_A_T and not it["flags"] & IF_B_T for it in items)
+    assert len(items) == 4 * 2  # 64 rows x 512 columns in 16 x 256 blocks
+    assert all((int(it["count"]) >> 16) <= 16 and (int(it["count"]) & 0xFFFF) <= 256 for it in items)
     check_ew(EW["MAXIMUM"], a, b, torch.float32)
-    check_ew(EW["GELU"], a, torch.zeros(()), torch.float32) if False else None
+    check_ew(EW["RELU"], a, None, torch.float32)   # unary through the same blocks
+
+
+@pytest.mark.parametrize("R,C", [(1, 300), (15, 17), (16, 256), (17, 257), (40, 1000), (300, 9)])
+def test_2d_blocks_cover_ragged_shapes(R, C):
+    a = torch.randn(C, R).t()                      # transposed
+    b = torch.randn(R, C)                          # contiguous
+    check_ew(EW["SUB"], a, b, torch.float32)
+    check_ew(EW["SUB"], b, a, torch.float32)       # transposed second operand
+    items = check_ew(EW["MUL"], a, a, torch.float32)  # both transposed
+    if R > 1:
+        assert all(it["flags"] & IF_A_T and it["flags"] & IF_B_T for it in items)
+    check_ew(EW["ADD"], b, torch.randn(C), torch.float32)        # row broadcast: row mode
+    check_ew(EW["ADD"], b, torch.randn(R, 1), torch.float32)     # column broadcast: row mode
+    big = torch.randn(R, 2 * C)
+    check_ew(EW["MAXIMUM"], big[:, ::2], b, torch.float16)       # stride-2 rows, 16-bit out
+
+
+def test_row_mode_long_rows_are_split():
+    a = torch.randn(3, 20000)
+    items = check_ew(EW["ADD"], a, torch.randn(20000), torch.float32)
+    assert all(it["kind"] == IK_EW_2D and not it["flags"] & (IF_A_T | IF_B_T) for it in items)
+    assert len(items) == 3 * 3  # 8192-column pieces of each row
+
+
+def test_transposed_output_is_walked_in_its_own_order():
+    out = torch.empty(30, 50).t()                  # [50, 30] view of a column-major buffer
+    a, b = torch.randn(50, 30), torch.randn(30)
+    items, lay = plan_ew(EW["ADD"], a, b, out)
+    run_items(items, lay, Memory(a, b, out), op_fn)
+    assert same_bits(out, a + b)
+    assert int(lay["so"][1]) == 1                  # columns follow the output's contiguous dim
 
 
 def test_broadcast_row_and_scalar_operands():
@@ -84,6 +117,10 @@ def test_coalescing_merges_contiguous_dims():
     # a slice with a gap stays strided
     big = torch.randn(8, 40)
     items = check_ew(EW["ADD"], big[:, :32], torch.randn(8, 32), torch.float32)
+    assert items[0]["kind"] == IK_EW_2D
+    # three dims that do not merge stay on the generic path
+    cube = torch.randn(6, 7, 9)
+    items = check_ew(EW["ADD"], cube[:, :5, ::2], torch.randn(6, 5, 5), torch.float32)
     assert items[0]["kind"] == IK_EW_GENERIC
 
 
