@@ -297,15 +297,15 @@ __device__ __forceinline__ void with_dtype(int dt, F&& f) {
   else f(float{});
 }
 
-template <int OP>
-__device__ __noinline__ void ew_2d(const TileCtx& c) {
+// apply(a, b) is the element operation (its parameters captured).
+template <typename F>
+__device__ __forceinline__ void ew_2d_body(const TileCtx& c, F&& apply) {
   const WorkItem& it = c.m->item;
   const Layout& L = c.m->ext.layout;
   const uint32_t nr = it.count >> 16, nc = it.count & 0xffffu;
   const int64_t r0 = (int64_t)(uint32_t)it.x, c0 = (int64_t)(it.x >> 32);
   const int32_t a0s = (int32_t)L.sa[0], a1s = (int32_t)L.sa[1], b0s = (int32_t)L.sb[0], b1s = (int32_t)L.sb[1];
   const int32_t o0s = (int32_t)L.so[0], o1s = (int32_t)L.so[1];
-  const float p0 = L.params[0], p1 = L.params[1];
   const int dta = it.dt_a, dtb = it.dt_b, dto = it.dt_o;
   const uint32_t flags = it.flags;
   const bool has_b = (flags & IF_B_PRESENT) != 0;
@@ -340,7 +340,7 @@ __device__ __noinline__ void ew_2d(const TileCtx& c) {
 #pragma unroll
           for (uint32_t u = 0; u < kBatch; ++u) {
             const uint32_t j = j0 + 32 * u;
-            if (j < nc) Or[(int32_t)j * o1s] = from_f<TO>(ew_apply<OP>(va[u], vb[u], p0, p1));
+            if (j < nc) Or[(int32_t)j * o1s] = from_f<TO>(apply(va[u], vb[u]));
           }
         }
       }
@@ -382,13 +382,20 @@ __device__ __noinline__ void ew_2d(const TileCtx& c) {
         const float av = a_t ? ptx::ld_shared_f(sta + k) : ld_elem(A, dta, (int32_t)r * a0s + (int32_t)j * a1s);
         const float bv = b_t ? ptx::ld_shared_f(stb + k)
                              : ((b_mem && !b_col) ? ld_elem(B, dtb, (int32_t)r * b0s + (int32_t)j * b1s) : bj);
-        oc[(int32_t)r * o0s] = from_f<TO>(ew_apply<OP>(av, bv, p0, p1));
+        oc[(int32_t)r * o0s] = from_f<TO>(apply(av, bv));
       }
     }
   });
   // the stage buffer is next filled by bulk copies (async proxy) after these generic writes
   ptx::fence_proxy_async_smem();
 }
+
+template <int OP>
+__device__ __noinline__ void ew_2d(const TileCtx& c) {
+  const float p0 = c.m->ext.layout.params[0], p1 = c.m->ext.layout.params[1];
+  ew_2d_body(c, [=](float a, float b) { return ew_apply<OP>(a, b, p0, p1); });
+}
+
 
 template <int OP>
 __device__ void ew_tile(const TileCtx& c) {
@@ -399,44 +406,72 @@ __device__ void ew_tile(const TileCtx& c) {
 }
 
 // ---- reductions ------------------------------------------------------------------------
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
 
-// Rows of one item: warp w reduces rows w, w + nwarps, ...  Each lane keeps four
-// partial sums in a fixed order, so the result is deterministic.
-__device__ __noinline__ void row_reduce_tile(const TileCtx& c) {
+// Rows of one item; every row is read by all 32 lanes of a warp on consecutive elements (no
+// bank conflicts on staged rows).  Rows of 128 elements or more: one row per warp step, four
+// partial sums per lane.  Shorter rows: four rows per warp step, one partial sum per lane and
+// row, the four rows' shuffle reductions interleaved.  The order of additions depends only
+// on C, so the result is deterministic.  Inlined in the compute loop (no call through the
+// tile table), loads specialised by dtype.
+__device__ __forceinline__ void row_reduce_body(const TileCtx& c) {
   const WorkItem& it = c.m->item;
   const uint32_t rows = it.count;
   const int64_t C = it.aux;
   const int64_t rs = (int64_t)it.x;
   const int64_t is = (int64_t)it.b;
-  const int dta = it.dt_a;
-  const int es = dtype_size(dta);
   const unsigned char* base =
       (c.m->staged & 1) ? c.sa + c.m->a_off : reinterpret_cast<const unsigned char*>(it.a);
   const uint32_t warp = c.tid >> 5, lane = c.tid & 31, nw = c.nt >> 5;
   const bool mean = (it.flags & IF_MEAN) != 0;
-  for (uint32_t r = warp; r < rows; r += nw) {
-    const unsigned char* row = base + (int64_t)r * rs * es;
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-    int64_t j = lane;
-    for (; j + 96 < C; j += 128) {
-      s0 = __fadd_rn(s0, ld_elem(row, dta, j * is));
-      s1 = __fadd_rn(s1, ld_elem(row, dta, (j + 32) * is));
-      s2 = __fadd_rn(s2, ld_elem(row, dta, (j + 64) * is));
-      s3 = __fadd_rn(s3, ld_elem(row, dta, (j + 96) * is));
+  void* out = reinterpret_cast<void*>(it.o);
+  const int dto = it.dt_o;
+  with_dtype(it.dt_a, [&](auto tag) {
+    using T = decltype(tag);
+    const T* X = reinterpret_cast<const T*>(base);
+    if (C >= 128) {
+      for (uint32_t r = warp; r < rows; r += nw) {
+        const T* row = X + (int64_t)r * rs;
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+        int64_t j = lane;
+        for (; j + 96 < C; j += 128) {
+          s0 = __fadd_rn(s0, to_f<T>(row[j * is]));
+          s1 = __fadd_rn(s1, to_f<T>(row[(j + 32) * is]));
+          s2 = __fadd_rn(s2, to_f<T>(row[(j + 64) * is]));
+          s3 = __fadd_rn(s3, to_f<T>(row[(j + 96) * is]));
+        }
+        for (; j < C; j += 32) s0 = __fadd_rn(s0, to_f<T>(row[j * is]));
+        float s = __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+        if (lane == 0) st_elem(out, dto, r, mean ? __fdiv_rn(s, (float)C) : s);
+      }
+      return;
     }
-    for (; j < C; j += 32) s0 = __fadd_rn(s0, ld_elem(row, dta, j * is));
-    float s = warp_sum(__fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3)));
-    if (lane == 0) {
-      if (mean) s = __fdiv_rn(s, (float)C);
-      st_elem(reinterpret_cast<void*>(it.o), it.dt_o, r, s);
+    const int32_t c32 = (int32_t)C, is32 = (int32_t)is;
+    for (uint32_t rb = warp * 4; rb < rows; rb += nw * 4) {
+      float s[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        s[q] = 0.f;
+        if (rb + q < rows) {
+          const T* row = X + (int64_t)(rb + q) * rs;
+          for (int32_t j = lane; j < c32; j += 32) s[q] = __fadd_rn(s[q], to_f<T>(row[j * is32]));
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) s[q] = __fadd_rn(s[q], __shfl_xor_sync(0xffffffffu, s[q], o));
+      }
+      if (lane < 4 && rb + lane < rows) {
+        const float v = lane == 0 ? s[0] : lane == 1 ? s[1] : lane == 2 ? s[2] : s[3];
+        st_elem(out, dto, rb + lane, mean ? __fdiv_rn(v, (float)C) : v);
+      }
     }
-  }
+  });
 }
+
+__device__ __noinline__ void row_reduce_tile(const TileCtx& c) { row_reduce_body(c); }
 
 // Arbitrary reduced axes: one output element per thread, serial over the reduced extent.
 __device__ __noinline__ void red_generic_tile(const TileCtx& c) {

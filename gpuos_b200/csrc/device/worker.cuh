@@ -181,7 +181,11 @@ __device__ __forceinline__ void compute_loop(const WorkerParams& P, const Worker
       ctx.tid = ctid;
       ctx.nt = nct;
       if (iter == 0 && ctid == 0) tl_mark(P, TL_TILE0);
-      if (kind != IK_EW_CONTIG || !f32_staged_tile(m, ctx.sa, ctx.sb, ctid, nct)) {
+      // inlined paths first (no register saves around a call through the tile table)
+      if (kind == IK_EW_CONTIG && f32_staged_tile(m, ctx.sa, ctx.sb, ctid, nct)) {
+      } else if (kind == IK_ROW_REDUCE) {
+        row_reduce_body(ctx);
+      } else {
         const uint32_t fi =
             (kind == IK_EW_CONTIG || kind == IK_EW_GENERIC || kind == IK_EW_2D) ? m.item.op : GPUOS_EW_NUM_OPS;
         TileFn fn = g_tile_fns[fi];
@@ -486,6 +490,13 @@ __device__ __forceinline__ void warp_copy16(void* dst, const void* src, uint32_t
   }
 }
 
+// Copy `bytes` (multiple of 16) within shared memory with the warp.
+__device__ __forceinline__ void warp_copy_smem16(void* dst, const void* src, uint32_t bytes, uint32_t lane) {
+  for (uint32_t off = lane * 16; off < bytes; off += 32 * 16)
+    *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(dst) + off) =
+        *reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned char*>(src) + off);
+}
+
 // Arm stage s as the exit sentinel (lane 0).
 __device__ __forceinline__ void arm_exit(SmemHeader& H, uint32_t s) {
   H.meta[s].item.kind = IK_EXIT;
@@ -613,7 +624,18 @@ __device__ __forceinline__ bool stage_item(const WorkerParams& P, const WorkerSh
   if (!ok) return false;
 
   if (it.kind == IK_EW_GENERIC || it.kind == IK_EW_2D || it.kind == IK_RED_GENERIC) {
-    warp_copy16(&m.ext.layout, P.layouts + (it.aux & P.layout_mask), sizeof(Layout), lane);
+    if (H.lay_valid && H.lay_key == it.aux) {
+      warp_copy_smem16(&m.ext.layout, &H.lay_cache, sizeof(Layout), lane);
+    } else {
+      warp_copy16(&m.ext.layout, P.layouts + (it.aux & P.layout_mask), sizeof(Layout), lane);
+      __syncwarp();
+      warp_copy_smem16(&H.lay_cache, &m.ext.layout, sizeof(Layout), lane);
+      __syncwarp();
+      if (lane == 0) {
+        H.lay_key = it.aux;
+        H.lay_valid = 1;
+      }
+    }
   } else if (it.kind == IK_TASK) {
     warp_copy16(&m.ext.task, P.tasks + (it.aux & P.task_mask), sizeof(Task), lane);
   }
@@ -731,6 +753,7 @@ __device__ __forceinline__ void producer_loop(const WorkerParams& P, const Worke
     C.spin_ns = ptx::ld_acquire_gpu(&dc->p_spin_ns);
     C.read_sum = C.read_n = C.read_max = 0;
     C.mirrored = st.tail_cache;
+    H.lay_valid = 0;
     C.rounds = C.timeouts = C.work_resumes = C.parked_seen = 0;
     for (int k = 0; k < 7; ++k) C.dg[k] = 0;
   }

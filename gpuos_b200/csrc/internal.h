@@ -304,6 +304,12 @@ struct alignas(128) SmemHeader {
   StageMeta meta[kMaxStages];
   WorkItem dcache[2][8];           // descriptors of the current / next chunk (ticket & 7)
   ProdCold cold;
+  // the layout record last copied from the ring: every tile of a request shares its layout,
+  // so later tiles copy it from here instead of over PCIe (key: the item's aux, which holds
+  // the layout's unmasked ring sequence number)
+  Layout lay_cache;
+  uint32_t lay_key;
+  uint32_t lay_valid;
 };
 
 // Compute threads per worker CTA at most (plus the dequeue and completer warps): 512 threads

@@ -1030,10 +1030,12 @@ static int append_plan_locked(gpuos_rt* rt, const Plan& p, const Task* task) {
   for (int i = 0; i < p.nreads; ++i) rt->hz.insert(p.reads[i], false);
   rt->hz.insert(p.write, true);
 
+  // items carry the layout's unmasked sequence number (the worker masks it to a ring slot and
+  // uses the full value as the key of its cached copy, so a reused slot never looks cached)
   uint32_t layout_idx = 0, task_idx = 0;
   if (p.has_layout) {
-    layout_idx = (uint32_t)(rt->layout_w & (rt->layout_cap - 1));
-    rt->layouts[layout_idx] = p.layout;
+    rt->layouts[rt->layout_w & (rt->layout_cap - 1)] = p.layout;
+    layout_idx = (uint32_t)rt->layout_w;
     ++rt->layout_w;
   }
   if (task) {
