@@ -66,6 +66,8 @@ def parse():
     p.add_argument("--workload", choices=["c1", "c2", "c3", "c4"], default="c1",
                    help="c1: the headline workload (default).  c2-c4: the mixed-op, strided/broadcast "
                         "mixed-dtype and reduction streams, one GPU, measured for the kernel's roofline")
+    p.add_argument("--config-requests", type=int, default=0,
+                   help="c2-c4: requests per step (default: the configuration's full count)")
     return p.parse_args()
 
 
@@ -464,11 +466,17 @@ def run_config(args):
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:
         raise SystemExit("--workload c2..c4 runs on one GPU")
     torch.cuda.set_device(0)
+    if args.worker_mode == "drain":
+        # every launch (the one at init included) exits as soon as its work is done
+        os.environ["GPUOS_IDLE_QUIESCE_MS"] = "0"
     from gpuos_b200 import gpuos_ext as g
     # a ring large enough for a whole step (a strided request is many tiles): one flush per step
     g.init(capacity=65536, threads_per_block=256)
+    if args.worker_mode == "drain":
+        g.set_idle_quiesce_ms(0)
     build = {"c2": build_c2, "c3": build_c3, "c4": build_c4}[args.workload]
-    reqs, nbytes, check, desc, extra = build(g)
+    kw = {"n_req": args.config_requests} if args.config_requests > 0 else {}
+    reqs, nbytes, check, desc, extra = build(g, **kw)
     torch.cuda.synchronize()
     sub_ew, sub_red = g.submit_elementwise, g.submit_reduction
 
@@ -518,7 +526,7 @@ def run_config(args):
         "correct_sample": f"{len(sample)} requests against PyTorch CPU eager",
     }
     g.shutdown()
-    if args.workload == "c2":
+    if args.workload == "c2" and not args.no_extras:
         line["scheduler_e2e"] = c2_scheduler(args, extra)
     print(json.dumps(line), flush=True)
 
