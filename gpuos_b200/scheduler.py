@@ -57,10 +57,23 @@ _REDUCE = {"aten::sum.dim_IntList", "aten::mean.dim", "aten::sum", "aten::mean"}
 
 
 def _storage_key(t: torch.Tensor) -> int:
-    try:
-        return t.untyped_storage().data_ptr()
-    except Exception:
-        return t.data_ptr()
+    """Base address of the tensor's storage (a view's data pointer minus its offset), without
+    building a storage object on every call."""
+    return t.data_ptr() - t.storage_offset() * t.element_size()
+
+
+# op overload -> (route, name): 1 binary, 2 unary, 3 parametric unary, 4 reduction, 0 not ours
+_ROUTES: dict = {}
+
+
+def _route(func):
+    r = _ROUTES.get(func)
+    if r is None:
+        name = func.name()
+        kind = (1 if name in _BINARY else 2 if name in _UNARY else 3 if name in _PARAMETRIC
+                else 4 if name in _REDUCE else 0)
+        r = _ROUTES[func] = (kind, name)
+    return r
 
 
 class _GPUOSSchedulerMode(TorchDispatchMode):
@@ -127,10 +140,7 @@ class _GPUOSSchedulerMode(TorchDispatchMode):
         return isinstance(v, (float, int, bool)) and not isinstance(v, complex)
 
     # -- scheduling ---------------------------------------------------------------------
-    def _try_schedule_binary(self, func, a, b, *, alpha=None, out=None):
-        if torch.is_grad_enabled():
-            return None
-        name = func.name()
+    def _try_schedule_binary(self, name, a, b, *, alpha=None, out=None):
         op = _BINARY[name]
         a_t, b_t = isinstance(a, torch.Tensor), isinstance(b, torch.Tensor)
         if not a_t or not self._ok_tensor(a):
@@ -139,7 +149,7 @@ class _GPUOSSchedulerMode(TorchDispatchMode):
             if b.dim() == 0 and not b.is_cuda:
                 b = b.item()
                 b_t = False
-            elif not self._ok_tensor(b) or b.device != a.device:
+            elif not self._ok_tensor(b) or b.get_device() != a.get_device():
                 return None
         if not b_t and not self._ok_scalar(b):
             return None
@@ -152,11 +162,17 @@ class _GPUOSSchedulerMode(TorchDispatchMode):
             if not b_t:  # a + alpha * scalar folds to a scalar operand
                 op = _E.EW_ADD if name == "aten::add.Tensor" else _E.EW_SUB
                 b = float(b) * p0
-        try:
-            shape = torch.broadcast_shapes(a.shape, b.shape) if b_t else a.shape
-        except RuntimeError:
-            return None
-        dtype = torch.result_type(a, b)
+        if b_t:
+            shape = a.shape
+            if b.shape != shape:
+                try:
+                    shape = torch.broadcast_shapes(shape, b.shape)
+                except RuntimeError:
+                    return None
+            dtype = a.dtype if b.dtype == a.dtype else torch.result_type(a, b)
+        else:
+            shape = a.shape
+            dtype = a.dtype  # a floating tensor keeps its dtype against a Python number
         if dtype not in _FLOATS:
             return None
         if out is None:
@@ -256,17 +272,18 @@ class _GPUOSSchedulerMode(TorchDispatchMode):
         return out
 
     def __torch_dispatch__(self, func, types, args=(), kwargs=None):
-        name = func.name()
+        kind, name = _route(func)
         kwargs = kwargs or {}
         res = None
-        if not torch.is_grad_enabled():
-            if name in _BINARY and len(args) >= 2:
-                res = self._try_schedule_binary(func, args[0], args[1], alpha=kwargs.get("alpha"),
-                                                out=kwargs.get("out"))
-            elif (name in _UNARY or name in _PARAMETRIC or name in _REDUCE) and args and self._ok_tensor(args[0]):
-                if name in _UNARY:
+        if kind and not torch.is_grad_enabled():
+            if kind == 1:
+                if len(args) >= 2:
+                    res = self._try_schedule_binary(name, args[0], args[1], alpha=kwargs.get("alpha"),
+                                                    out=kwargs.get("out"))
+            elif args and self._ok_tensor(args[0]):
+                if kind == 2:
                     res = self._schedule_unary(_UNARY[name], args[0])
-                elif name in _PARAMETRIC:
+                elif kind == 3:
                     res = self._try_parametric(name, args, kwargs)
                 else:
                     res = self._try_reduce(name, args, kwargs)
