@@ -504,8 +504,63 @@ __device__ __noinline__ void red_generic_tile(const TileCtx& c) {
   }
 }
 
+// ---- top-k of rows ----------------------------------------------------------------------
+// Preference key of a value: larger is preferred.  IEEE order as unsigned integers, NaN above
+// every number for largest-first (PyTorch's topk orders NaN as the largest value) and below
+// every number for smallest-first.
+__device__ __forceinline__ uint32_t topk_key(float v, bool largest) {
+  const uint32_t b = __float_as_uint(v);
+  const uint32_t key = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  if (v != v) return largest ? 0xffffffffu : 0u;
+  return largest ? key : ~key;
+}
+
+// Warp w takes rows w, w + nwarps, ...  Every candidate has a distinct packed value
+// (key << 32 | ~index, so equal values prefer the lower index); round q takes the warp-wide
+// maximum below round q-1's winner, so k rounds give the k preferred elements in order and
+// nothing has to be marked.  Values are copied bit for bit (they keep x's dtype).
+__device__ __noinline__ void topk_tile(const TileCtx& c) {
+  const WorkItem& it = c.m->item;
+  const uint32_t rows = it.count, n = it.aux, k = (uint32_t)it.x;
+  const bool largest = ((it.x >> 32) & 1u) != 0;
+  const int dt = it.dt_a;
+  const int es = dtype_size(dt);
+  const unsigned char* base =
+      (c.m->staged & 1) ? c.sa + c.m->a_off : reinterpret_cast<const unsigned char*>(it.a);
+  unsigned char* vals = reinterpret_cast<unsigned char*>(it.o);
+  int64_t* idx = reinterpret_cast<int64_t*>(it.b);
+  const uint32_t warp = c.tid >> 5, lane = c.tid & 31, nw = c.nt >> 5;
+  for (uint32_t r = warp; r < rows; r += nw) {
+    const unsigned char* row = base + (int64_t)r * n * es;
+    unsigned long long last = ~0ull;
+    for (uint32_t q = 0; q < k; ++q) {
+      unsigned long long best = 0;
+      for (uint32_t j = lane; j < n; j += 32) {
+        const unsigned long long pk =
+            ((unsigned long long)topk_key(ld_elem(row, dt, j), largest) << 32) | (0xffffffffu - j);
+        if (pk < last && pk > best) best = pk;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
+      }
+      last = best;
+      if (lane == 0) {
+        const uint32_t j = 0xffffffffu - (uint32_t)best;
+        const int64_t o = (int64_t)r * k + q;
+        if (es == 4) reinterpret_cast<uint32_t*>(vals)[o] = reinterpret_cast<const uint32_t*>(row)[j];
+        else reinterpret_cast<uint16_t*>(vals)[o] = reinterpret_cast<const uint16_t*>(row)[j];
+        idx[o] = j;
+      }
+    }
+  }
+}
+
 __device__ void reduce_tile(const TileCtx& c) {
-  if (c.m->item.kind == IK_ROW_REDUCE) row_reduce_tile(c);
+  const uint8_t kind = c.m->item.kind;
+  if (kind == IK_ROW_REDUCE) row_reduce_tile(c);
+  else if (kind == IK_TOPK) topk_tile(c);
   else red_generic_tile(c);
 }
 

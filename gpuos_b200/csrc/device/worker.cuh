@@ -563,6 +563,19 @@ __device__ __forceinline__ void stage_copies(const WorkerShared& W, StageMeta& m
       m.staged = 0;
       ptx::mbar_arrive(full);
     }
+  } else if (it.kind == IK_TOPK) {
+    const uint64_t span = (uint64_t)it.count * it.aux * dtype_size(it.dt_a);
+    const uint64_t a0 = it.a & ~15ull;
+    const uint64_t a1 = (it.a + span + 15) & ~15ull;
+    if (a1 - a0 <= W.stage_bytes) {
+      m.a_off = (uint32_t)(it.a - a0);
+      m.staged = 1;
+      ptx::mbar_arrive_expect_tx(full, (uint32_t)(a1 - a0));
+      ptx::bulk_g2s(ptx::smem_addr(buf), reinterpret_cast<const void*>(a0), (uint32_t)(a1 - a0), full);
+    } else {
+      m.staged = 0;
+      ptx::mbar_arrive(full);
+    }
   } else {
     m.staged = 0;
     ptx::mbar_arrive(full);
@@ -586,7 +599,7 @@ __device__ __forceinline__ bool stage_item(const WorkerParams& P, const WorkerSh
   const WorkItem it = m.item;
   int ok = 1;
   if (lane == 0) {
-    if (it.kind == IK_NONE || it.kind > IK_EW_2D || it.batch >= kNumBatchSlots ||
+    if (it.kind == IK_NONE || it.kind > IK_TOPK || it.batch >= kNumBatchSlots ||
         (it.kind != IK_TASK && it.kind != IK_ROW_REDUCE && it.kind != IK_RED_GENERIC && it.op >= GPUOS_EW_NUM_OPS)) {
       report_error(P, DE_BAD_ITEM, st.ticket);
       ok = 0;

@@ -28,6 +28,7 @@ enum ItemKind : uint8_t {
   IK_RED_GENERIC = 4, // arbitrary-axes reduction, one output element per thread
   IK_TASK = 5,        // reference-layout Task dispatched through g_op_alias/g_op_table
   IK_EW_2D = 6,       // element-wise block of a 2-D strided / broadcast layout (layout record)
+  IK_TOPK = 7,        // top-k of each row of a group of contiguous rows (staged like a row group)
   IK_EXIT = 255       // in-CTA sentinel (never in the ring)
 };
 
@@ -320,6 +321,8 @@ constexpr uint32_t kHalfBytes = 16384;                // one operand tile
 // EW_2D geometry: transpose-mode blocks are 16 rows x 256 columns (a float [16][256] tile
 // per transposed operand fills one stage half); row-mode blocks hold about 8192 elements.
 constexpr int64_t k2dBlockRows = 16, k2dBlockCols = 256, k2dRowTile = 8192;
+// Top-k on the batched path: k rounds of a warp-wide selection per row, so k is bounded.
+constexpr int kTopkMaxK = 256;
 
 // ---- fixed device scratch of gpuos_ew_batch_noalloc ----------------------------------
 // One statically sized block per device holds everything a one-shot worker launch needs

@@ -1007,6 +1007,45 @@ PyObject* py_submit_reduce(PyObject*, PyObject* args) {
   return submit_task_common(dout, t, ks, 2);
 }
 
+// submit_topk_rows(x, values, indices, k, largest) — top-k of every row of a contiguous x
+// [..., n] into contiguous values [..., k] (x's dtype) and int64 indices [..., k]; pending
+// until flush like the other batched requests.
+static bool row_major(const at::Tensor& t) { return t.is_contiguous(); }
+
+PyObject* py_submit_topk_rows(PyObject*, PyObject* args) {
+  PyObject *xo, *vo, *io;
+  int k = 0, largest = 1;
+  if (!PyArg_ParseTuple(args, "OOOip", &xo, &vo, &io, &k, &largest)) return nullptr;
+  GpuosOperand x, v;
+  const int dx = to_operand(xo, &x, "x");
+  if (dx < 0) return nullptr;
+  const int dv = to_operand(vo, &v, "values");
+  if (dv < 0) return nullptr;
+  if (!THPVariable_Check(io)) return PyErr_Format(PyExc_TypeError, "indices must be a torch.Tensor");
+  const at::Tensor& xt = THPVariable_Unpack(xo);
+  const at::Tensor& vt = THPVariable_Unpack(vo);
+  const at::Tensor& it = THPVariable_Unpack(io);
+  if (!it.is_cuda() || it.get_device() != dx || dv != dx)
+    return PyErr_Format(PyExc_RuntimeError, "x, values and indices must be on the same CUDA device");
+  if (it.scalar_type() != at::kLong) return PyErr_Format(PyExc_ValueError, "indices must be int64");
+  if (vt.scalar_type() != xt.scalar_type()) return PyErr_Format(PyExc_ValueError, "values must have x's dtype");
+  if (xt.dim() < 1 || !row_major(xt) || !row_major(vt) || !row_major(it))
+    return PyErr_Format(PyExc_ValueError, "x, values and indices must be contiguous");
+  const int64_t n = xt.size(-1);
+  const int64_t rows = n > 0 ? xt.numel() / n : 0;
+  if (vt.numel() != rows * k || it.numel() != rows * k)
+    return PyErr_Format(PyExc_ValueError, "values and indices must hold k elements per row of x");
+  gpuos_rt* rt = rt_for(dx);
+  if (!rt) return nullptr;
+  const int st = gpuos_rt_submit_topk(rt, x.data, x.dtype, rows, n, v.data, static_cast<int64_t*>(it.data_ptr()),
+                                      k, largest);
+  if (st) return raise_status(st);
+  keep(dx, xo);
+  keep(dx, vo);
+  keep(dx, io);
+  Py_RETURN_NONE;
+}
+
 PyMethodDef kMethods[] = {
     {"init", (PyCFunction)(void (*)(void))py_init, METH_VARARGS | METH_KEYWORDS,
      "init(capacity=4096, threads_per_block=256, device=None)"},
@@ -1025,6 +1064,8 @@ PyMethodDef kMethods[] = {
     {"submit_div", (PyCFunction)(void (*)(void))py_submit_div, METH_FASTCALL, "out = a / b (pending until flush)"},
     {"submit_elementwise", (PyCFunction)(void (*)(void))py_submit_elementwise, METH_FASTCALL,
      "submit_elementwise(op, a, b, out, p0=0.0, p1=0.0)"},
+    {"submit_topk_rows", py_submit_topk_rows, METH_VARARGS,
+     "submit_topk_rows(x, values, indices, k, largest): top-k of each row of x (pending until flush)"},
     {"submit_reduction", (PyCFunction)(void (*)(void))py_submit_reduction, METH_FASTCALL,
      "submit_reduction(op, x, out, axes, keepdim)"},
     {"flush", (PyCFunction)(void (*)(void))py_flush, METH_VARARGS | METH_KEYWORDS, "flush(sync=False, device=None) -> ticket"},

@@ -212,6 +212,7 @@ struct Plan {
   Range reads[2];
   int nreads = 0;
   Range write;
+  Range write2;  // a second output (top-k indices), empty otherwise
 };
 
 constexpr uint32_t kGenericTile = 8192;
@@ -1023,12 +1024,14 @@ static int append_plan_locked(gpuos_rt* rt, const Plan& p, const Task* task) {
   bool hazard = false;
   for (int i = 0; i < p.nreads && !hazard; ++i) hazard = rt->hz.conflicts(p.reads[i], false);
   if (!hazard) hazard = rt->hz.conflicts(p.write, true);
+  if (!hazard) hazard = rt->hz.conflicts(p.write2, true);
   if (hazard || rt->hz.size() > (1u << 20)) {
     rt->hz.clear();
     rt->seg_wait = rt->item_w;
   }
   for (int i = 0; i < p.nreads; ++i) rt->hz.insert(p.reads[i], false);
   rt->hz.insert(p.write, true);
+  rt->hz.insert(p.write2, true);
 
   // items carry the layout's unmasked sequence number (the worker masks it to a ring slot and
   // uses the full value as the key of its cached copy, so a reused slot never looks cached)
@@ -1261,6 +1264,47 @@ extern "C" int gpuos_rt_submit_reduce(gpuos_rt* rt, int red_op, const GpuosOpera
   if (e) return e;
   std::lock_guard<std::mutex> lk(rt->mu);
   return append_plan_locked(rt, plan, nullptr);
+}
+
+// Top-k of every row of x [rows, n] (contiguous): values [rows, k] in x's dtype and int64
+// indices [rows, k], both contiguous, largest or smallest first.  Rows are grouped so that a
+// group fits one stage (a row longer than a stage is read from global memory).
+extern "C" int gpuos_rt_submit_topk(gpuos_rt* rt, const void* x, int dtype, int64_t rows, int64_t n, void* values,
+                                    int64_t* indices, int k, int largest) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  if (!dtype_ok(dtype)) return fail(GPUOS_ERR_INVALID, "unsupported dtype (only float32, float16 and bfloat16)");
+  if (rows < 0 || n <= 0 || n >= (int64_t(1) << 31)) return fail(GPUOS_ERR_INVALID, "bad row count or row length");
+  if (k < 1 || k > n || k > kTopkMaxK) return fail(GPUOS_ERR_INVALID, "k must be in [1, min(n, %d)]", kTopkMaxK);
+  if (rows == 0) return GPUOS_OK;
+  if (!x || !values || !indices) return fail(GPUOS_ERR_INVALID, "null data pointer");
+  const int es = dtype_size(dtype);
+  static thread_local Plan p;
+  p.items.clear();
+  p.has_layout = false;
+  p.nreads = 0;
+  WorkItem proto;
+  std::memset(&proto, 0, sizeof(proto));
+  proto.kind = IK_TOPK;
+  proto.dt_a = proto.dt_o = (uint8_t)dtype;
+  proto.dt_b = kF32;
+  proto.aux = (uint32_t)n;
+  proto.x = (uint64_t)(uint32_t)k | ((uint64_t)(largest ? 1 : 0) << 32);
+  const int64_t row_bytes = n * es;
+  const int64_t rows_per = std::min<int64_t>(4096, std::max<int64_t>(1, ((int64_t)rt->stage_bytes - 32) / row_bytes));
+  const uint64_t X = (uint64_t)(uintptr_t)x, V = (uint64_t)(uintptr_t)values, I = (uint64_t)(uintptr_t)indices;
+  for (int64_t r0 = 0; r0 < rows; r0 += rows_per) {
+    WorkItem it = proto;
+    it.count = (uint32_t)std::min<int64_t>(rows_per, rows - r0);
+    it.a = X + (uint64_t)(r0 * row_bytes);
+    it.o = V + (uint64_t)(r0 * k * es);
+    it.b = I + (uint64_t)(r0 * k * 8);
+    p.items.push_back(it);
+  }
+  p.reads[p.nreads++] = Range{X, X + (uint64_t)(rows * row_bytes)};
+  p.write = Range{V, V + (uint64_t)(rows * k * es)};
+  p.write2 = Range{I, I + (uint64_t)(rows * k * 8)};
+  std::lock_guard<std::mutex> lk(rt->mu);
+  return append_plan_locked(rt, p, nullptr);
 }
 
 static Range tensorref_range(const TensorRef& t) {

@@ -62,7 +62,8 @@ def _storage_key(t: torch.Tensor) -> int:
     return t.data_ptr() - t.storage_offset() * t.element_size()
 
 
-# op overload -> (route, name): 1 binary, 2 unary, 3 parametric unary, 4 reduction, 0 not ours
+# op overload -> (route, name): 1 binary, 2 unary, 3 parametric unary, 4 reduction, 5 top-k,
+# 0 not ours
 _ROUTES: dict = {}
 
 
@@ -71,7 +72,7 @@ def _route(func):
     if r is None:
         name = func.name()
         kind = (1 if name in _BINARY else 2 if name in _UNARY else 3 if name in _PARAMETRIC
-                else 4 if name in _REDUCE else 0)
+                else 4 if name in _REDUCE else 5 if name == "aten::topk" else 0)
         r = _ROUTES[func] = (kind, name)
     return r
 
@@ -176,7 +177,10 @@ class _GPUOSSchedulerMode(TorchDispatchMode):
         if dtype not in _FLOATS:
             return None
         if out is None:
-            out = torch.empty(shape, dtype=dtype, device=a.device)
+            if shape == a.shape and dtype == a.dtype and a.is_contiguous():
+                out = torch.empty_like(a)  # the same contiguous tensor, allocated faster
+            else:
+                out = torch.empty(shape, dtype=dtype, device=a.device)
         elif not (isinstance(out, torch.Tensor) and out.is_cuda and out.dtype in _FLOATS):
             return None
         gpuos_ext.submit_elementwise(op, a, b if b_t else float(b), out, p0, 0.0)
@@ -271,6 +275,30 @@ class _GPUOSSchedulerMode(TorchDispatchMode):
         self.scheduled += 1
         return out
 
+    def _try_topk(self, args, kwargs):
+        """aten::topk(self, k, dim=-1, largest=True, sorted=True) along the last dim of a
+        contiguous tensor, k <= min(n, 256): the runtime's batched top-k (the reference sends
+        topk to torch::topk, scheduler.py:346-370).  The values come preferred first, which
+        also satisfies sorted=False."""
+        x = args[0]
+
+        def arg(i, key, default):
+            return kwargs[key] if key in kwargs else (args[i] if len(args) > i else default)
+
+        k, dim, largest = arg(1, "k", None), arg(2, "dim", -1), arg(3, "largest", True)
+        if not isinstance(k, int) or x.dim() == 0 or not x.is_contiguous():
+            return None
+        n = x.shape[-1]
+        if (dim if dim >= 0 else dim + x.dim()) != x.dim() - 1 or not (1 <= k <= min(n, 256)):
+            return None
+        shape = tuple(x.shape[:-1]) + (k,)
+        values = torch.empty(shape, dtype=x.dtype, device=x.device)
+        indices = torch.empty(shape, dtype=torch.int64, device=x.device)
+        gpuos_ext.submit_topk_rows(x, values, indices, k, bool(largest))
+        self._mark(x, values, indices)
+        self.scheduled += 1
+        return values, indices
+
     def __torch_dispatch__(self, func, types, args=(), kwargs=None):
         kind, name = _route(func)
         kwargs = kwargs or {}
@@ -285,8 +313,10 @@ class _GPUOSSchedulerMode(TorchDispatchMode):
                     res = self._schedule_unary(_UNARY[name], args[0])
                 elif kind == 3:
                     res = self._try_parametric(name, args, kwargs)
-                else:
+                elif kind == 4:
                     res = self._try_reduce(name, args, kwargs)
+                else:
+                    res = self._try_topk(args, kwargs)
         if res is not None:
             return res
         # Not scheduled: make sure no pending request reads or writes what this op touches.

@@ -189,6 +189,16 @@ int gpuos_rt_submit_ew(gpuos_rt* rt, int op, const GpuosOperand* a, const GpuosO
                        int b_is_scalar, double b_scalar, const GpuosOperand* out,
                        const float* params, int nparams);
 
+/* Batched top-k (replaces the torch::topk call behind submit_topk, gpuos_ext.cpp:1050-1071, on
+ * the persistent worker): for every row of x [rows, n] (contiguous, dtype a GpuosDtype float
+ * code) writes the k largest (largest != 0) or smallest elements, preferred first, to values
+ * [rows, k] (x's dtype) and their positions to indices [rows, k] (int64), both contiguous.  NaN
+ * counts as the largest value (as PyTorch's topk); equal values take the lower position first.
+ * 1 <= k <= min(n, 256).  Pending until gpuos_rt_flush, ordered against other requests that
+ * touch the same memory. */
+int gpuos_rt_submit_topk(gpuos_rt* rt, const void* x, int dtype, int64_t rows, int64_t n, void* values,
+                         int64_t* indices, int k, int largest);
+
 /* Batched reduction: out = sum|mean of x over `axes` (gpuos_ext.cpp:1016-1045). */
 int gpuos_rt_submit_reduce(gpuos_rt* rt, int red_op, const GpuosOperand* x,
                            const GpuosOperand* out, const int* axes, int naxes, int keepdim);
