@@ -705,53 +705,67 @@ def main():
                             "clocks": rclk}
 
         # ---- e2e: host buffers, H2D + D2H inside every step, through the public API.  Each
-        # step is split into 8 chunks of requests: the H2D copies of all chunks are queued on
-        # a copy-in stream, chunk c is flushed as soon as its copy has landed, and its D2H
-        # copy is queued on a copy-out stream once its flush ticket has completed, so the two
-        # copy directions and the worker overlap ----
+        # step is split into 8 chunks of requests: chunk c is flushed as soon as its H2D copy has
+        # landed and its D2H copy is queued once its flush ticket has completed, so the two copy
+        # directions and the worker overlap.  Two sets of device buffers alternate between
+        # steps, so the H2D copies of step s+1 are queued right behind those of step s (into the
+        # set step s-1 used, which is complete) and the copy engine never waits for the host ----
         hA, hB = A.pin_memory(), B.pin_memory()
         hO = torch.empty_like(hA).pin_memory()
+        sets = [(a, b, out, a_rows, b_rows, o_rows)]
+        a2, b2, out2 = torch.empty_like(a), torch.empty_like(b), torch.empty_like(out)
+        sets.append((a2, b2, out2, list(a2.unbind(0)), list(b2.unbind(0)), list(out2.unbind(0))))
         g.quiesce()
         barrier()
         cur = torch.cuda.current_stream()
         cs, ds = torch.cuda.Stream(), torch.cuda.Stream()
         nchunk = 8
         bounds = [(c * R // nchunk, (c + 1) * R // nchunk) for c in range(nchunk)]
-        out_done = [None] * nchunk
+        out_done = [[None] * nchunk for _ in range(2)]
+
+        def queue_h2d(k):
+            da, db = sets[k][0], sets[k][1]
+            evs = []
+            with torch.cuda.stream(cs):
+                for lo, hi in bounds:
+                    da[lo:hi].copy_(hA[lo:hi], non_blocking=True)
+                    db[lo:hi].copy_(hB[lo:hi], non_blocking=True)
+                    ev = torch.cuda.Event()
+                    ev.record(cs)
+                    evs.append(ev)
+            return evs
+
+        def queue_d2h(k, c):
+            lo, hi = bounds[c]
+            with torch.cuda.stream(ds):
+                hO[lo:hi].copy_(sets[k][2][lo:hi], non_blocking=True)
+                out_done[k][c] = torch.cuda.Event()
+                out_done[k][c].record(ds)
+
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         f0.record(cur)
         cs.wait_stream(cur)
         ds.wait_stream(cur)
-        for _ in range(args.steps):
-            landed = []
-            with torch.cuda.stream(cs):
-                for lo, hi in bounds:
-                    a[lo:hi].copy_(hA[lo:hi], non_blocking=True)
-                    b[lo:hi].copy_(hB[lo:hi], non_blocking=True)
-                    ev = torch.cuda.Event()
-                    ev.record(cs)
-                    landed.append(ev)
+        landed_next = queue_h2d(0)
+        for step in range(args.steps):
+            k = step % 2
+            landed = landed_next
+            if step + 1 < args.steps:
+                landed_next = queue_h2d(1 - k)  # the other set: its last step has completed
+            _, _, _, ar, br, orow = sets[k]
             seqs = []
             for c, (lo, hi) in enumerate(bounds):
                 for i in range(lo, hi):
-                    subs[i](a_rows[i], b_rows[i], o_rows[i])
+                    subs[i](ar[i], br[i], orow[i])
                 landed[c].synchronize()
-                if out_done[c] is not None:
-                    out_done[c].synchronize()  # the previous step's D2H of these rows has run
+                if out_done[k][c] is not None:
+                    out_done[k][c].synchronize()  # the D2H of this set's rows two steps ago has run
                 seqs.append(g.flush())
                 if c:
                     g.wait(seqs[c - 1])
-                    plo, phi = bounds[c - 1]
-                    with torch.cuda.stream(ds):
-                        hO[plo:phi].copy_(out[plo:phi], non_blocking=True)
-                        out_done[c - 1] = torch.cuda.Event()
-                        out_done[c - 1].record(ds)
+                    queue_d2h(k, c - 1)
             g.wait(seqs[-1])
-            plo, phi = bounds[-1]
-            with torch.cuda.stream(ds):
-                hO[plo:phi].copy_(out[plo:phi], non_blocking=True)
-                out_done[-1] = torch.cuda.Event()
-                out_done[-1].record(ds)
+            queue_d2h(k, nchunk - 1)
         cur.wait_stream(ds)
         cur.wait_stream(cs)
         f1.record(cur)
@@ -760,7 +774,8 @@ def main():
         line["e2e"] = {"value": job_rate(R * args.steps, world, e2e_ms), "unit": UNIT,
                        "h2d_bytes_per_step": 2 * R * N * 4, "d2h_bytes_per_step": R * N * 4,
                        "correct": bool(torch.equal(hO, ref)),
-                       "how": "8 chunks per step; H2D, worker and D2H overlap across chunks"}
+                       "how": "8 chunks per step; H2D, worker and D2H overlap across chunks; two device "
+                              "buffer sets alternate so the next step's H2D queues behind this one's"}
 
         # ---- latency: single 4096-element requests, sync flush each ----
         g.set_idle_quiesce_ms(200)
