@@ -792,6 +792,25 @@ def main():
         line["latency_us"] = {"p50": lat[len(lat) // 2], "p99": lat[int(len(lat) * 0.99)],
                               "load": "one 4096-element request per sync flush, back to back"}
 
+        # ---- the same step through the bulk submitter (one submit_many call per step) ----
+        g.set_idle_quiesce_ms(200 if args.worker_mode == "persistent" else 0)
+        codes = [g.EW_ADD if int(o) == 0 else g.EW_MUL for o in ops]
+        for _ in range(3):
+            g.submit_many(codes, a_rows, b_rows, o_rows)
+            g.flush(sync=True)
+        m0, m1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        m0.record()
+        for _ in range(args.steps):
+            g.submit_many(codes, a_rows, b_rows, o_rows)
+            g.flush(sync=True)
+        m1.record()
+        m1.synchronize()
+        bulk_ok = bool(torch.equal(out.cpu(), ref))
+        line["bulk_submit"] = {"value": job_rate(R * args.steps, world, max_over_ranks(m0.elapsed_time(m1))),
+                               "unit": UNIT, "correct": bulk_ok,
+                               "what": "the same steps with one submit_many call per step instead of "
+                                       f"{R} submit_add/submit_mul calls (inputs in HBM)"}
+
         # ---- baseline (b): GPU per-op torch eager ----
         g.quiesce()
         torch.cuda.synchronize()

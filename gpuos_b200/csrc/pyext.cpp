@@ -1046,6 +1046,74 @@ PyObject* py_submit_topk_rows(PyObject*, PyObject* args) {
   Py_RETURN_NONE;
 }
 
+// submit_many(ops, a, b, out) — many element-wise requests in one call: a, b and out are
+// sequences of tensors of one length (b may be None when every op is unary), ops one op code
+// or a sequence of codes.  Nothing is submitted if any request is invalid.
+struct FastSeq {
+  PyObject* o = nullptr;
+  ~FastSeq() { Py_XDECREF(o); }
+};
+
+PyObject* py_submit_many(PyObject*, PyObject* const* args, Py_ssize_t nargs) {
+  if (nargs != 4) {
+    PyErr_SetString(PyExc_TypeError, "expected (ops, a, b, out)");
+    return nullptr;
+  }
+  FastSeq fa, fb, fo, fops;
+  if (!(fa.o = PySequence_Fast(args[1], "a must be a sequence of tensors"))) return nullptr;
+  if (args[2] != Py_None && !(fb.o = PySequence_Fast(args[2], "b must be a sequence of tensors or None")))
+    return nullptr;
+  if (!(fo.o = PySequence_Fast(args[3], "out must be a sequence of tensors"))) return nullptr;
+  const Py_ssize_t n = PySequence_Fast_GET_SIZE(fa.o);
+  if (PySequence_Fast_GET_SIZE(fo.o) != n || (fb.o && PySequence_Fast_GET_SIZE(fb.o) != n))
+    return PyErr_Format(PyExc_ValueError, "a, b and out must have the same length");
+  long op_all = -1;
+  if (PyLong_Check(args[0])) {
+    op_all = PyLong_AsLong(args[0]);
+  } else {
+    if (!(fops.o = PySequence_Fast(args[0], "ops must be an op code or a sequence of op codes"))) return nullptr;
+    if (PySequence_Fast_GET_SIZE(fops.o) != n) return PyErr_Format(PyExc_ValueError, "ops must have one code per request");
+  }
+  if (n == 0) Py_RETURN_NONE;
+  static thread_local std::vector<GpuosOperand> va, vb, vo;
+  static thread_local std::vector<int> vops;
+  va.resize((size_t)n);
+  vb.resize((size_t)n);
+  vo.resize((size_t)n);
+  vops.resize((size_t)n);
+  PyObject** ia = PySequence_Fast_ITEMS(fa.o);
+  PyObject** ib = fb.o ? PySequence_Fast_ITEMS(fb.o) : nullptr;
+  PyObject** io = PySequence_Fast_ITEMS(fo.o);
+  int dev = -1;
+  for (Py_ssize_t i = 0; i < n; ++i) {
+    if (fops.o) {
+      const long v = PyLong_AsLong(PySequence_Fast_GET_ITEM(fops.o, i));
+      if (v == -1 && PyErr_Occurred()) return nullptr;
+      vops[(size_t)i] = (int)v;
+    } else {
+      vops[(size_t)i] = (int)op_all;
+    }
+    const int d1 = to_operand(ia[i], &va[(size_t)i], "a");
+    if (d1 < 0) return nullptr;
+    const int d3 = to_operand(io[i], &vo[(size_t)i], "out");
+    if (d3 < 0) return nullptr;
+    int d2 = d1;
+    if (ib && (d2 = to_operand(ib[i], &vb[(size_t)i], "b")) < 0) return nullptr;
+    if (dev < 0) dev = d1;
+    if (d1 != dev || d2 != dev || d3 != dev) return PyErr_Format(PyExc_RuntimeError, "device mismatch");
+  }
+  gpuos_rt* rt = rt_for(dev);
+  if (!rt) return nullptr;
+  const int st = gpuos_rt_submit_ew_many(rt, (int)n, vops.data(), va.data(), ib ? vb.data() : nullptr, vo.data());
+  if (st) return raise_status(st);
+  for (Py_ssize_t i = 0; i < n; ++i) {
+    keep(dev, ia[i]);
+    if (ib) keep(dev, ib[i]);
+    keep(dev, io[i]);
+  }
+  Py_RETURN_NONE;
+}
+
 PyMethodDef kMethods[] = {
     {"init", (PyCFunction)(void (*)(void))py_init, METH_VARARGS | METH_KEYWORDS,
      "init(capacity=4096, threads_per_block=256, device=None)"},
@@ -1066,6 +1134,8 @@ PyMethodDef kMethods[] = {
      "submit_elementwise(op, a, b, out, p0=0.0, p1=0.0)"},
     {"submit_topk_rows", py_submit_topk_rows, METH_VARARGS,
      "submit_topk_rows(x, values, indices, k, largest): top-k of each row of x (pending until flush)"},
+    {"submit_many", (PyCFunction)(void (*)(void))py_submit_many, METH_FASTCALL,
+     "submit_many(ops, a, b, out): many element-wise requests in one call (pending until flush)"},
     {"submit_reduction", (PyCFunction)(void (*)(void))py_submit_reduction, METH_FASTCALL,
      "submit_reduction(op, x, out, axes, keepdim)"},
     {"flush", (PyCFunction)(void (*)(void))py_flush, METH_VARARGS | METH_KEYWORDS, "flush(sync=False, device=None) -> ticket"},

@@ -1255,6 +1255,36 @@ extern "C" int gpuos_rt_submit_ew(gpuos_rt* rt, int op, const GpuosOperand* a, c
   return append_plan_locked(rt, plan, nullptr);
 }
 
+// Several element-wise requests in one call: every request is planned (and validated) before
+// any is appended, then all are appended under one acquisition of the runtime lock.
+extern "C" int gpuos_rt_submit_ew_many(gpuos_rt* rt, int n, const int* ops, const GpuosOperand* a,
+                                       const GpuosOperand* b, const GpuosOperand* out) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  if (n < 0) return fail(GPUOS_ERR_INVALID, "negative request count");
+  if (n == 0) return GPUOS_OK;
+  if (!ops || !a || !out) return fail(GPUOS_ERR_INVALID, "null operand array");
+  static thread_local std::vector<Plan> plans;
+  if ((int)plans.size() < n) plans.resize((size_t)n);
+  for (int i = 0; i < n; ++i) {
+    EwReq r;
+    r.op = ops[i];
+    r.a = &a[i];
+    r.b = b ? &b[i] : nullptr;
+    r.b_imm = false;
+    r.b_val = 0.f;
+    r.out = &out[i];
+    for (int k = 0; k < 4; ++k) r.params[k] = 0.f;
+    const int e = plan_ew(r, kHalfBytes, &plans[(size_t)i]);
+    if (e) return e;
+  }
+  std::lock_guard<std::mutex> lk(rt->mu);
+  for (int i = 0; i < n; ++i) {
+    const int e = append_plan_locked(rt, plans[(size_t)i], nullptr);
+    if (e) return e;
+  }
+  return GPUOS_OK;
+}
+
 extern "C" int gpuos_rt_submit_reduce(gpuos_rt* rt, int red_op, const GpuosOperand* x, const GpuosOperand* out,
                                       const int* axes, int naxes, int keepdim) {
   if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");

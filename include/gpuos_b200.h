@@ -199,6 +199,13 @@ int gpuos_rt_submit_ew(gpuos_rt* rt, int op, const GpuosOperand* a, const GpuosO
 int gpuos_rt_submit_topk(gpuos_rt* rt, const void* x, int dtype, int64_t rows, int64_t n, void* values,
                          int64_t* indices, int k, int largest);
 
+/* Bulk form of gpuos_rt_submit_ew for n requests: request i is ops[i] on a[i], b[i] (b may be
+ * NULL when every op is unary) and out[i], parameters 0.  A bulk submitter beside the
+ * reference's one-call-per-op submit_* (gpuos_ext.cpp:638-672): every request is validated
+ * before any is submitted, and all are appended under one lock acquisition. */
+int gpuos_rt_submit_ew_many(gpuos_rt* rt, int n, const int* ops, const GpuosOperand* a, const GpuosOperand* b,
+                            const GpuosOperand* out);
+
 /* Batched reduction: out = sum|mean of x over `axes` (gpuos_ext.cpp:1016-1045). */
 int gpuos_rt_submit_reduce(gpuos_rt* rt, int red_op, const GpuosOperand* x,
                            const GpuosOperand* out, const int* axes, int naxes, int keepdim);
