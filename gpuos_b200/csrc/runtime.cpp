@@ -1066,8 +1066,9 @@ static void keeper_main(gpuos_rt* rt) {
     std::lock_guard<std::mutex> lk(rt->mu);
     rt->hc->host_beat = rt->hc->host_beat + 1;
     reap_locked(rt);
-    if (rt->launched && rt->idle_quiesce_ms > 0 && rt->inflight.empty() && rt->pend_reqs == 0 &&
-        rt->item_w == rt->item_pub && rt->hc->quit_epoch < rt->epoch &&
+    // idle: nothing published is in flight (requests not yet flushed do not need the worker,
+    // and their flush relaunches it), so kernels on other streams get the SMs back
+    if (rt->launched && rt->idle_quiesce_ms > 0 && rt->inflight.empty() && rt->hc->quit_epoch < rt->epoch &&
         mono_ns() - rt->last_activity_ns > (uint64_t)rt->idle_quiesce_ms * 1000000ull) {
       rt->hc->quit_epoch = rt->epoch;
     }
@@ -1402,7 +1403,16 @@ extern "C" int gpuos_rt_flush(gpuos_rt* rt, int flags, cudaStream_t dep_stream, 
     cudaError_t q = cudaStreamQuery(dep_stream);
     if (q == cudaErrorNotReady) {
       const uint64_t t0 = mono_ns();
+      bool asked = false;
       while ((q = cudaStreamQuery(dep_stream)) == cudaErrorNotReady) {
+        if (!asked && mono_ns() - t0 > 50ull * 1000) {
+          // The kernels on the caller's stream may need the SM resources the resident worker
+          // holds (all of them at 448 compute threads): stop the worker (work already
+          // published drains first); this flush's publish relaunches it.
+          std::lock_guard<std::mutex> lk(rt->mu);
+          if (rt->launched && rt->hc->quit_epoch < rt->epoch) rt->hc->quit_epoch = rt->epoch;
+          asked = true;
+        }
         if (mono_ns() - t0 > 30ull * 1000 * 1000 * 1000) return fail(GPUOS_ERR_TIMEOUT, "dependency stream did not drain");
         std::this_thread::yield();
       }

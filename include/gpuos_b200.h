@@ -251,11 +251,13 @@ int gpuos_rt_quiesce(gpuos_rt* rt, int timeout_ms);
 int gpuos_rt_set_debug_level(gpuos_rt* rt, int level);
 int gpuos_rt_set_yield_every(gpuos_rt* rt, uint64_t every);
 /* Host-side idle time after which the worker is stopped (0: stop after every drain; -1:
- * never; default 200, env GPUOS_IDLE_QUIESCE_MS).  A resident worker occupies every SM
- * (registers and shared memory), so kernels on other streams of the device wait until it
- * stops.  With -1 they wait until gpuos_rt_quiesce or shutdown: a blocking CUDA call that
- * waits for such a kernel (a synchronous copy, a stream synchronize) does not return
- * before then, and a flush whose inputs come from such a kernel fails after 30 s. */
+ * never; default 200, env GPUOS_IDLE_QUIESCE_MS).  The worker is idle when nothing flushed
+ * is in flight (requests not yet flushed do not keep it).  A resident worker holds most of
+ * every SM (all of its registers at 448 compute threads), so kernels on other streams that
+ * do not fit beside it wait until it stops.  A flush whose inputs come from such a kernel
+ * stops the worker itself and relaunches it.  With -1 other waits last until
+ * gpuos_rt_quiesce or shutdown: a blocking CUDA call that waits for such a kernel (a
+ * synchronous copy, a stream synchronize) does not return before then. */
 int gpuos_rt_set_idle_quiesce_ms(gpuos_rt* rt, int ms);
 /* Bound (ms) of the worker's in-grid waits (default 5000, env GPUOS_DEVICE_WAIT_MS).  A
  * worker reads the bound when it is launched, so a running worker is stopped first

@@ -162,3 +162,39 @@ def test_errors_are_exceptions(rt):
         rt.submit_add(a.double(), a.double(), a.double())
     with pytest.raises(RuntimeError, match="CUDA"):
         rt.submit_add(a.cpu(), a.cpu(), a.cpu())
+
+
+def test_inputs_from_kernels_queued_behind_a_full_worker(rt):
+    # At 448 compute threads one worker CTA holds every register of its SM, so a PyTorch kernel
+    # queued after the worker started cannot run before the worker stops.  A flush whose
+    # inputs come from such a kernel must stop the worker itself, and an idle worker must stop
+    # even while requests wait unflushed, or the caller's stream never drains.
+    import time as _t
+
+    def drained(limit_s=5.0):
+        t0 = _t.monotonic()
+        while not torch.cuda.current_stream().query():
+            if _t.monotonic() - t0 > limit_s:
+                return False
+            _t.sleep(0.001)
+        return True
+
+    rt.shutdown()
+    try:
+        rt.init(capacity=8192, threads_per_block=448)
+        x = torch.randn(1 << 16, device="cuda")  # queued behind the resident worker
+        y = torch.empty_like(x)
+        t0 = _t.monotonic()
+        rt.submit_add(x, x, y)
+        rt.flush(sync=True)
+        assert _t.monotonic() - t0 < 5.0
+        assert drained()
+        assert torch.equal(y.cpu(), x.cpu() + x.cpu())
+        z = torch.randn(1 << 16, device="cuda")
+        rt.submit_mul(z, z, y)  # pending, not flushed: the idle worker still stops
+        assert drained()
+        rt.flush(sync=True)
+        assert torch.equal(y.cpu(), z.cpu() * z.cpu())
+    finally:
+        rt.shutdown()
+        rt.init(capacity=8192, threads_per_block=256)
