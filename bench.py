@@ -704,6 +704,27 @@ def main():
                                                     "traffic": traffic1},
                             "clocks": rclk}
 
+        # ---- the same bytes through one library kernel: torch.add over the whole 4096x4096
+        # step in one launch (2 reads : 1 write, like the worker's step) ----
+        g.quiesce()
+        torch.cuda.synchronize()
+        for _ in range(3):
+            torch.add(a, b, out=out)
+        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        kreps = 20
+        k0.record()
+        for _ in range(kreps):
+            torch.add(a, b, out=out)
+        k1.record()
+        k1.synchronize()
+        lib_gbs = R * N * BYTES_PER_ELEM / (k0.elapsed_time(k1) / kreps * 1e-3) / 1e9
+        line["roofline"]["same_traffic_library_kernel"] = {
+            "what": "torch.add(a, b, out=out) over the step's 4096x4096 fp32 in one launch, CUDA events",
+            "achieved": lib_gbs, "frac": lib_gbs / peak, "worker_over_library": achieved / lib_gbs}
+        for i in range(R):  # restore the step's results for the checks below
+            subs[i](a_rows[i], b_rows[i], o_rows[i])
+        g.flush(sync=True)
+
         # ---- e2e: host buffers, H2D + D2H inside every step, through the public API.  Each
         # step is split into 8 chunks of requests: chunk c is flushed as soon as its H2D copy has
         # landed and its D2H copy is queued once its flush ticket has completed, so the two copy
