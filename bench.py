@@ -66,6 +66,7 @@ def parse():
     p.add_argument("--workload", choices=["c1", "c2", "c3", "c4"], default="c1",
                    help="c1: the headline workload (default).  c2-c4: the mixed-op, strided/broadcast "
                         "mixed-dtype and reduction streams, one GPU, measured for the kernel's roofline")
+    p.add_argument("--e2e-chunks", type=int, default=4, help="chunks per step of the e2e pipeline")
     p.add_argument("--config-requests", type=int, default=0,
                    help="c2-c4: requests per step (default: the configuration's full count)")
     return p.parse_args()
@@ -726,7 +727,8 @@ def main():
         g.flush(sync=True)
 
         # ---- e2e: host buffers, H2D + D2H inside every step, through the public API.  Each
-        # step is split into 8 chunks of requests: chunk c is flushed as soon as its H2D copy has
+        # step is split into chunks of requests (4 by default; 2, 4, 8, 16 measured 1.44, 1.43,
+        # 1.35, 1.22 M ops/s: every chunk costs host waits): chunk c is flushed as soon as its H2D copy has
         # landed and its D2H copy is queued once its flush ticket has completed, so the two copy
         # directions and the worker overlap.  Two sets of device buffers alternate between
         # steps, so the H2D copies of step s+1 are queued right behind those of step s (into the
@@ -740,7 +742,7 @@ def main():
         barrier()
         cur = torch.cuda.current_stream()
         cs, ds = torch.cuda.Stream(), torch.cuda.Stream()
-        nchunk = 8
+        nchunk = max(1, args.e2e_chunks)
         bounds = [(c * R // nchunk, (c + 1) * R // nchunk) for c in range(nchunk)]
         out_done = [[None] * nchunk for _ in range(2)]
 
@@ -795,7 +797,7 @@ def main():
         line["e2e"] = {"value": job_rate(R * args.steps, world, e2e_ms), "unit": UNIT,
                        "h2d_bytes_per_step": 2 * R * N * 4, "d2h_bytes_per_step": R * N * 4,
                        "correct": bool(torch.equal(hO, ref)),
-                       "how": "8 chunks per step; H2D, worker and D2H overlap across chunks; two device "
+                       "how": f"{nchunk} chunks per step; H2D, worker and D2H overlap across chunks; two device "
                               "buffer sets alternate so the next step's H2D queues behind this one's"}
 
         # ---- latency: single 4096-element requests, sync flush each ----
