@@ -63,9 +63,11 @@ def parse():
     p.add_argument("--no-extras", action="store_true", help="skip baselines, latency, e2e (profiling runs)")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--latency-samples", type=int, default=2000)
-    p.add_argument("--workload", choices=["c1", "c2", "c3", "c4"], default="c1",
+    p.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "c5"], default="c1",
                    help="c1: the headline workload (default).  c2-c4: the mixed-op, strided/broadcast "
-                        "mixed-dtype and reduction streams, one GPU, measured for the kernel's roofline")
+                        "mixed-dtype and reduction streams, one GPU, measured for the kernel's roofline.  "
+                        "c5: dependent chains over N runtimes with an NVRTC op_mul switched in at request "
+                        "50000, a dual-slot switch and a rollback (torchrun for N > 1)")
     p.add_argument("--e2e-chunks", type=int, default=4, help="chunks per step of the e2e pipeline")
     p.add_argument("--config-requests", type=int, default=0,
                    help="c2-c4: requests per step (default: the configuration's full count)")
@@ -229,8 +231,26 @@ def cpu_threads():
         return os.cpu_count() or 1
 
 
+def time_cpu_path(cpu: CpuPath, warm_passes: int, min_passes: int, seconds: float, warm_seconds: float = 3.0):
+    """Steady-state rate of the CPU path: warm-up until both `warm_passes` passes and
+    `warm_seconds` have gone by (process pool, page faults, clocks), then time passes until both
+    `min_passes` passes and `seconds` have gone by.  Returns (passes timed, seconds)."""
+    t0 = time.perf_counter()
+    k = 0
+    while k < warm_passes or time.perf_counter() - t0 < warm_seconds:
+        cpu.run()
+        k += 1
+    n = 0
+    t0 = time.perf_counter()
+    while n < min_passes or time.perf_counter() - t0 < seconds:
+        cpu.run()
+        n += 1
+    return n, time.perf_counter() - t0
+
+
 def run_reference(args, rank, world):
-    """The reference's CPU path: PyTorch CPU eager over the identical request stream."""
+    """The reference's CPU path: PyTorch CPU eager over the identical request stream, timed over
+    the same steady-state window as the cpu_baseline leg of the GPU arm."""
     if rank != 0:
         return None
     import oracle.reference_semantics  # noqa: F401  (CPU path lives with the oracle)
@@ -238,23 +258,19 @@ def run_reference(args, rank, world):
     A, B, ops = workload(0, args.requests, args.numel)
     out = torch.empty_like(A)
     cpu = CpuPath(A, B, out, ops.tolist(), threads)
-    for _ in range(args.warmup):
-        cpu.run()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        cpu.run()
-    dt = time.perf_counter() - t0
+    passes, dt = time_cpu_path(cpu, args.warmup, args.steps, args.cpu_seconds)
     cpu.close()
     ok = torch.equal(out, torch.where(ops[:, None] == 0, A + B, A * B))
-    v = args.requests * args.steps / dt
+    v = args.requests * passes / dt
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / passes * 1e3, "timed_passes": passes,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded U(-1,1))",
         "config": {"workload": WORKLOAD, "requests": args.requests, "numel": args.numel, "l2": "inputs > L2"},
         "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{args.steps} steps x {args.requests} requests (full workload)"},
+                         "sample": f"{passes} passes x {args.requests} requests in {dt:.1f} s after >= 3 s of "
+                                   f"warm-up (full workload)"},
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "correct": bool(ok),
     }
@@ -459,6 +475,234 @@ def build_c4(g_ext, seed=1234 + 4, n_req=8192):
     return reqs, nbytes, check, desc, {}
 
 
+# ---- config 5: dependent chains over per-GPU runtimes with an online switch, a dual-slot switch
+# and a rollback (test/online_switch.cpp:170-228, test/dual_slot_switch.cpp:139-168) -------------
+C5_SWITCH = (50000, 55000, 60000)   # global request index at which phases 1, 2, 3 begin
+C5_SENTINEL = 1234.5678              # initial value of every chain output (a lost request keeps it)
+
+
+def c5_workload(chains=2048, depth=32, n=4096, seed=1234 + 5):
+    """Op of step k of chain c drawn uniformly from the 19 config-2 operators; a chain's start
+    value ~ U(-4,4); binary operators take a per-chain second operand (U(0.5,2) for div and
+    pow's exponent, U(-4,4) otherwise).  Values can leave every operator's domain on the way
+    (log of a negative, exp overflow): IEEE results (NaN, inf) are compared like any other."""
+    g = torch.Generator().manual_seed(seed)
+    kinds = torch.randint(0, 19, (chains, depth), generator=g)
+    y0 = torch.rand(chains, n, generator=g) * 8 - 4
+    yg = torch.rand(chains, n, generator=g) * 8 - 4
+    yp = torch.rand(chains, n, generator=g) * 1.5 + 0.5
+    return kinds, y0, yg, yp
+
+
+def _rows_within(got, ref, exact, x, name):
+    """Per-row check (bool per row): bit-exact, or within 2 ulp (GELU: PyTorch CPU's own error
+    bound); NaN matches NaN."""
+    gn, rn = torch.isnan(got), torch.isnan(ref)
+    gi = got.contiguous().view(torch.int32).to(torch.int64)
+    ri = ref.contiguous().view(torch.int32).to(torch.int64)
+    gi = torch.where(gi < 0, -(gi & 0x7FFFFFFF), gi)
+    ri = torch.where(ri < 0, -(ri & 0x7FFFFFFF), ri)
+    d = (gi - ri).abs()
+    ok = d == 0 if exact else d <= 2
+    if name == "gelu":
+        ok |= (got - ref).abs() <= 8 * x.abs() * 2.0 ** -24
+    ok = torch.where(gn | rn, gn & rn, ok)
+    return ok.all(dim=1)
+
+
+def c5_run(g, rank, world, barrier, chains=2048, depth=32, n=4096, n_probe=2, reps=1, warmup=0):
+    """Runs the config-5 stream `warmup + reps` times on this rank's chains and returns a dict of
+    measurements and checks.  Every pass: slot 0 = add, alias 0 = 0 at the start; a multiply
+    compiled by NVRTC for sm_100a is staged (compiled and linked) before the pass and committed
+    into slot 0 at request 50000 (online switch); at 55000 slot 0 returns to add and logical 0
+    is routed to physical slot 1 holding the compiled multiply (dual-slot switch); at 60000 the
+    alias is rolled back.  Each phase change is an epoch fence: every rank completes its requests
+    below the index, all ranks meet (barrier), switch, and meet again."""
+    ops = _c2_ops()
+    kinds_all, y0, yg, yp = c5_workload(chains, depth, n)
+    mine = [c for c in range(chains) if c % world == rank]
+    m = len(mine)
+    kinds = kinds_all[mine]
+    kl = kinds.tolist()
+    Yd = torch.full((depth + 1, m, n), C5_SENTINEL, device="cuda")
+    YG, YP = yg[mine].cuda(), yp[mine].cuda()
+    i = torch.arange(n, dtype=torch.float32)
+    PA, PB = (0.5 * i).cuda(), (1.0 + (torch.arange(n) % 5).float()).cuda()
+    codes = [getattr(g, o[1]) for o in ops]
+    binary = [o[2] for o in ops]
+    params = [o[3] for o in ops]
+    uses_p = [o[0] in ("div", "pow") for o in ops]
+    sub_ew, sub_bin, flush = g.submit_elementwise, g.submit_binary, g.flush
+    add0, mul1 = g.builtin_op_address(0), g.builtin_op_address(1)
+    # global order: request index k * chains + c (step k of chain c)
+    plan = [[(j, k * chains + c) for j, c in enumerate(mine)] for k in range(depth)]
+    results = []
+    for rep in range(warmup + reps):
+        Yd[1:].fill_(C5_SENTINEL)
+        Yd[0].copy_(y0[mine].cuda())
+        g.set_slot(0, add0)
+        g.set_slot(1, mul1)
+        g.set_alias(0, 0)
+        t_stage = time.perf_counter()
+        staged = g.jit_stage("A * B", 2)        # compiled + linked ahead of the switch point
+        t_stage = time.perf_counter() - t_stage
+        probes = []                              # (phase, output)
+        lat = []
+        fences = []
+        phase = 0
+        jit_addr = None
+        torch.cuda.synchronize()
+        barrier()
+        t0 = time.perf_counter()
+        for k in range(depth):
+            row_in, row_out = Yd[k], Yd[k + 1]
+            segs = [[]]
+            for j, gi in plan[k]:
+                if phase + len(segs) - 1 < len(C5_SWITCH) and gi >= C5_SWITCH[phase + len(segs) - 1]:
+                    segs.append([])
+                segs[-1].append(j)
+            for si, seg in enumerate(segs):
+                if si > 0:
+                    # epoch fence: everything below the switch index is complete on every rank
+                    tf = time.perf_counter()
+                    barrier()
+                    phase += 1
+                    if phase == 1:
+                        g.jit_commit(staged, 0)              # online switch: slot 0 multiplies
+                        jit_addr = g.get_slot(0)
+                    elif phase == 2:
+                        g.set_slot(0, add0)                  # undo, then route 0 -> physical slot 1
+                        g.set_slot(1, jit_addr)
+                        g.set_alias(0, 1)
+                    else:
+                        g.set_alias(0, 0)                    # rollback
+                    barrier()
+                    fences.append((time.perf_counter() - tf) * 1e3)
+                ts = []
+                for j in seg:
+                    kd = kl[j][k]
+                    y = (YP[j] if uses_p[kd] else YG[j]) if binary[kd] else None
+                    ts.append(time.perf_counter_ns())
+                    sub_ew(codes[kd], row_in[j], y, row_out[j], *params[kd])
+                for _ in range(n_probe if seg else 0):
+                    o = torch.empty_like(PA)
+                    sub_bin(0, PA, PB, o)
+                    probes.append((phase, o))
+                flush(True)
+                te = time.perf_counter_ns()
+                lat.extend((te - t) / 1e3 for t in ts)
+        while phase < len(C5_SWITCH):  # a rank with no request past an index still takes part
+            barrier()
+            phase += 1
+            barrier()
+        torch.cuda.synchronize()
+        elapsed = time.perf_counter() - t0
+        results.append({"elapsed_s": elapsed, "lat": lat, "fences_ms": fences, "probes": probes,
+                        "stage_s": t_stage})
+    # restore the table
+    g.set_alias(0, 0)
+    g.set_slot(0, add0)
+    g.set_slot(1, mul1)
+    # ---- checks of the last pass: every request against PyTorch CPU on the GPU's own input ----
+    Y = Yd.cpu()
+    YGc, YPc = YG.cpu(), YP.cpu()
+    lost = wrong = 0
+    for k in range(depth):
+        for kd, (name, code, bin_, prm, exact, fn) in enumerate(ops):
+            rows = (kinds[:, k] == kd).nonzero().flatten()
+            if rows.numel() == 0:
+                continue
+            x = Y[k][rows]
+            y = (YPc if uses_p[kd] else YGc)[rows] if bin_ else None
+            ref = fn(x, y)
+            got = Y[k + 1][rows]
+            ok = _rows_within(got, ref, exact, x, name)
+            untouched = (got == C5_SENTINEL).all(dim=1) & ~(ref == C5_SENTINEL).all(dim=1)
+            lost += int(untouched.sum())
+            wrong += int((~ok & ~untouched).sum())
+    padd, pmul = (PA + PB).cpu(), (PA * PB).cpu()
+    last = results[-1]
+    mis = 0
+    per_phase = [0, 0, 0, 0]
+    for ph, o in last["probes"]:
+        per_phase[ph] += 1
+        ref = pmul if ph in (1, 2) else padd
+        if not torch.equal(o.cpu(), ref):
+            mis += 1
+    finite = float(torch.isfinite(Y[depth]).float().mean())
+    return {"requests": m * depth, "results": results, "lost": lost, "wrong": wrong, "misdispatched": mis,
+            "probes_per_phase": per_phase, "finite_fraction_final": finite}
+
+
+def run_c5_bench(args):
+    """Config 5 at N GPUs (one rank per GPU under torchrun): the 2048 x 32 chain stream split
+    round-robin over the ranks' runtimes ("strong" scaling: the total work is fixed).  Fences
+    and the max over ranks use a gloo group (host only: a barrier needs no SM of a GPU whose
+    worker is running).  value = all requests / slowest rank's pass time, fences included."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+    torch.cuda.set_device(local if world > 1 else 0)
+    from gpuos_b200 import gpuos_ext as g
+    g.init(capacity=8192, threads_per_block=256)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    l0 = g.launches()
+    clocks = Clocks(torch.cuda.current_device())
+    clocks.start()
+    r = c5_run(g, rank, world, barrier, reps=args.steps, warmup=max(0, args.warmup))
+    clk = clocks.stop()
+    launches = g.launches() - l0
+    res = r["results"][max(0, args.warmup):]
+    el = [x["elapsed_s"] for x in res]
+    lat = [v for x in res for v in x["lat"]]
+    tot = torch.tensor([r["lost"], r["wrong"], r["misdispatched"], r["requests"]], dtype=torch.float64)
+    mx = torch.tensor(el + [max(f for x in res for f in x["fences_ms"])], dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(tot)
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        lat_t = torch.tensor(lat, dtype=torch.float64)
+        gathered = [torch.zeros_like(lat_t) for _ in range(world)]
+        dist.all_gather(gathered, lat_t)
+        lat = torch.cat(gathered).tolist()
+    g.shutdown()
+    if rank == 0:
+        ms = statistics.median(mx[:-1].tolist()) * 1e3
+        lat.sort()
+        q = lambda p: lat[min(len(lat) - 1, int(p * len(lat)))]  # noqa: E731
+        total = int(tot[3])
+        line = {
+            "metric": METRIC, "value": total / (ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": len(res),
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32 compute", "data": "synthetic (seeded)",
+            "config": {"workload": "config 5: 2048 chains x 32 dependent element-wise ops on [4096] fp32 "
+                                   "(ops uniform over the 19 config-2 operators), one sync flush per chain step, "
+                                   "chains round-robin over the ranks' runtimes; NVRTC op_mul committed into slot 0 "
+                                   "at request 50000, dual-slot switch at 55000, rollback at 60000",
+                       "requests": total, "switch_at": list(C5_SWITCH),
+                       "parallelism": f"{world} independent runtimes, host gloo barriers at the switch points"},
+            "latency_us": {"p50": q(0.5), "p99": q(0.99), "what": "submit call to return of the step's sync flush"},
+            "lost": int(tot[0]), "wrong": int(tot[1]), "misdispatched": int(tot[2]),
+            "probes_per_phase_rank0": r["probes_per_phase"], "fence_ms_max": float(mx[-1]),
+            "stage_s_rank0": statistics.median(x["stage_s"] for x in res),
+            "finite_fraction_final_rank0": r["finite_fraction_final"],
+            "gpu_launches": launches, "clocks": clk,
+            "what": "value: all requests of a pass / slowest rank's pass (host clock, fences included); "
+                    "every request checked against PyTorch CPU on its GPU input; probes through op 0 per segment",
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_config(args):
     """One GPU: every request of the configuration submitted through the runtime's calls, then
     one flush(sync=True) per step.  `value` is requests/s with the submit calls; `device` is the
@@ -555,7 +799,10 @@ def c2_scheduler(args, extra):
 
 def main():
     args = parse()
-    if args.workload != "c1":
+    if args.workload == "c5" and args.impl == "ours":
+        run_c5_bench(args)
+        return
+    if args.workload not in ("c1", "c5"):
         run_config(args)
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -858,18 +1105,11 @@ def main():
         if rank == 0 and world == 1:
             threads = cpu_threads()
             cpu = CpuPath(A.clone(), B.clone(), torch.empty_like(A), ops_l, threads)
-            cpu.run()
-            steps = 0
-            t0 = time.perf_counter()
-            while True:
-                cpu.run()
-                steps += 1
-                if time.perf_counter() - t0 >= args.cpu_seconds:
-                    break
-            dt = time.perf_counter() - t0
+            steps, dt = time_cpu_path(cpu, args.warmup, args.steps, args.cpu_seconds)
             cpu.close()
             line["cpu_baseline"] = {"value": R * steps / dt, "unit": UNIT, "cores": threads, "kind": "port",
-                                    "sample": f"{steps} steps x {R} requests in {dt:.1f} s (PyTorch CPU eager)"}
+                                    "sample": f"{steps} passes x {R} requests in {dt:.1f} s after >= 3 s of "
+                                              f"warm-up (PyTorch CPU eager)"}
     g.shutdown()
     if rank == 0:
         print(json.dumps(line), flush=True)

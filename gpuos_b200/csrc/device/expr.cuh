@@ -6,7 +6,9 @@
 // and one interpreter evaluates it per element; each of the kExprPrograms table entries has
 // its own operator address (op_expr<K>), so slots and aliases switch between them exactly as
 // between compiled operators.  Every thread runs the same instruction sequence (no
-// divergence); the stack lives in thread-local memory.
+// divergence); the stack lives in thread-local memory.  Transcendental functions are evaluated
+// in double precision and rounded once to float, like the built-in operators, so each call
+// contributes at most one float rounding error.
 #pragma once
 #include "refops.cuh"
 
@@ -42,9 +44,9 @@ __device__ __forceinline__ float expr_run(const ExprProg& p, float A, float B) {
       switch (op) {
         case XO_MIN: r = fminf(x, y); break;
         case XO_MAX: r = fmaxf(x, y); break;
-        case XO_POW: r = powf(x, y); break;
+        case XO_POW: r = (float)pow((double)x, (double)y); break;
         case XO_FMOD: r = fmodf(x, y); break;
-        case XO_ATAN2: r = atan2f(x, y); break;
+        case XO_ATAN2: r = (float)atan2((double)x, (double)y); break;
         default: r = copysignf(x, y); break;
       }
       st[sp++] = r;
@@ -77,30 +79,30 @@ __device__ __forceinline__ float expr_run(const ExprProg& p, float A, float B) {
     switch (op) {
       case XO_NEG: r = -x; break;
       case XO_NOT: r = x == 0.f ? 1.f : 0.f; break;
-      case XO_EXP: r = expf(x); break;
-      case XO_LOG: r = logf(x); break;
-      case XO_LOG1P: r = log1pf(x); break;
-      case XO_EXPM1: r = expm1f(x); break;
+      case XO_EXP: r = (float)exp((double)x); break;
+      case XO_LOG: r = (float)log((double)x); break;
+      case XO_LOG1P: r = (float)log1p((double)x); break;
+      case XO_EXPM1: r = (float)expm1((double)x); break;
       case XO_SQRT: r = sqrtf(x); break;
-      case XO_RSQRT: r = rsqrtf(x); break;
+      case XO_RSQRT: r = (float)(1.0 / sqrt((double)x)); break;
       case XO_ABS: r = fabsf(x); break;
-      case XO_TANH: r = tanhf(x); break;
-      case XO_SIN: r = sinf(x); break;
-      case XO_COS: r = cosf(x); break;
-      case XO_TAN: r = tanf(x); break;
-      case XO_ERF: r = erff(x); break;
+      case XO_TANH: r = (float)tanh((double)x); break;
+      case XO_SIN: r = (float)sin((double)x); break;
+      case XO_COS: r = (float)cos((double)x); break;
+      case XO_TAN: r = (float)tan((double)x); break;
+      case XO_ERF: r = (float)erf((double)x); break;
       case XO_FLOOR: r = floorf(x); break;
       case XO_CEIL: r = ceilf(x); break;
       case XO_TRUNC: r = truncf(x); break;
       case XO_ROUND: r = roundf(x); break;
-      case XO_EXP2: r = exp2f(x); break;
-      case XO_LOG2: r = log2f(x); break;
-      case XO_LOG10: r = log10f(x); break;
-      case XO_SINH: r = sinhf(x); break;
-      case XO_COSH: r = coshf(x); break;
-      case XO_ASIN: r = asinf(x); break;
-      case XO_ACOS: r = acosf(x); break;
-      default: r = atanf(x); break;
+      case XO_EXP2: r = (float)exp2((double)x); break;
+      case XO_LOG2: r = (float)log2((double)x); break;
+      case XO_LOG10: r = (float)log10((double)x); break;
+      case XO_SINH: r = (float)sinh((double)x); break;
+      case XO_COSH: r = (float)cosh((double)x); break;
+      case XO_ASIN: r = (float)asin((double)x); break;
+      case XO_ACOS: r = (float)acos((double)x); break;
+      default: r = (float)atan((double)x); break;
     }
     st[sp - 1] = r;
   }

@@ -179,6 +179,22 @@ struct ExprProg {
 };
 static_assert(sizeof(ExprProg) == 336, "ExprProg layout");
 
+// ---- worker modules -------------------------------------------------------------------
+// The worker runs from this library's module until an operator compiled at run time is
+// installed; from then on it runs from a module that links the worker's relocatable code with
+// every such operator (function pointers are only called within the module they belong to).
+// gpuos_module_addrs writes each module's built-in operator addresses in this order.
+enum ModuleAddr : int {
+  MA_ADD = 0,                                      // op_add (slot 0 at init)
+  MA_MUL = 1,                                      // op_mul (slot 1 at init)
+  MA_BATCH = 2,                                    // op_batch (slot 10 at init)
+  MA_REF_OPS = 3,                                  // reference-ABI element-wise ops, then sum, mean
+  MA_EXPR_FNS = MA_REF_OPS + GPUOS_EW_NUM_OPS + 2, // expression-program operators
+  MA_EXPR_PROGS = MA_EXPR_FNS + kExprPrograms,     // address of the module's program table
+  MA_COUNT
+};
+constexpr int kMaxJitOps = 64;  // run-time compiled operators per device
+
 // Per-CTA cycle counters (clock64) of one launch, written when the CTA exits.
 enum DiagSlot {
   DG_P_WAIT_EMPTY = 0,  // dequeue warp: waiting for a free stage

@@ -819,14 +819,144 @@ PyObject* py_builtin_op_address(PyObject*, PyObject* args, PyObject* kw) {
   int dev = 0;
   gpuos_rt* rt = rt_arg(devobj, &dev);
   if (!rt) return nullptr;
+  // the address in the worker module the runtime of this device currently runs
   OpPtrInt addr = 0;
-  cudaSetDevice(dev);
-  cudaStream_t s = c10::cuda::getCurrentCUDAStream((c10::DeviceIndex)dev).stream();
-  cudaError_t e = gpu_get_builtin_op_async(code, &addr, s);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-  if (e != cudaSuccess) return PyErr_Format(PyExc_RuntimeError, "builtin_op_address: %s", cudaGetErrorString(e));
+  const int st = gpuos_rt_builtin_op(rt, code, &addr);
+  if (st) return raise_status(st);
   return PyLong_FromUnsignedLongLong(addr);
 }
+
+// ---- operators compiled at run time (NVRTC for sm_100a, linked into the worker) ---------------
+PyObject* py_register_jit(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"expr", "arity", "slot", "device", nullptr};
+  const char* expr;
+  int arity, slot = -1;
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "si|iO", const_cast<char**>(kwlist), &expr, &arity, &slot, &devobj))
+    return nullptr;
+  int dev = 0;
+  gpuos_rt* rt = rt_arg(devobj, &dev);
+  if (!rt) return nullptr;
+  int out = -1, st;
+  Busy busy(dev);
+  Py_BEGIN_ALLOW_THREADS st = gpuos_rt_register_jit(rt, expr, arity, slot, &out);
+  Py_END_ALLOW_THREADS
+  if (st) return raise_status(st);
+  return PyLong_FromLong(out);
+}
+
+PyObject* py_load_custom(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"ptx", "entry", "slot", "device", nullptr};
+  const char* ptx;  // PTX is text: no embedded NUL
+  const char* entry;
+  int slot = -1;
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "ss|iO", const_cast<char**>(kwlist), &ptx, &entry, &slot, &devobj))
+    return nullptr;
+  const size_t n = std::strlen(ptx);
+  int dev = 0;
+  gpuos_rt* rt = rt_arg(devobj, &dev);
+  if (!rt) return nullptr;
+  int out = -1, st;
+  Busy busy(dev);
+  Py_BEGIN_ALLOW_THREADS st = gpuos_rt_load_custom(rt, ptx, (size_t)n, entry, slot, &out);
+  Py_END_ALLOW_THREADS
+  if (st) return raise_status(st);
+  return PyLong_FromLong(out);
+}
+
+// Staged operator: a capsule that frees the staged image when dropped.
+void staged_free(PyObject* cap) {
+  void* p = PyCapsule_GetPointer(cap, "gpuos_jit_staged");
+  if (p) gpuos_rt_jit_discard(static_cast<gpuos_jit_staged*>(p));
+}
+
+PyObject* py_jit_stage(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"expr", "arity", "device", nullptr};
+  const char* expr;
+  int arity;
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "si|O", const_cast<char**>(kwlist), &expr, &arity, &devobj))
+    return nullptr;
+  int dev = 0;
+  gpuos_rt* rt = rt_arg(devobj, &dev);
+  if (!rt) return nullptr;
+  gpuos_jit_staged* st = nullptr;
+  int e;
+  Busy busy(dev);
+  Py_BEGIN_ALLOW_THREADS e = gpuos_rt_jit_stage(rt, expr, arity, &st);
+  Py_END_ALLOW_THREADS
+  if (e) return raise_status(e);
+  return PyCapsule_New(st, "gpuos_jit_staged", staged_free);
+}
+
+PyObject* py_jit_commit(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"staged", "slot", "device", nullptr};
+  PyObject* cap;
+  int slot = -1;
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "O|iO", const_cast<char**>(kwlist), &cap, &slot, &devobj)) return nullptr;
+  auto* st = static_cast<gpuos_jit_staged*>(PyCapsule_GetPointer(cap, "gpuos_jit_staged"));
+  if (!st) return nullptr;
+  int dev = 0;
+  gpuos_rt* rt = rt_arg(devobj, &dev);
+  if (!rt) return nullptr;
+  int out = -1, e;
+  Busy busy(dev);
+  Py_BEGIN_ALLOW_THREADS e = gpuos_rt_jit_commit(rt, st, slot, &out);
+  Py_END_ALLOW_THREADS
+  if (e) return raise_status(e);
+  return PyLong_FromLong(out);
+}
+
+PyObject* py_jit_ops(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"device", nullptr};
+  PyObject* devobj = Py_None;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "|O", const_cast<char**>(kwlist), &devobj)) return nullptr;
+  gpuos_rt* rt = rt_arg(devobj, nullptr);
+  if (!rt) return nullptr;
+  const int n = gpuos_rt_jit_ops(rt);
+  if (n < 0) return raise_status(-n);
+  return PyLong_FromLong(n);
+}
+
+// Device-free: NVRTC output (relocatable sm_100a code, or PTX) of a CUDA source.
+PyObject* py_jit_compile(PyObject*, PyObject* args, PyObject* kw) {
+  static const char* kwlist[] = {"src", "ptx", nullptr};
+  const char* src;
+  int ptx = 0;
+  if (!PyArg_ParseTupleAndKeywords(args, kw, "s|p", const_cast<char**>(kwlist), &src, &ptx)) return nullptr;
+  size_t n = 0;
+  int st;
+  Py_BEGIN_ALLOW_THREADS st = gpuos_jit_compile(src, ptx, nullptr, 0, &n);
+  Py_END_ALLOW_THREADS
+  if (st) return raise_status(st);
+  std::string buf(n, '\0');
+  Py_BEGIN_ALLOW_THREADS st = gpuos_jit_compile(src, ptx, &buf[0], n, &n);
+  Py_END_ALLOW_THREADS
+  if (st) return raise_status(st);
+  if (ptx) {
+    while (!buf.empty() && buf.back() == '\0') buf.pop_back();
+    return PyUnicode_FromStringAndSize(buf.data(), (Py_ssize_t)buf.size());
+  }
+  return PyBytes_FromStringAndSize(buf.data(), (Py_ssize_t)n);
+}
+
+// Device-free: compile an expression operator and link it with the worker; returns the size of
+// the linked image.
+PyObject* py_jit_check_expr(PyObject*, PyObject* args) {
+  const char* expr;
+  int arity;
+  if (!PyArg_ParseTuple(args, "si", &expr, &arity)) return nullptr;
+  size_t n = 0;
+  int st;
+  Py_BEGIN_ALLOW_THREADS st = gpuos_jit_check_expr(expr, arity, &n);
+  Py_END_ALLOW_THREADS
+  if (st) return raise_status(st);
+  return PyLong_FromSize_t(n);
+}
+
+PyObject* py_jit_nvrtc_version(PyObject*, PyObject*) { return PyLong_FromLong(gpuos_jit_nvrtc_version()); }
 
 PyObject* py_register_builtin(PyObject*, PyObject* args, PyObject* kw) {
   static const char* kwlist[] = {"kind", "op", "device", nullptr};
@@ -1169,7 +1299,24 @@ PyMethodDef kMethods[] = {
     {"register_builtin", (PyCFunction)(void (*)(void))py_register_builtin, METH_VARARGS | METH_KEYWORDS,
      "register_builtin(kind, op) -> slot"},
     {"register_expr", (PyCFunction)(void (*)(void))py_register_expr, METH_VARARGS | METH_KEYWORDS,
-     "NVRTC-compile an expression operator into a slot"},
+     "register_expr(key, expr, arity, slot=-1): expression operator run by the worker's interpreter"},
+    {"register_jit", (PyCFunction)(void (*)(void))py_register_jit, METH_VARARGS | METH_KEYWORDS,
+     "register_jit(expr, arity, slot=-1): NVRTC-compile an expression operator for sm_100a, link it "
+     "into the worker, install it in a slot"},
+    {"load_custom", (PyCFunction)(void (*)(void))py_load_custom, METH_VARARGS | METH_KEYWORDS,
+     "load_custom(ptx, entry, slot=-1): link PTX holding extern \"C\" __device__ void entry(const Task&) "
+     "into the worker, install entry in a slot"},
+    {"jit_stage", (PyCFunction)(void (*)(void))py_jit_stage, METH_VARARGS | METH_KEYWORDS,
+     "jit_stage(expr, arity) -> staged operator (compiled and linked; the worker keeps running)"},
+    {"jit_commit", (PyCFunction)(void (*)(void))py_jit_commit, METH_VARARGS | METH_KEYWORDS,
+     "jit_commit(staged, slot=-1) -> slot (stops the worker, loads the module, installs the operator)"},
+    {"jit_ops", (PyCFunction)(void (*)(void))py_jit_ops, METH_VARARGS | METH_KEYWORDS,
+     "operators compiled at run time installed on the device"},
+    {"jit_compile", (PyCFunction)(void (*)(void))py_jit_compile, METH_VARARGS | METH_KEYWORDS,
+     "jit_compile(src, ptx=False): NVRTC output for sm_100a (no device needed)"},
+    {"jit_check_expr", py_jit_check_expr, METH_VARARGS,
+     "jit_check_expr(expr, arity) -> linked image bytes (no device needed)"},
+    {"jit_nvrtc_version", py_jit_nvrtc_version, METH_NOARGS, "NVRTC version in use (major*1000+minor*10)"},
     {"sync_poll_processed", py_sync_poll_processed, METH_NOARGS, "completed requests (zero-copy)"},
     {"sync_poll_heartbeat", py_sync_poll_heartbeat, METH_NOARGS, "worker heartbeat (zero-copy)"},
     {"sync_poll_ready", py_sync_poll_ready, METH_NOARGS, "worker ready (zero-copy)"},

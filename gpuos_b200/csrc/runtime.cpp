@@ -32,6 +32,7 @@
 #include <vector>
 
 #include "internal.h"
+#include "jit.h"
 
 using namespace gpuos;
 
@@ -41,7 +42,7 @@ extern "C" cudaError_t gpuos_internal_set_worker_smem(size_t smem);
 extern "C" cudaError_t gpuos_internal_table_ptrs(void** table, void** alias);
 extern "C" cudaError_t gpuos_internal_preload_kernels();
 extern "C" cudaError_t gpuos_internal_worker_occupancy(int threads, size_t smem, int* blocks);
-extern "C" cudaError_t gpuos_internal_set_expr_prog(int k, const void* prog, cudaStream_t s);
+extern "C" cudaError_t gpuos_internal_module_addrs(unsigned long long* d_out, cudaStream_t s);
 namespace gpuos {
 int expr_compile(const char* expr, int arity, ExprProg* out, std::string* err);
 }
@@ -775,7 +776,10 @@ struct gpuos_rt {
   Layout* layouts = nullptr;
   uint64_t item_cap = 0, task_cap = 0, layout_cap = 0;
   DevCtl* dc = nullptr;
-  void* op_table = nullptr;
+  // this runtime's op table and alias (device memory; the worker resolves Tasks through them at
+  // dequeue time).  The reference C ABI's table (launch_persistent_worker) stays separate: it
+  // only ever holds addresses of this library's module.
+  void* op_table = nullptr;  // OpPtrInt[GPUOS_MAX_OPS], followed by int alias[GPUOS_MAX_OPS]
   void* op_alias = nullptr;
 
   std::mutex mu;
@@ -805,6 +809,16 @@ struct gpuos_rt {
   std::atomic<bool> stop{false};
   int next_slot = 20;
   int next_expr = 0;  // expression programs installed on this device
+  // Worker module: this library's until an operator compiled at run time is installed, then
+  // the module that links the worker with every such operator (jit_mod.worker != nullptr).
+  jit::Module jit_mod;
+  std::vector<jit::Module> old_mods;  // earlier linked modules, kept loaded until shutdown
+  std::vector<jit::Op> jit_ops;       // operators of the current linked module, in install order
+  std::vector<uint64_t> addr_map;     // current module: MA_COUNT built-in addresses, then one per jit op
+  std::vector<uint64_t> static_map;   // this library's module
+  std::vector<ExprProg> expr_progs;   // host copies of the installed expression programs
+  unsigned long long* addr_dev = nullptr;  // device output of the address kernels
+  std::mutex jit_mu;                  // one operator install at a time
   int ctas_per_sm = 1;  // worker CTAs resident per SM (each with its own dequeue warp)
   int grid = 0;         // worker CTAs per launch
   int cta_threads = 0;  // compute threads per worker CTA
@@ -917,7 +931,15 @@ static int launch_worker_locked(gpuos_rt* rt) {
     CK(cudaEventRecord(ev0, rt->kstream));
   }
   // one dequeue warp + one completer warp + threads_per_block compute threads
-  CK(gpuos_internal_launch_batch_worker(&P, rt->grid, rt->cta_threads + 64, rt->smem, rt->kstream));
+  if (rt->jit_mod.worker) {
+    void* args[] = {&P};
+    std::string err;
+    const int st = jit::launch(rt->jit_mod.worker, (unsigned)rt->grid, (unsigned)(rt->cta_threads + 64), rt->smem,
+                               rt->kstream, args, &err);
+    if (st) return fail(st, "worker launch: %s", err.c_str());
+  } else {
+    CK(gpuos_internal_launch_batch_worker(&P, rt->grid, rt->cta_threads + 64, rt->smem, rt->kstream));
+  }
   if (rt->time_launches) {
     CK(cudaEventRecord(ev1, rt->kstream));
     rt->launch_events.emplace_back(ev0, ev1);
@@ -1106,6 +1128,8 @@ extern "C" int gpuos_rt_init(int device, int capacity, int threads_per_block, gp
   auto cleanup = [&](int code) {
     if (rt->host_block) cudaFreeHost(rt->host_block);
     if (rt->dc) cudaFree(rt->dc);
+    if (rt->addr_dev) cudaFree(rt->addr_dev);
+    if (rt->op_table) cudaFree(rt->op_table);
     if (rt->kstream) cudaStreamDestroy(rt->kstream);
     if (rt->cstream) cudaStreamDestroy(rt->cstream);
     delete rt;
@@ -1163,7 +1187,34 @@ extern "C" int gpuos_rt_init(int device, int capacity, int threads_per_block, gp
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&rt->cstream, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = launch_init_builtin_ops(rt->cstream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(rt->cstream);
-  if (e == cudaSuccess) e = gpuos_internal_table_ptrs(&rt->op_table, &rt->op_alias);
+  // built-in operator addresses of this library's module
+  if (e == cudaSuccess) e = cudaMalloc(&rt->addr_dev, sizeof(unsigned long long) * (MA_COUNT + kMaxJitOps));
+  if (e == cudaSuccess) e = gpuos_internal_module_addrs(rt->addr_dev, rt->cstream);
+  rt->static_map.assign(MA_COUNT, 0);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(rt->static_map.data(), rt->addr_dev, sizeof(uint64_t) * MA_COUNT, cudaMemcpyDeviceToHost,
+                        rt->cstream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(rt->cstream);
+  rt->addr_map = rt->static_map;
+  // the runtime's table as launch_init_builtin_ops sets the reference one
+  // (persistent_kernel.cu:115-130): empty slots, identity alias, add@0, mul@1, batch@10
+  static thread_local OpPtrInt init_table[GPUOS_MAX_OPS];
+  static thread_local int init_alias[GPUOS_MAX_OPS];
+  for (int i = 0; i < GPUOS_MAX_OPS; ++i) {
+    init_table[i] = 0;
+    init_alias[i] = i;
+  }
+  init_table[0] = rt->static_map[MA_ADD];
+  init_table[1] = rt->static_map[MA_MUL];
+  init_table[10] = rt->static_map[MA_BATCH];
+  if (e == cudaSuccess) e = cudaMalloc(&rt->op_table, sizeof(init_table) + sizeof(init_alias));
+  if (e == cudaSuccess) {
+    rt->op_alias = static_cast<unsigned char*>(rt->op_table) + sizeof(init_table);
+    e = cudaMemcpyAsync(rt->op_table, init_table, sizeof(init_table), cudaMemcpyHostToDevice, rt->cstream);
+  }
+  if (e == cudaSuccess) e = cudaMemcpyAsync(rt->op_alias, init_alias, sizeof(init_alias), cudaMemcpyHostToDevice, rt->cstream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(rt->cstream);
+  rt->expr_progs.assign(kExprPrograms, ExprProg());
   if (e == cudaSuccess) e = gpuos_internal_set_worker_smem(rt->smem);
   if (e == cudaSuccess) e = gpuos_internal_preload_kernels();
   int resident = 0;
@@ -1231,6 +1282,10 @@ extern "C" int gpuos_rt_shutdown(gpuos_rt* rt) {
   for (cudaEvent_t ev : rt->spare_events) cudaEventDestroy(ev);
   cudaStreamDestroy(rt->kstream);
   cudaStreamDestroy(rt->cstream);
+  jit::unload(&rt->jit_mod);
+  for (jit::Module& m : rt->old_mods) jit::unload(&m);
+  cudaFree(rt->addr_dev);
+  cudaFree(rt->op_table);
   cudaFree(rt->dc);
   cudaFreeHost(rt->host_block);
   delete rt;
@@ -1688,11 +1743,26 @@ extern "C" int gpuos_rt_stats(gpuos_rt* rt, int64_t* v, int n) {
 }
 
 // ---- op table control --------------------------------------------------------------------
+static uint64_t translate_addr(const std::vector<uint64_t>& from, const std::vector<uint64_t>& to, uint64_t a,
+                               bool* found);
+
 extern "C" int gpuos_rt_set_slot(gpuos_rt* rt, int slot, OpPtrInt fn) {
   if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
   if (slot < 0 || slot >= GPUOS_MAX_OPS) return fail(GPUOS_ERR_INVALID, "slot %d out of range", slot);
+  {
+    // once the worker runs from a linked module, an address of this library's module (from
+    // gpu_get_builtin_op_async) names the same operator of the linked module
+    std::lock_guard<std::mutex> lk(rt->mu);
+    if (rt->jit_mod.worker) {
+      bool found = false;
+      fn = translate_addr(rt->static_map, rt->addr_map, fn, &found);
+    }
+  }
   CK(cudaSetDevice(rt->device));
-  CK(gpu_set_op_table_async(slot, fn, rt->cstream));
+  static thread_local OpPtrInt staged;
+  staged = fn;
+  CK(cudaMemcpyAsync(static_cast<OpPtrInt*>(rt->op_table) + slot, &staged, sizeof(OpPtrInt), cudaMemcpyHostToDevice,
+                     rt->cstream));
   CK(cudaStreamSynchronize(rt->cstream));
   return GPUOS_OK;
 }
@@ -1712,7 +1782,10 @@ extern "C" int gpuos_rt_set_alias(gpuos_rt* rt, int logical, int physical) {
   if (logical < 0 || logical >= GPUOS_MAX_OPS || physical < 0 || physical >= GPUOS_MAX_OPS)
     return fail(GPUOS_ERR_INVALID, "alias %d -> %d out of range", logical, physical);
   CK(cudaSetDevice(rt->device));
-  CK(gpu_set_alias_async(logical, physical, rt->cstream));
+  static thread_local int staged;
+  staged = physical;
+  CK(cudaMemcpyAsync(static_cast<int*>(rt->op_alias) + logical, &staged, sizeof(int), cudaMemcpyHostToDevice,
+                     rt->cstream));
   CK(cudaStreamSynchronize(rt->cstream));
   return GPUOS_OK;
 }
@@ -1727,16 +1800,50 @@ extern "C" int gpuos_rt_get_alias(gpuos_rt* rt, int logical, int* physical) {
   return GPUOS_OK;
 }
 
+// Address of built-in operator `code` in the worker module the runtime currently runs
+// (codes as gpu_get_builtin_op_async: 0, 1, 10, 100+k, 200+k), 0 if there is none.
+static uint64_t builtin_addr_locked(gpuos_rt* rt, int code) {
+  int i = -1;
+  if (code == 0) i = MA_ADD;
+  else if (code == 1) i = MA_MUL;
+  else if (code == 10) i = MA_BATCH;
+  else if (code >= 100 && code < 100 + GPUOS_EW_NUM_OPS + 2) i = MA_REF_OPS + (code - 100);
+  else if (code >= 200 && code < 200 + kExprPrograms) i = MA_EXPR_FNS + (code - 200);
+  return i < 0 ? 0 : rt->addr_map[i];
+}
+
+// An address of this library's module (or of an earlier linked module) names the same operator
+// in the current module; anything else is kept as written.
+static uint64_t translate_addr(const std::vector<uint64_t>& from, const std::vector<uint64_t>& to, uint64_t a,
+                               bool* found) {
+  if (a == 0) return 0;
+  for (size_t i = 0; i < from.size() && i < to.size(); ++i) {
+    if (i == (size_t)MA_EXPR_PROGS) continue;
+    if (from[i] == a) {
+      *found = true;
+      return to[i];
+    }
+  }
+  return a;
+}
+
+extern "C" int gpuos_rt_builtin_op(gpuos_rt* rt, int code, OpPtrInt* addr) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  if (!addr) return fail(GPUOS_ERR_INVALID, "null output");
+  std::lock_guard<std::mutex> lk(rt->mu);
+  *addr = builtin_addr_locked(rt, code);
+  if (!*addr) return fail(GPUOS_ERR_INVALID, "no built-in operator %d", code);
+  return GPUOS_OK;
+}
+
 static int register_builtin_code(gpuos_rt* rt, int code, int* slot) {
   if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
   OpPtrInt addr = 0;
-  CK(cudaSetDevice(rt->device));
-  CK(gpu_get_builtin_op_async(code, &addr, rt->cstream));
-  CK(cudaStreamSynchronize(rt->cstream));
-  if (!addr) return fail(GPUOS_ERR_INVALID, "no built-in operator %d", code);
   int s;
   {
     std::lock_guard<std::mutex> lk(rt->mu);
+    addr = builtin_addr_locked(rt, code);
+    if (!addr) return fail(GPUOS_ERR_INVALID, "no built-in operator %d", code);
     if (rt->next_slot >= GPUOS_MAX_OPS) return fail(GPUOS_ERR_FULL, "op table full (%d slots)", GPUOS_MAX_OPS);
     s = rt->next_slot++;
   }
@@ -1756,10 +1863,9 @@ extern "C" int gpuos_rt_register_builtin_ew(gpuos_rt* rt, int ew_op, int* slot) 
   return register_builtin_code(rt, 100 + ew_op, slot);
 }
 
-// register_elementwise for an expression that is not a built-in operator
-// (gpuos_ext.cpp:814-881): compile it into a program, write the program into the next free
-// device program entry, then point `slot` at that entry's operator.  Nothing is loaded while
-// the worker runs, so no worker needs to stop (the reference's module load waits for it).
+// register_elementwise through the expression interpreter: compile the expression into a
+// program, write the program into the next free program entry of the running worker module,
+// then point `slot` at that entry's operator.  Nothing is loaded and the worker keeps running.
 extern "C" int gpuos_rt_register_expr(gpuos_rt* rt, const char* key, const char* expr, int arity, int slot,
                                       int* slot_out) {
   (void)key;  // the key -> slot registry lives with the caller (the Python module caches it)
@@ -1769,7 +1875,9 @@ extern "C" int gpuos_rt_register_expr(gpuos_rt* rt, const char* key, const char*
   std::string err;
   int e = expr_compile(expr, arity, &prog, &err);
   if (e) return fail(e, "expression '%s': %s", expr ? expr : "", err.c_str());
+  std::lock_guard<std::mutex> jl(rt->jit_mu);  // the worker module does not change meanwhile
   int k, s;
+  uint64_t progs, addr;
   {
     std::lock_guard<std::mutex> lk(rt->mu);
     if (rt->next_expr >= kExprPrograms)
@@ -1777,11 +1885,13 @@ extern "C" int gpuos_rt_register_expr(gpuos_rt* rt, const char* key, const char*
     if (slot < 0 && rt->next_slot >= GPUOS_MAX_OPS) return fail(GPUOS_ERR_FULL, "op table full (%d slots)", GPUOS_MAX_OPS);
     k = rt->next_expr++;
     s = slot >= 0 ? slot : rt->next_slot++;
+    rt->expr_progs[k] = prog;
+    progs = rt->addr_map[MA_EXPR_PROGS];
+    addr = rt->addr_map[MA_EXPR_FNS + k];
   }
   CK(cudaSetDevice(rt->device));
-  CK(gpuos_internal_set_expr_prog(k, &prog, rt->cstream));
-  OpPtrInt addr = 0;
-  CK(gpu_get_builtin_op_async(200 + k, &addr, rt->cstream));
+  CK(cudaMemcpyAsync(reinterpret_cast<void*>(progs + (uint64_t)k * sizeof(ExprProg)), &prog, sizeof(ExprProg),
+                     cudaMemcpyHostToDevice, rt->cstream));
   CK(cudaStreamSynchronize(rt->cstream));
   if (!addr) return fail(GPUOS_ERR_CUDA, "expression operator %d has no address", k);
   e = gpuos_rt_set_slot(rt, s, addr);
@@ -1789,6 +1899,277 @@ extern "C" int gpuos_rt_register_expr(gpuos_rt* rt, const char* key, const char*
   if (slot_out) *slot_out = s;
   return GPUOS_OK;
 }
+
+// ---- operators compiled at run time ---------------------------------------------------------
+// Stop the worker (published work drains first) and wait for it to leave the device.
+static int stop_worker_locked(gpuos_rt* rt, int timeout_ms) {
+  if (rt->failed) return fail(GPUOS_ERR_DEVICE, "%s", rt->fail_msg.c_str());
+  if (!rt->launched) return GPUOS_OK;
+  const uint64_t ep = rt->epoch;
+  if (rt->hc->quit_epoch < ep) rt->hc->quit_epoch = ep;
+  const uint64_t t0 = mono_ns();
+  while (true) {
+    const uint64_t st = rt->rep->state;
+    if ((st >> 8) == ep && (st & 0xff) == WS_EXITED) break;
+    if (rt->rep->error) return check_device_error_locked(rt);
+    if (mono_ns() - t0 > (uint64_t)timeout_ms * 1000000ull) return fail(GPUOS_ERR_TIMEOUT, "worker did not stop");
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+  CK(cudaStreamSynchronize(rt->kstream));
+  return GPUOS_OK;
+}
+
+// An operator compiled and linked, not yet installed: the linked image holds the worker, every
+// operator installed before it (`id` of them) and this one.
+struct gpuos_jit_staged {
+  int device = -1;
+  int id = 0;
+  jit::Op op;
+  std::vector<jit::Op> ops;
+  std::vector<char> image;
+};
+
+// Compile nothing, link `op` with the worker and the operators installed so far.
+static int stage_jit_op(gpuos_rt* rt, int id, jit::Op op, gpuos_jit_staged** out) {
+  auto* st = new gpuos_jit_staged();
+  st->device = rt->device;
+  st->id = id;
+  st->op = std::move(op);
+  {
+    std::lock_guard<std::mutex> jl(rt->jit_mu);
+    if ((int)rt->jit_ops.size() != id) {
+      delete st;
+      return fail(GPUOS_ERR_INVALID, "another operator was installed meanwhile; stage again");
+    }
+    if (id >= kMaxJitOps) {
+      delete st;
+      return fail(GPUOS_ERR_FULL, "all %d run-time compiled operators of this device are in use", kMaxJitOps);
+    }
+    st->ops = rt->jit_ops;
+  }
+  st->ops.push_back(st->op);
+  std::string err;
+  const int e = jit::link(st->ops, &st->image, &err);
+  if (e) {
+    delete st;
+    return fail(e, "%s", err.c_str());
+  }
+  *out = st;
+  return GPUOS_OK;
+}
+
+// Stop the worker, load the staged module, carry the op table and the expression programs over
+// to it, and run the worker from it from the next publish on.  *addr_out = the new operator's
+// address.  On failure the runtime keeps its previous module (the worker restarts from it with
+// the next publish).
+static int commit_jit_op(gpuos_rt* rt, const gpuos_jit_staged& st, uint64_t* addr_out) {
+  std::lock_guard<std::mutex> jl(rt->jit_mu);
+  if (st.device != rt->device) return fail(GPUOS_ERR_INVALID, "staged for device %d", st.device);
+  if ((int)rt->jit_ops.size() != st.id)
+    return fail(GPUOS_ERR_INVALID, "another operator was installed after this one was staged; stage again");
+  const std::vector<jit::Op>& ops = st.ops;
+  std::string err;
+  CK(cudaSetDevice(rt->device));
+  std::lock_guard<std::mutex> lk(rt->mu);
+  // a module load waits for kernels running on the device: load with the worker stopped
+  int e = stop_worker_locked(rt, 30000);
+  if (e) return e;
+  jit::Module m;
+  e = jit::load(st.image, ops, &m, &err);
+  if (e) return fail(e, "%s", err.c_str());
+  auto undo = [&](int code, const char* what) {
+    jit::unload(&m);
+    return fail(code, "%s: %s", what, err.c_str());
+  };
+  if (jit::set_smem(m.worker, rt->smem, &err)) return undo(GPUOS_ERR_CUDA, "linked worker");
+  int resident = 0;
+  if (jit::occupancy(m.worker, rt->cta_threads + 64, rt->smem, &resident, &err)) return undo(GPUOS_ERR_CUDA, "linked worker");
+  if (resident < rt->ctas_per_sm) {
+    err = std::to_string(resident) + " CTAs per SM fit";
+    return undo(GPUOS_ERR_UNSUPPORTED, "linked worker");
+  }
+  // built-in and operator addresses of the linked module
+  void* a0[] = {&rt->addr_dev};
+  if (jit::launch(m.addrs, 1, 64, 0, rt->cstream, a0, &err)) return undo(GPUOS_ERR_CUDA, "address kernel");
+  std::vector<unsigned long long*> outs(ops.size());
+  for (size_t j = 0; j < ops.size(); ++j) {
+    outs[j] = rt->addr_dev + MA_COUNT + j;
+    void* a1[] = {&outs[j]};
+    if (jit::launch(m.op_addr[j], 1, 1, 0, rt->cstream, a1, &err)) return undo(GPUOS_ERR_CUDA, "operator address kernel");
+  }
+  std::vector<uint64_t> nmap(MA_COUNT + ops.size(), 0);
+  std::vector<uint64_t> table(GPUOS_MAX_OPS, 0);
+  cudaError_t ce = cudaMemcpyAsync(nmap.data(), rt->addr_dev, sizeof(uint64_t) * nmap.size(), cudaMemcpyDeviceToHost,
+                                   rt->cstream);
+  if (ce == cudaSuccess)
+    ce = cudaMemcpyAsync(table.data(), rt->op_table, sizeof(uint64_t) * GPUOS_MAX_OPS, cudaMemcpyDeviceToHost,
+                         rt->cstream);
+  if (ce == cudaSuccess) ce = cudaStreamSynchronize(rt->cstream);
+  if (ce != cudaSuccess) {
+    err = cudaGetErrorString(ce);
+    return undo(GPUOS_ERR_CUDA, "module addresses");
+  }
+  for (size_t j = 0; j < ops.size(); ++j)
+    if (nmap[MA_COUNT + j] == 0) return undo(GPUOS_ERR_CUDA, "operator without an address");
+  // op table: every entry that names an operator of the previous module names the same one here
+  for (uint64_t& t : table) {
+    bool found = false;
+    uint64_t v = translate_addr(rt->addr_map, nmap, t, &found);
+    if (!found) v = translate_addr(rt->static_map, nmap, t, &found);
+    t = v;
+  }
+  ce = cudaMemcpyAsync(rt->op_table, table.data(), sizeof(uint64_t) * GPUOS_MAX_OPS, cudaMemcpyHostToDevice,
+                       rt->cstream);
+  // expression programs installed so far
+  if (ce == cudaSuccess && rt->next_expr > 0)
+    ce = cudaMemcpyAsync(reinterpret_cast<void*>(nmap[MA_EXPR_PROGS]), rt->expr_progs.data(),
+                         sizeof(ExprProg) * rt->next_expr, cudaMemcpyHostToDevice, rt->cstream);
+  if (ce == cudaSuccess) ce = cudaStreamSynchronize(rt->cstream);
+  if (ce != cudaSuccess) {
+    err = cudaGetErrorString(ce);
+    return undo(GPUOS_ERR_CUDA, "op table");
+  }
+  if (rt->jit_mod.mod) rt->old_mods.push_back(rt->jit_mod);
+  rt->jit_mod = m;
+  rt->jit_ops = ops;
+  rt->addr_map = nmap;
+  if (addr_out) *addr_out = nmap[MA_COUNT + ops.size() - 1];
+  return GPUOS_OK;
+}
+
+static int next_slot_for(gpuos_rt* rt, int slot, int* s) {
+  std::lock_guard<std::mutex> lk(rt->mu);
+  if (slot >= 0) {
+    *s = slot;
+    return GPUOS_OK;
+  }
+  if (rt->next_slot >= GPUOS_MAX_OPS) return fail(GPUOS_ERR_FULL, "op table full (%d slots)", GPUOS_MAX_OPS);
+  *s = rt->next_slot++;
+  return GPUOS_OK;
+}
+
+static int current_jit_id(gpuos_rt* rt) {
+  std::lock_guard<std::mutex> jl(rt->jit_mu);
+  return (int)rt->jit_ops.size();
+}
+
+extern "C" int gpuos_rt_jit_stage(gpuos_rt* rt, const char* expr, int arity, gpuos_jit_staged** staged) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  if (!expr || !staged) return fail(GPUOS_ERR_INVALID, "null argument");
+  *staged = nullptr;
+  const int id = current_jit_id(rt);
+  std::string src, err;
+  int e = jit::ew_source(id, expr, arity, &src, &err);
+  if (e) return fail(e, "expression '%s': %s", expr, err.c_str());
+  jit::Op op;
+  op.objs.resize(1);
+  op.objs[0].name = "gpuos_jit_op_" + std::to_string(id);
+  e = jit::compile(src, (op.objs[0].name + ".cu").c_str(), "cubin", &op.objs[0].bytes, &err);
+  if (e) return fail(e, "expression '%s': %s", expr, err.c_str());
+  op.addr_kernel = "gpuos_jit_addr_" + std::to_string(id);
+  return stage_jit_op(rt, id, std::move(op), staged);
+}
+
+extern "C" int gpuos_rt_jit_stage_ptx(gpuos_rt* rt, const char* ptx, size_t ptx_len, const char* entry,
+                                      gpuos_jit_staged** staged) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  if (!ptx || ptx_len == 0 || !entry || !staged) return fail(GPUOS_ERR_INVALID, "empty PTX or entry name");
+  *staged = nullptr;
+  const int id = current_jit_id(rt);
+  std::string src, err;
+  int e = jit::bridge_source(id, entry, &src, &err);
+  if (e) return fail(e, "entry '%s': %s", entry, err.c_str());
+  jit::Op op;
+  op.objs.resize(2);
+  op.objs[0].ptx = true;
+  op.objs[0].name = "gpuos_custom_" + std::to_string(id) + ".ptx";
+  op.objs[0].bytes.assign(ptx, ptx + ptx_len);
+  if (op.objs[0].bytes.back() != '\0') op.objs[0].bytes.push_back('\0');
+  op.objs[1].name = "gpuos_jit_bridge_" + std::to_string(id);
+  e = jit::compile(src, (op.objs[1].name + ".cu").c_str(), "cubin", &op.objs[1].bytes, &err);
+  if (e) return fail(e, "bridge for '%s': %s", entry, err.c_str());
+  op.addr_kernel = "gpuos_jit_addr_" + std::to_string(id);
+  return stage_jit_op(rt, id, std::move(op), staged);
+}
+
+extern "C" int gpuos_rt_jit_commit(gpuos_rt* rt, gpuos_jit_staged* staged, int slot, int* slot_out) {
+  if (!rt) return fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  if (!staged) return fail(GPUOS_ERR_INVALID, "nothing staged");
+  if (slot >= GPUOS_MAX_OPS) return fail(GPUOS_ERR_INVALID, "slot %d out of range", slot);
+  uint64_t addr = 0;
+  int e = commit_jit_op(rt, *staged, &addr);
+  if (e) return e;
+  int s = -1;
+  e = next_slot_for(rt, slot, &s);
+  if (e) return e;
+  e = gpuos_rt_set_slot(rt, s, addr);
+  if (e) return e;
+  if (slot_out) *slot_out = s;
+  return GPUOS_OK;
+}
+
+extern "C" void gpuos_rt_jit_discard(gpuos_jit_staged* staged) { delete staged; }
+
+extern "C" int gpuos_rt_register_jit(gpuos_rt* rt, const char* expr, int arity, int slot, int* slot_out) {
+  if (slot >= GPUOS_MAX_OPS) return fail(GPUOS_ERR_INVALID, "slot %d out of range", slot);
+  gpuos_jit_staged* st = nullptr;
+  int e = gpuos_rt_jit_stage(rt, expr, arity, &st);
+  if (e) return e;
+  e = gpuos_rt_jit_commit(rt, st, slot, slot_out);
+  delete st;
+  return e;
+}
+
+extern "C" int gpuos_rt_load_custom(gpuos_rt* rt, const char* ptx, size_t ptx_len, const char* entry, int slot,
+                                    int* slot_out) {
+  if (slot >= GPUOS_MAX_OPS) return fail(GPUOS_ERR_INVALID, "slot %d out of range", slot);
+  gpuos_jit_staged* st = nullptr;
+  int e = gpuos_rt_jit_stage_ptx(rt, ptx, ptx_len, entry, &st);
+  if (e) return e;
+  e = gpuos_rt_jit_commit(rt, st, slot, slot_out);
+  delete st;
+  return e;
+}
+
+extern "C" int gpuos_rt_jit_ops(gpuos_rt* rt) {
+  if (!rt) return -fail(GPUOS_ERR_NOT_INIT, "gpuos not initialized");
+  std::lock_guard<std::mutex> jl(rt->jit_mu);
+  return (int)rt->jit_ops.size();
+}
+
+// ---- device-free checks of the run-time compile path -----------------------------------------
+extern "C" int gpuos_jit_compile(const char* src, int ptx, void* out, size_t cap, size_t* size_out) {
+  if (!src) return fail(GPUOS_ERR_INVALID, "null source");
+  std::vector<char> bytes;
+  std::string err;
+  const int e = jit::compile(src, "user.cu", ptx ? "ptx" : "cubin", &bytes, &err);
+  if (e) return fail(e, "%s", err.c_str());
+  if (size_out) *size_out = bytes.size();
+  if (out) {
+    if (cap < bytes.size()) return fail(GPUOS_ERR_INVALID, "output buffer of %zu bytes, %zu needed", cap, bytes.size());
+    std::memcpy(out, bytes.data(), bytes.size());
+  }
+  return GPUOS_OK;
+}
+
+extern "C" int gpuos_jit_check_expr(const char* expr, int arity, size_t* image_bytes) {
+  if (!expr) return fail(GPUOS_ERR_INVALID, "null expression");
+  std::string src, err;
+  int e = jit::ew_source(0, expr, arity, &src, &err);
+  if (e) return fail(e, "expression '%s': %s", expr, err.c_str());
+  std::vector<jit::Op> ops(1);
+  ops[0].objs.resize(1);
+  ops[0].objs[0].name = "gpuos_jit_op_0";
+  e = jit::compile(src, "gpuos_jit_op_0.cu", "cubin", &ops[0].objs[0].bytes, &err);
+  if (e) return fail(e, "expression '%s': %s", expr, err.c_str());
+  std::vector<char> image;
+  e = jit::link(ops, &image, &err);
+  if (e) return fail(e, "%s", err.c_str());
+  if (image_bytes) *image_bytes = image.size();
+  return GPUOS_OK;
+}
+
+extern "C" int gpuos_jit_nvrtc_version(void) { return jit::nvrtc_version(); }
 
 extern "C" int gpuos_expr_compile(const char* expr, int arity, void* prog_out, int prog_bytes) {
   if (prog_out && prog_bytes < (int)sizeof(ExprProg)) return fail(GPUOS_ERR_INVALID, "program buffer smaller than %zu bytes", sizeof(ExprProg));

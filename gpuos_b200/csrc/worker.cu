@@ -38,6 +38,7 @@ __device__ OpFn g_builtin_ref_ops[GPUOS_EW_NUM_OPS + 2] = {
     ref_ew<24>, ref_ew<25>, ref_ew<26>, ref_ew<27>, ref_ew<28>, ref_ew<29>, op_reduce_sum,
     op_reduce_mean};
 
+#ifndef GPUOS_JIT_WORKER
 // persistent_kernel.cu:115-130: null table, identity alias, add@0, mul@1, batch@10.
 __global__ void init_builtin_ops_kernel() {
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
@@ -50,6 +51,8 @@ __global__ void init_builtin_ops_kernel() {
   if (idx == kBatchSlot) g_op_table[kBatchSlot] = op_batch;
 }
 
+#endif  // GPUOS_JIT_WORKER
+
 // Operator addresses of the expression programs (one per program index).
 __device__ OpFn g_expr_fns[kExprPrograms] = {
     op_expr<0>,  op_expr<1>,  op_expr<2>,  op_expr<3>,  op_expr<4>,  op_expr<5>,  op_expr<6>,  op_expr<7>,
@@ -57,6 +60,23 @@ __device__ OpFn g_expr_fns[kExprPrograms] = {
     op_expr<16>, op_expr<17>, op_expr<18>, op_expr<19>, op_expr<20>, op_expr<21>, op_expr<22>, op_expr<23>,
     op_expr<24>, op_expr<25>, op_expr<26>, op_expr<27>, op_expr<28>, op_expr<29>, op_expr<30>, op_expr<31>};
 
+// Every built-in operator address of this module, in the order of ModuleAddr, and the address
+// of this module's expression-program table.  The runtime keeps one such list per loaded
+// worker module (this library's own, and each module linked with run-time compiled
+// operators) and translates op-table entries between them when it switches modules.
+extern "C" __global__ void gpuos_module_addrs(unsigned long long* out) {
+  const int i = threadIdx.x;
+  if (i == 0) {
+    out[MA_ADD] = reinterpret_cast<unsigned long long>(&op_add);
+    out[MA_MUL] = reinterpret_cast<unsigned long long>(&op_mul);
+    out[MA_BATCH] = reinterpret_cast<unsigned long long>(&op_batch);
+    out[MA_EXPR_PROGS] = reinterpret_cast<unsigned long long>(&g_expr_progs[0]);
+  }
+  if (i < GPUOS_EW_NUM_OPS + 2) out[MA_REF_OPS + i] = reinterpret_cast<unsigned long long>(g_builtin_ref_ops[i]);
+  if (i < kExprPrograms) out[MA_EXPR_FNS + i] = reinterpret_cast<unsigned long long>(g_expr_fns[i]);
+}
+
+#ifndef GPUOS_JIT_WORKER
 __global__ void builtin_addr_kernel(int which, unsigned long long* out) {
   if (which == -1) *out = reinterpret_cast<unsigned long long>(&op_add);
   else if (which == -2) *out = reinterpret_cast<unsigned long long>(&op_mul);
@@ -68,11 +88,14 @@ __global__ void builtin_addr_kernel(int which, unsigned long long* out) {
   else *out = 0ull;
 }
 
+#endif  // GPUOS_JIT_WORKER
+
 extern "C" __global__ void __launch_bounds__(kMaxComputeThreads + 64, 1) gpuos_batch_worker(const __grid_constant__ WorkerParams P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   batch_worker_body(P, smem_raw);
 }
 
+#ifndef GPUOS_JIT_WORKER
 // ---- Task-ring worker (persistent_kernel.cu:138-231) --------------------------------------
 // Same protocol as the reference (CAS claim of q.head < q.tail, dispatch through the alias
 // and op table at dequeue time, completion counted after a system fence) with three
@@ -168,9 +191,12 @@ __global__ void ring_worker_kernel(WorkQueue q) {
   }
 }
 
+#endif  // GPUOS_JIT_WORKER
 }  // namespace gpuos
 
 using namespace gpuos;
+
+#ifndef GPUOS_JIT_WORKER
 
 // ---- reference C ABI (persistent_kernel.cu:233-269) --------------------------------------
 extern "C" cudaError_t launch_init_builtin_ops(cudaStream_t stream) {
@@ -187,7 +213,14 @@ extern "C" cudaError_t gpuos_internal_preload_kernels() {
   if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, builtin_addr_kernel);
   if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, gpuos_batch_worker);
   if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, ring_worker_kernel);
+  if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, gpuos_module_addrs);
   return e;
+}
+
+// Built-in operator addresses of this library's module (MA_COUNT values) into device memory.
+extern "C" cudaError_t gpuos_internal_module_addrs(unsigned long long* d_out, cudaStream_t s) {
+  gpuos_module_addrs<<<1, 64, 0, s>>>(d_out);
+  return cudaGetLastError();
 }
 
 extern "C" cudaError_t launch_persistent_worker(WorkQueue q, int blocks, int threads, cudaStream_t stream) {
@@ -294,13 +327,6 @@ extern "C" cudaError_t gpuos_internal_table_ptrs(void** table, void** alias) {
   return cudaGetSymbolAddress(alias, g_op_alias);
 }
 
-// Write expression program k (host copy) into the device table, stream-ordered on s.
-extern "C" cudaError_t gpuos_internal_set_expr_prog(int k, const void* prog, cudaStream_t s) {
-  if (k < 0 || k >= kExprPrograms) return cudaErrorInvalidValue;
-  return cudaMemcpyToSymbolAsync(g_expr_progs, prog, sizeof(ExprProg), (size_t)k * sizeof(ExprProg),
-                                 cudaMemcpyHostToDevice, s);
-}
-
 extern "C" size_t gpuos_internal_smem_header_bytes() { return (sizeof(SmemHeader) + 127) & ~size_t(127); }
 
 // ---- fixed scratch of the no-allocation entry point ------------------------------------------
@@ -340,3 +366,4 @@ extern "C" cudaError_t gpuos_internal_noalloc_scratch(size_t smem, void** ptr, s
   *bytes = StaticScratch::kBytes;
   return cudaSuccess;
 }
+#endif  // GPUOS_JIT_WORKER

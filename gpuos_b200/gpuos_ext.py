@@ -5,16 +5,18 @@ Every function of the reference module is here with the same name, defaults and 
 meaning.  The compiled binding (``_gpuos_ext``) provides the hot calls directly; this file
 adds the registry-style calls that the reference implements next to them:
 
-* ``register_elementwise(key, expr, arity)`` (gpuos_ext.cpp:870-881): expressions with
+* ``register_elementwise(key, expr, arity)`` (gpuos_ext.cpp:814-881): expressions with
   the exact semantics of a built-in operator map to that operator's reference-ABI device
-  function; any other C float expression is compiled on the host into a program for the
-  worker's expression interpreter (``register_expr``), so registering never loads a module
-  next to the running worker.
+  function; any other C float expression is compiled by NVRTC for sm_100a, linked into the
+  worker and installed in a slot (``register_jit``).  ``backend="interp"`` runs it on the
+  worker's expression interpreter instead, which loads nothing and never stops the worker.
 * ``register_reduce(key, op_name)`` (gpuos_ext.cpp:1003-1014): built-in sum/mean.
-* ``register_topk`` / ``submit_topk`` (gpuos_ext.cpp:1050-1071): slot 42; values are
-  produced by ``torch.topk`` as in the reference (top-k is not on the batched path).
-* ``load_and_register_custom(ptx, entry_name, slot)`` (gpuos_ext.cpp:1079-1088): not
-  provided; raises NotImplementedError.
+* ``register_topk`` / ``submit_topk`` (gpuos_ext.cpp:1050-1071): slot 42; top-k along the
+  last dimension of a contiguous tensor runs on the persistent worker, other cases through
+  ``torch.topk`` as in the reference.
+* ``load_and_register_custom(ptx, entry_name, slot)`` (gpuos_ext.cpp:1079-1088): PTX that
+  defines ``extern "C" __device__ void entry_name(const Task&)`` is linked into the worker
+  and the function's device address goes into ``slot``.
 
 Importing this module without the compiled extension raises ImportError: there is no CPU
 or PyTorch fallback for the runtime itself.
@@ -67,20 +69,33 @@ def _device_key(device=None) -> int:
     return torch.device(device).index if not isinstance(device, int) else device
 
 
-def register_elementwise(key: str, expr: str, arity: int, *, slot: int = -1, device=None) -> int:
-    """Register an element-wise operator ``R = expr(A[, B])`` and return its table slot."""
+def register_elementwise(key: str, expr: str, arity: int, *, slot: int = -1, device=None,
+                         backend: str = "auto") -> int:
+    """Register an element-wise operator ``R = expr(A[, B])`` and return its table slot.
+
+    backend: "auto" (a built-in operator when ``expr`` means exactly one and no slot is given,
+    otherwise NVRTC), "nvrtc", "builtin" or "interp" (the worker's expression interpreter)."""
     if arity not in (1, 2):
         raise ValueError("arity must be 1 or 2")
+    if backend not in ("auto", "nvrtc", "builtin", "interp"):
+        raise ValueError("backend must be 'auto', 'nvrtc', 'builtin' or 'interp'")
     dev = _device_key(device)
     with _reg_lock:
         hit = _slots.get((dev, key))
         if hit is not None and slot < 0:
             return hit
         op = _EXACT_EXPR.get(_norm(expr))
-        if op is not None and slot < 0:
+        if backend == "builtin" or (backend == "auto" and op is not None and slot < 0):
+            if op is None:
+                raise ValueError(f"{expr!r} is not a built-in operator")
             s = _ext.register_builtin("elementwise", op, device=dev)
-        else:
+            if slot >= 0:
+                _ext.set_slot(slot, _ext.get_slot(s, device=dev), device=dev)
+                s = slot
+        elif backend == "interp":
             s = _ext.register_expr(key, expr, arity, slot, device=dev)
+        else:
+            s = _ext.register_jit(expr, arity, slot, device=dev)
         _slots[(dev, key)] = s
         return s
 
@@ -108,17 +123,32 @@ def register_topk(key: str, k: int, dim: int, largest: bool, sorted: bool) -> in
 
 
 def submit_topk(slot: int, x, values, indices, k: int, dim: int, largest: bool, sorted: bool) -> None:  # noqa: A002
+    """Top-k of x along dim into values/indices, complete when this call returns (the reference
+    runs torch::topk on the calling thread, gpuos_ext.cpp:1050-1071).  Along the last dimension
+    of a contiguous float tensor with k <= 256 it runs on the persistent worker (sorted, ties to
+    the lower position); other cases use torch.topk as the reference does."""
+    nd = x.dim()
+    d = dim + nd if dim < 0 else dim
+    if (nd >= 1 and d == nd - 1 and x.is_cuda and x.is_contiguous() and x.numel() > 0
+            and x.dtype in (torch.float32, torch.float16, torch.bfloat16) and 1 <= k <= min(x.shape[-1], 256)
+            and values.is_contiguous() and indices.is_contiguous() and values.dtype == x.dtype
+            and indices.dtype == torch.int64 and tuple(values.shape) == tuple(x.shape[:-1]) + (k,)
+            and tuple(indices.shape) == tuple(values.shape)):
+        n = x.shape[-1]
+        _ext.submit_topk_rows(x.view(-1, n), values.view(-1, k), indices.view(-1, k), k, bool(largest))
+        _ext.flush(True, device=x.device.index)
+        return
     v, i = torch.topk(x, k, dim, largest, sorted)
     values.copy_(v)
     indices.copy_(i)
 
 
-def load_and_register_custom(ptx: str, entry_name: str, slot: int) -> None:
-    """Not provided.  Calling an operator of a separately loaded module from the persistent
-    worker hung the worker on B200 in this build's tests, so operators are not injected as
-    machine code; use ``register_elementwise`` with an expression instead."""
-    raise NotImplementedError("custom PTX operators are not supported; register an expression with "
-                              "register_elementwise instead")
+def load_and_register_custom(ptx: str, entry_name: str, slot: int) -> int:
+    """Link PTX that defines ``extern "C" __device__ void entry_name(const Task&)`` (the
+    reference operator ABI) into the worker and install the function in ``slot``.  The
+    reference stores the host handle of a kernel in the slot instead (gpuos_ext.cpp:347-354,
+    1079-1088)."""
+    return _ext.load_custom(ptx, entry_name, slot)
 
 
 def reset_registry() -> None:

@@ -273,9 +273,11 @@ int gpuos_rt_debug_inject_stall(gpuos_rt* rt);
 int gpuos_rt_stats(gpuos_rt* rt, int64_t* vals, int n);
 const char* gpuos_rt_stat_names(void);
 
-/* Op table control of the runtime's device (gpuos_ext.cpp:361-363,
- * persistent_kernel.cu:251-257).  Writes take effect for Tasks dequeued after the
- * call returns (online switch / dual-slot switch / rollback). */
+/* Op table control of the runtime (gpuos_ext.cpp:361-363, persistent_kernel.cu:251-257).
+ * The runtime's table starts as launch_init_builtin_ops sets the reference one (add@0, mul@1,
+ * batch@10, identity alias).  Writes take effect for Tasks dequeued after the call returns
+ * (online switch / dual-slot switch / rollback).  An address of this library's module (from
+ * gpu_get_builtin_op_async) is taken to mean the same operator of the module the worker runs. */
 int gpuos_rt_set_slot(gpuos_rt* rt, int slot, OpPtrInt fn);
 int gpuos_rt_get_slot(gpuos_rt* rt, int slot, OpPtrInt* fn);
 int gpuos_rt_set_alias(gpuos_rt* rt, int logical, int physical);
@@ -287,15 +289,16 @@ int gpuos_rt_get_alias(gpuos_rt* rt, int logical, int* physical);
 int gpuos_rt_register_builtin_reduce(gpuos_rt* rt, int red_op, int* slot);
 int gpuos_rt_register_builtin_ew(gpuos_rt* rt, int ew_op, int* slot);
 
-/* register_elementwise for expressions that are not a built-in operator
- * (gpuos_ext.cpp:814-881, there NVRTC): `expr` is a C float expression in A (and B when
+/* register_elementwise through the worker's expression interpreter (the alternative to
+ * gpuos_rt_register_jit that loads nothing and never stops the worker;
+ * gpuos_ext.cpp:814-881 compiles with NVRTC): `expr` is a C float expression in A (and B when
  * arity == 2) — literals, + - * /, comparisons, ! && ||, ?:, (float) casts and the float
  * functions exp log log1p expm1 sqrt rsqrt fabs tanh sin cos tan erf floor ceil trunc round
  * exp2 log2 log10 sinh cosh asin acos atan fmin fmax pow fmod atan2 copysign (with or
  * without the f suffix).  It is compiled on the host into a program for the worker's stack
  * machine (at most 64 steps, 16 stack slots) and becomes a reference-ABI operator: element i
  * of out = expr of element i of in0/in1 under the Task's broadcast strides, computed in float
- * and stored as out's dtype.  Up to 32 expressions per device; the operator goes to `slot`
+ * (transcendental functions in double, rounded once) and stored as out's dtype.  Up to 32 expressions per device; the operator goes to `slot`
  * (< 0: next free slot >= 20), *slot_out receives the slot.  No module is loaded, so a
  * running worker keeps running. */
 int gpuos_rt_register_expr(gpuos_rt* rt, const char* key, const char* expr, int arity,
@@ -305,6 +308,67 @@ int gpuos_rt_register_expr(gpuos_rt* rt, const char* key, const char* expr, int 
  * prog_out non-NULL (prog_bytes >= 336) the program is copied out: code[64] (uint8 opcodes),
  * imm[64] (float constants), then int32 len, arity, depth. */
 int gpuos_expr_compile(const char* expr, int arity, void* prog_out, int prog_bytes);
+
+/* ---- operators compiled at run time ---------------------------------------------------------
+ * Replaces the reference's NVRTC path (pytorch_ext/gpuos_ext.cpp:316-363 compile + load +
+ * address read, :814-881 register_elementwise, :1079-1088 load_and_register_custom).  There
+ * each operator is a module of its own whose address the running worker calls; here each
+ * operator is compiled by NVRTC as relocatable sm_100a code held to the worker's register
+ * budget, linked (nvJitLink) with the worker's relocatable code and every operator installed
+ * before it, and the worker runs from the linked module: the call stays inside one module.
+ * Installing stops the worker (published work drains first), loads the linked module (a module
+ * load waits for kernels running on the device), carries the op table and expression programs
+ * over to the new module's addresses and lets the next flush relaunch the worker.  Queued
+ * requests are not lost.  Each runtime resolves Tasks through its own op table (gpuos_rt_set_slot,
+ * gpuos_rt_set_alias); the table of the reference C ABI (gpu_set_op_table_async, read by
+ * launch_persistent_worker) is separate and only ever holds addresses of this library's module.
+ * NVRTC and nvJitLink are opened from $CUDA_HOME/lib64 (default /usr/local/cuda).  Up to 64
+ * operators per device. */
+
+/* register_elementwise (gpuos_ext.cpp:814-881): element i of out = expr(A[, B]) over a
+ * reference-layout Task, A and B read with the Task's sizes/strides and dtypes, computed in
+ * float with every transcendental function evaluated in double and rounded once, stored as
+ * out's dtype (round to nearest even).  expr is a C float expression (no ';', braces or
+ * quotes).  Goes to `slot` (< 0: next free slot >= 20); *slot_out receives it. */
+int gpuos_rt_register_jit(gpuos_rt* rt, const char* expr, int arity, int slot, int* slot_out);
+
+/* load_and_register_custom (gpuos_ext.cpp:1079-1088, fixed): `ptx` (ptx_len bytes) holds
+ * extern "C" __device__ void <entry>(const Task&) (the reference operator ABI, src/common.h:71);
+ * it is linked into the worker and entry's device address goes to `slot` (the reference stores
+ * a host CUfunction handle there). */
+int gpuos_rt_load_custom(gpuos_rt* rt, const char* ptx, size_t ptx_len, const char* entry, int slot,
+                         int* slot_out);
+
+/* The two halves of gpuos_rt_register_jit / gpuos_rt_load_custom, so that the slow half can run
+ * ahead of a switch point: gpuos_rt_jit_stage[_ptx] compiles and links (seconds; no device
+ * work, the worker keeps running), gpuos_rt_jit_commit stops the worker, loads the staged module
+ * and installs the operator in `slot` (milliseconds).  A staged operator can be committed only
+ * while no other operator was installed on the device after it was staged
+ * (GPUOS_ERR_INVALID otherwise: stage again).  gpuos_rt_jit_discard frees a staged operator
+ * (committed or not). */
+typedef struct gpuos_jit_staged gpuos_jit_staged;
+int gpuos_rt_jit_stage(gpuos_rt* rt, const char* expr, int arity, gpuos_jit_staged** staged);
+int gpuos_rt_jit_stage_ptx(gpuos_rt* rt, const char* ptx, size_t ptx_len, const char* entry,
+                           gpuos_jit_staged** staged);
+int gpuos_rt_jit_commit(gpuos_rt* rt, gpuos_jit_staged* staged, int slot, int* slot_out);
+void gpuos_rt_jit_discard(gpuos_jit_staged* staged);
+
+/* Operators compiled at run time installed on the runtime's device (negative: -status). */
+int gpuos_rt_jit_ops(gpuos_rt* rt);
+
+/* Address of a built-in operator (codes as gpu_get_builtin_op_async) in the worker module the
+ * runtime currently runs: what a slot must hold to run that operator. */
+int gpuos_rt_builtin_op(gpuos_rt* rt, int code, OpPtrInt* addr);
+
+/* Device-free checks (no CUDA device needed).  gpuos_jit_compile: NVRTC output of `src` for
+ * sm_100a (relocatable code, or PTX when ptx != 0); *size_out receives its size, copied to out
+ * when out != NULL and cap is large enough.  gpuos_jit_check_expr: compile a
+ * gpuos_rt_register_jit operator and link it with the worker; *image_bytes receives the size
+ * of the linked image.  gpuos_jit_nvrtc_version: major*1000 + minor*10, 0 if NVRTC cannot be
+ * opened. */
+int gpuos_jit_compile(const char* src, int ptx, void* out, size_t cap, size_t* size_out);
+int gpuos_jit_check_expr(const char* expr, int arity, size_t* image_bytes);
+int gpuos_jit_nvrtc_version(void);
 
 /* Device %globaltimer stamps of a completed flush: start of its first item and end
  * of its last item (ns).  Returns GPUOS_ERR_INVALID if `seq` is not complete or has

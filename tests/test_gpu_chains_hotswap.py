@@ -8,6 +8,7 @@ value (no lost or reordered request)."""
 import pytest
 import torch
 
+import bench
 from oracle.reference_semantics import same_bits
 
 pytestmark = pytest.mark.gpu
@@ -68,3 +69,17 @@ def test_chains_with_online_switch_and_alias_rollback(rt):
         ref = add_ref if phase in (0, 3) else mul_ref
         for out in outs:
             assert same_bits(out.cpu(), ref), phase
+
+
+def test_config5_full_size_one_gpu(rt):
+    """Config 5 at its full size on one runtime: 2048 chains x 32 dependent requests over the 19
+    config-2 operators, an NVRTC-compiled multiply committed into slot 0 at request 50000, the
+    dual-slot switch at 55000 and the rollback at 60000.  Every one of the 65536 requests is
+    checked against PyTorch CPU applied to its own GPU input (bit-exact or within 2 ulp), a
+    request that never ran keeps the sentinel value of its output (lost), and every probe Task
+    through op 0 must show its phase's operator (misdispatched)."""
+    r = bench.c5_run(rt, 0, 1, lambda: None)
+    assert r["requests"] == 2048 * 32
+    assert r["lost"] == 0 and r["wrong"] == 0 and r["misdispatched"] == 0, r
+    assert all(p > 0 for p in r["probes_per_phase"]), r["probes_per_phase"]
+    assert rt.get_slot(0) == rt.builtin_op_address(0) and rt.get_alias(0) == 0

@@ -161,6 +161,7 @@ def test_reference_task_ring_worker_c_abi(rt):
 
     assert lib.gpuos_ring_set_idle_limit_ms(5000, s) == 0
     mul_addr = rt.builtin_op_address(1)
+    lib.gpu_set_alias_async.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
     proc = ctypes.c_ulonglong(0)
     lib.gpu_get_processed_count_async(ctypes.byref(proc), s)
     stream.synchronize()
@@ -180,11 +181,16 @@ def test_reference_task_ring_worker_c_abi(rt):
     try:
         assert lib.launch_persistent_worker(q, 8, 128, s) == 0
         tail = 0
+        side_s = ctypes.c_void_p(side.cuda_stream)
         for phase, out in enumerate(outs):
+            # the ring worker resolves Tasks through the reference C ABI's table
+            # (test/dual_slot_switch.cpp:151, 158); the copy runs beside the running worker
             if phase == 1:
-                rt.set_alias(0, 1)
+                assert lib.gpu_set_alias_async(0, 1, side_s) == 0
+                side.synchronize()
             if phase == 2:
-                rt.set_alias(0, 0)
+                assert lib.gpu_set_alias_async(0, 0, side_s) == 0
+                side.synchronize()
             host = torch.frombuffer(bytearray(tasks_bytes(out, tail)), dtype=torch.uint8).pin_memory()
             with torch.cuda.stream(side):
                 ring[(tail % cap) * 496:(tail % cap) * 496 + ntask * 496].copy_(host, non_blocking=True)
@@ -208,7 +214,8 @@ def test_reference_task_ring_worker_c_abi(rt):
     finally:
         publish(2, 1)  # quit
         stream.synchronize()
-        rt.set_alias(0, 0)
+        lib.gpu_set_alias_async(0, 0, s)
+        stream.synchronize()
     assert mul_addr != 0
     Ac, Bc = A.cpu(), B.cpu()
     assert same_bits(outs[0].cpu(), Ac + Bc)
