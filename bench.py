@@ -607,6 +607,7 @@ def c5_run(g, rank, world, barrier, chains=2048, depth=32, n=4096, n_probe=2, re
     Y = Yd.cpu()
     YGc, YPc = YG.cpu(), YP.cpu()
     lost = wrong = 0
+    wrong_by_op, wrong_examples = {}, []
     for k in range(depth):
         for kd, (name, code, bin_, prm, exact, fn) in enumerate(ops):
             rows = (kinds[:, k] == kd).nonzero().flatten()
@@ -619,7 +620,18 @@ def c5_run(g, rank, world, barrier, chains=2048, depth=32, n=4096, n_probe=2, re
             ok = _rows_within(got, ref, exact, x, name)
             untouched = (got == C5_SENTINEL).all(dim=1) & ~(ref == C5_SENTINEL).all(dim=1)
             lost += int(untouched.sum())
-            wrong += int((~ok & ~untouched).sum())
+            bad = ~ok & ~untouched
+            nb = int(bad.sum())
+            wrong += nb
+            if nb:
+                wrong_by_op[name] = wrong_by_op.get(name, 0) + nb
+                r0 = int(bad.nonzero()[0])
+                gr, rr, xr = got[r0], ref[r0], x[r0]
+                diff = (gr != rr) & ~(torch.isnan(gr) & torch.isnan(rr))
+                e0 = int(diff.nonzero()[0]) if bool(diff.any()) else 0
+                if len(wrong_examples) < 8:
+                    wrong_examples.append({"op": name, "step": k, "x": float(xr[e0]), "got": float(gr[e0]),
+                                           "ref": float(rr[e0])})
     padd, pmul = (PA + PB).cpu(), (PA * PB).cpu()
     last = results[-1]
     mis = 0
@@ -631,6 +643,7 @@ def c5_run(g, rank, world, barrier, chains=2048, depth=32, n=4096, n_probe=2, re
             mis += 1
     finite = float(torch.isfinite(Y[depth]).float().mean())
     return {"requests": m * depth, "results": results, "lost": lost, "wrong": wrong, "misdispatched": mis,
+            "wrong_by_op": wrong_by_op, "wrong_examples": wrong_examples,
             "probes_per_phase": per_phase, "finite_fraction_final": finite}
 
 

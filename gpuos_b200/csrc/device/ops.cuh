@@ -60,7 +60,12 @@ __device__ __forceinline__ float ew_apply(float a, float b, float p0, float p1) 
   else if constexpr (OP == GPUOS_EW_POW) return (float)pow((double)a, (double)b);
   else if constexpr (OP == GPUOS_EW_COPY) return a;
   else if constexpr (OP == GPUOS_EW_RELU) return a < 0.f ? 0.f : a;
-  else if constexpr (OP == GPUOS_EW_SIGMOID) return (float)(1.0 / (1.0 + exp(-(double)a)));
+  else if constexpr (OP == GPUOS_EW_SIGMOID) {
+    // PyTorch CPU forms 1 / (1 + exp(-x)) in float: where exp(-x) overflows float (x below about
+    // -88.72) the result is 0, not the (denormal) true value
+    const double e = exp(-(double)a);
+    return isinf((float)e) ? 0.f : (float)(1.0 / (1.0 + e));
+  }
   else if constexpr (OP == GPUOS_EW_TANH) return (float)tanh((double)a);
   else if constexpr (OP == GPUOS_EW_EXP) return (float)exp((double)a);
   else if constexpr (OP == GPUOS_EW_LOG) return (float)log((double)a);
@@ -71,6 +76,10 @@ __device__ __forceinline__ float ew_apply(float a, float b, float p0, float p1) 
   else if constexpr (OP == GPUOS_EW_HARDSWISH)
     return __fdiv_rn(__fmul_rn(a, min_std(max_std(__fadd_rn(a, 3.f), 0.f), 6.f)), 6.f);
   else if constexpr (OP == GPUOS_EW_GELU) {
+    // PyTorch CPU (its vectorised kernel, which every tensor of 8 or more elements takes) gives NaN
+    // for +-inf and overflows to +inf once x (1 + erf(x / sqrt 2)) does in float (x >= 2^127)
+    if (isinf(a)) return qnan();
+    if (a >= 1.7014118346046923e38f) return __int_as_float(0x7f800000);
     const double x = a;
     return (float)(x * 0.5 * (1.0 + erf(x * 0.70710678118654752440)));
   } else if constexpr (OP == GPUOS_EW_GELU_TANH) {

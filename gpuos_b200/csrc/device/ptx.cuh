@@ -13,6 +13,11 @@ __device__ __forceinline__ uint64_t now_ns() {
   return t;
 }
 
+// Nanoseconds from `since` to `now`, 0 if `since` is later.  Reads of %globaltimer by different
+// warps are not ordered with each other: a stamp another warp wrote just before can be ahead of
+// this warp's next read, and a plain subtraction then wraps to ~2^64 (an instant "expired" wait).
+__device__ __forceinline__ uint64_t elapsed(uint64_t now, uint64_t since) { return now > since ? now - since : 0; }
+
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

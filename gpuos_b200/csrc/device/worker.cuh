@@ -40,11 +40,14 @@ __device__ __forceinline__ unsigned char* stage_buf(const WorkerShared& W, uint3
   return W.bufs + (size_t)s * W.stage_bytes;
 }
 
-__device__ __forceinline__ void report_error(const WorkerParams& P, uint32_t code, uint64_t item) {
+__device__ __forceinline__ void report_error(const WorkerParams& P, uint32_t code, uint64_t item,
+                                             uint64_t waited_ns = 0, uint64_t bound_ns = 0) {
   if (atomicCAS(&P.dc->abort, 0u, 1u) == 0u) {
+    if (bound_ns) P.dc->err_wait = ((waited_ns / 1000) << 32) | (bound_ns / 1000000);
     ptx::st_relaxed_sys(&P.rep->error_item, item);
     ptx::fence_acq_rel_sys();
     ptx::st_relaxed_sys(&P.rep->error, ((uint64_t)code << 32) | (uint32_t)blockIdx.x);
+    if (P.sticky_error) atomicCAS(P.sticky_error, 0ull, ((unsigned long long)code << 32) | (uint32_t)blockIdx.x);
   }
 }
 
@@ -126,12 +129,16 @@ __device__ void account(const WorkerParams& P, const DoneRun* runs, int nruns, b
 // Bounded wait on an mbarrier phase (one lane).  `alive` is a %globaltimer stamp another
 // role refreshes while it makes progress; the wait fails once it is older than `limit`.
 __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, const unsigned long long* alive,
-                                           uint64_t limit) {
+                                           uint64_t limit, uint64_t* waited) {
   uint32_t spins = 0;
   while (!ptx::mbar_try_wait(bar, parity)) {
     if ((++spins & 1023u) == 0) {
       const uint64_t a = *reinterpret_cast<const volatile unsigned long long*>(alive);
-      if (ptx::now_ns() - a > limit) return false;
+      const uint64_t w = ptx::elapsed(ptx::now_ns(), a);
+      if (w > limit) {
+        *waited = w;
+        return false;
+      }
     }
   }
   return true;
@@ -159,8 +166,9 @@ __device__ __forceinline__ void compute_loop(const WorkerParams& P, const Worker
   uint32_t s = 0, parity = 0;  // stage and phase parity of use `iter` (stages are used in order)
   for (uint64_t iter = 0;; ++iter, s = s + 1 == S ? 0 : s + 1, parity ^= s == 0 ? 1u : 0u) {
     unsigned long long c0 = clock64();
-    if (!wait_phase(ptx::smem_addr(&H.full[s]), parity, &H.prod_alive, H.full_wait_ns)) {
-      report_error(P, DE_WAIT_FULL, iter);
+    uint64_t waited = 0;
+    if (!wait_phase(ptx::smem_addr(&H.full[s]), parity, &H.prod_alive, H.full_wait_ns, &waited)) {
+      report_error(P, DE_WAIT_FULL, iter, waited, H.full_wait_ns);
       return;
     }
     const StageMeta& m = H.meta[s];
@@ -230,8 +238,9 @@ __device__ __forceinline__ void completer_loop(const WorkerParams& P, const Work
         nruns = 0;
         pending = 0;
       }
-      if (!wait_phase(full, parity, &H.prod_alive, H.full_wait_ns)) {
-        report_error(P, DE_WAIT_FULL, iter);
+      uint64_t waited = 0;
+      if (!wait_phase(full, parity, &H.prod_alive, H.full_wait_ns, &waited)) {
+        report_error(P, DE_WAIT_FULL, iter, waited, H.full_wait_ns);
         kind = IK_EXIT;
       } else {
         const WorkItem& it = H.meta[s].item;
@@ -258,11 +267,12 @@ __device__ __forceinline__ void completer_loop(const WorkerParams& P, const Work
         nruns = 0;
         pending = 0;
       }
-      bool ok = wait_phase(done, parity, &H.prod_alive, H.full_wait_ns);
+      uint64_t waited = 0;
+      bool ok = wait_phase(done, parity, &H.prod_alive, H.full_wait_ns, &waited);
       unsigned long long c1 = clock64();
       t_wait += c1 - c0;
       if (!ok) {
-        report_error(P, DE_WAIT_FULL, iter);
+        report_error(P, DE_WAIT_DONE, iter, waited, H.full_wait_ns);
       } else {
         ptx::mbar_arrive(ptx::smem_addr(&H.empty[s]));  // stage back to the dequeue warp
         if (nruns && runs[nruns - 1].batch == batch && runs[nruns - 1].batch_seq == batch_seq) {
@@ -347,8 +357,8 @@ __device__ __forceinline__ bool wait_empty(const WorkerParams& P, SmemHeader& H,
     if ((++spins & 255u) == 0) {
       const uint64_t t = ptx::now_ns();
       *reinterpret_cast<volatile unsigned long long*>(&H.prod_alive) = t;
-      if (t - t0 > H.wait_limit_ns) {
-        report_error(P, DE_WAIT_EMPTY, iter);
+      if (ptx::elapsed(t, t0) > H.wait_limit_ns) {
+        report_error(P, DE_WAIT_EMPTY, iter, ptx::elapsed(t, t0), H.wait_limit_ns);
         return false;
       }
     }
@@ -367,7 +377,7 @@ __device__ __forceinline__ bool drain_own(const WorkerParams& P, SmemHeader& H, 
     const uint64_t t0 = ptx::now_ns();
     uint32_t spins = 0;
     while (!ptx::mbar_try_wait(bar, parity)) {
-      if ((++spins & 255u) == 0 && ptx::now_ns() - t0 > H.wait_limit_ns) {
+      if ((++spins & 255u) == 0 && ptx::elapsed(ptx::now_ns(), t0) > H.wait_limit_ns) {
         report_error(P, DE_WAIT_EMPTY, u);
         return false;
       }
@@ -428,7 +438,7 @@ __device__ __forceinline__ int park(const WorkerParams& P, SmemHeader& H, const 
       if ((++spins & 15u) == 0) {
         const uint64_t now = ptx::now_ns();
         *reinterpret_cast<volatile unsigned long long*>(&H.prod_alive) = now;
-        if (now - t0 > kGatherNs) {  // someone is still busy: retry later
+        if (ptx::elapsed(now, t0) > kGatherNs) {  // someone is still busy: retry later
           ++C.timeouts;
           C.parked_seen = count_parked(dc, round);
           break;
@@ -473,8 +483,8 @@ __device__ __forceinline__ int park(const WorkerParams& P, SmemHeader& H, const 
     if ((++spins & 63u) == 0) {
       const uint64_t now = ptx::now_ns();
       *reinterpret_cast<volatile unsigned long long*>(&H.prod_alive) = now;
-      if (now - t0 > H.wait_limit_ns) {
-        report_error(P, DE_WAIT_PARK, st.ticket);
+      if (ptx::elapsed(now, t0) > H.wait_limit_ns) {
+        report_error(P, DE_WAIT_PARK, st.ticket, ptx::elapsed(now, t0), H.wait_limit_ns);
         return PV_EXIT;
       }
     }
@@ -615,8 +625,8 @@ __device__ __forceinline__ bool stage_item(const WorkerParams& P, const WorkerSh
         if ((++spins & 63u) == 0) {
           const uint64_t now = ptx::now_ns();
           *reinterpret_cast<volatile unsigned long long*>(&H.prod_alive) = now;
-          if (now - t0 > H.wait_limit_ns) {
-            report_error(P, DE_WAIT_BARRIER, st.ticket);
+          if (ptx::elapsed(now, t0) > H.wait_limit_ns) {
+            report_error(P, DE_WAIT_BARRIER, st.ticket, ptx::elapsed(now, t0), H.wait_limit_ns);
             ok = 0;
             break;
           }
@@ -835,7 +845,7 @@ __device__ __forceinline__ void producer_loop(const WorkerParams& P, const Worke
           // only the leader reads host memory; everybody else polls its device mirror
           const uint64_t r0 = ptx::now_ns();
           t = ptx::ld_acquire_sys(&P.hc->tail);
-          const uint64_t dr = ptx::now_ns() - r0;
+          const uint64_t dr = ptx::elapsed(ptx::now_ns(), r0);
           C.read_sum += dr;
           ++C.read_n;
           if (dr > C.read_max) C.read_max = dr;
@@ -877,7 +887,7 @@ __device__ __forceinline__ void producer_loop(const WorkerParams& P, const Worke
             want_exit = C.quit_epoch >= P.epoch;
           }
           if (C.yield_every && ptx::ld_acquire_gpu(&dc->items_done) - dc->yield_base >= C.yield_every) want_exit = true;
-          if (now - C.beat_t > C.safety_ns) want_exit = true;
+          if (ptx::elapsed(now, C.beat_t) > C.safety_ns) want_exit = true;
           if (want_exit) {
             C.round = (C.round > C.seen_round ? C.round : C.seen_round) + 1;
             if (C.rounds == 0) tl_mark(P, TL_ROUND);
@@ -1026,7 +1036,7 @@ __device__ void batch_worker_body(const WorkerParams& P, unsigned char* smem_raw
     } else {
       const uint64_t t0 = ptx::now_ns();
       while (ptx::ld_acquire_gpu(&dc->launch_epoch) != P.epoch) {
-        if (ptx::now_ns() - t0 > P.wait_limit_ns) {
+        if (ptx::elapsed(ptx::now_ns(), t0) > P.wait_limit_ns) {
           report_error(P, DE_WAIT_START, 0);
           start_ok = 0;
           break;

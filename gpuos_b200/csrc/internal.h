@@ -135,7 +135,8 @@ enum DeviceError : uint32_t {
   DE_WAIT_START = 5,    // grid start coordination timed out
   DE_BAD_ITEM = 6,      // malformed item (kind / slot / ndim out of range)
   DE_NULL_OP = 7,       // table slot resolved to a null function
-  DE_HOST_LOST = 8      // host heartbeat stopped while idle
+  DE_HOST_LOST = 8,     // host heartbeat stopped while idle
+  DE_WAIT_DONE = 9      // completer: compute warps did not finish a stage in time
 };
 
 // Completion ticket of one flush (mapped pinned memory, one writer).
@@ -240,7 +241,7 @@ struct alignas(128) DevCtl {
   unsigned long long closing;      // leader requests grid exit (round number)
   unsigned long long verdict;      // (round << 2) | 1 resume | 2 exit
   unsigned long long park_min;     // lowest held ticket among parked CTAs
-  unsigned long long _reserved;
+  unsigned long long err_wait;      // first expired wait: (waited us << 32) | bound ms
   unsigned int abort;              // a CTA hit an error: everybody exits
   unsigned int exited;             // CTAs that left the current launch
   unsigned long long yield_base;   // items_done at launch (yield accounting)
@@ -275,6 +276,9 @@ struct WorkerParams {
   uint32_t compute_threads;
   uint32_t _pad;
   uint64_t wait_limit_ns;  // bound of the launch-start wait (HostCtl::wait_limit_ns at launch)
+  // optional: the first error of the launch is also recorded here (if still 0), in memory that
+  // outlives the launch's report (the no-allocation entry point's sticky error word)
+  unsigned long long* sticky_error;
 };
 
 // Per-stage bookkeeping in shared memory.
@@ -353,6 +357,9 @@ struct StaticScratch {
   static constexpr size_t kDevCtl = 256;
   static constexpr size_t kTickets = round_up256(kDevCtl + sizeof(DevCtl));
   static constexpr size_t kLayouts = kTickets + 256;  // tickets of batch slots 0..7
+  // ticket slot 7 (never used: every call is flush 1) holds the sticky error word, which the
+  // per-call image copy leaves alone
+  static constexpr size_t kSticky = kTickets + 7 * 32;
   static constexpr size_t kItems = round_up256(kLayouts + kMaxLayouts * sizeof(Layout));
   static constexpr size_t kBytes = kItems + kMaxItems * sizeof(WorkItem);
 };

@@ -884,12 +884,18 @@ static int check_device_error_locked(gpuos_rt* rt) {
                                 "start coordination wait expired",
                                 "malformed work item",
                                 "task dispatched to an empty op-table slot",
-                                "host heartbeat lost"};
+                                "host heartbeat lost",
+                                "completer: compute warps did not finish a stage in time"};
   const uint32_t code = (uint32_t)(e >> 32);
   rt->failed = true;
-  char buf[256];
-  snprintf(buf, sizeof(buf), "worker error: %s (block %u, item %llu)", code < 9 ? names[code] : "unknown",
-           (unsigned)(e & 0xffffffffu), (unsigned long long)rt->rep->error_item);
+  // how long the expired wait lasted against which bound (device memory, read on this error path)
+  unsigned long long ew = 0;
+  if (cudaSetDevice(rt->device) == cudaSuccess)
+    cudaMemcpy(&ew, &rt->dc->err_wait, sizeof(ew), cudaMemcpyDeviceToHost);
+  char buf[320];
+  snprintf(buf, sizeof(buf), "worker error: %s (block %u, item %llu%s%llu us of a %llu ms bound)",
+           code < 10 ? names[code] : "unknown", (unsigned)(e & 0xffffffffu), (unsigned long long)rt->rep->error_item,
+           ew ? "; waited " : "; ", ew >> 32, ew & 0xffffffffull);
   rt->fail_msg = buf;
   return fail(GPUOS_ERR_DEVICE, "%s", buf);
 }
@@ -2240,6 +2246,37 @@ extern "C" int gpuos_abi_sizes(int64_t* out, int n) {
 // is done).  Device memory is never allocated; host staging buffers are per thread and reused.
 extern "C" cudaError_t gpuos_internal_noalloc_scratch(size_t smem, void** ptr, size_t* bytes);
 
+// Wait for `stream` with a bound (GPUOS_NOALLOC_WAIT_MS, default 60000) instead of blocking for
+// good: the launch needs every SM at once, and other work can keep them.
+static int noalloc_wait(cudaStream_t stream) {
+  const uint64_t limit = (uint64_t)std::max(1, env_int("GPUOS_NOALLOC_WAIT_MS", 60000)) * 1000000ull;
+  const uint64_t t0 = mono_ns();
+  uint32_t spins = 0;
+  while (true) {
+    const cudaError_t q = cudaStreamQuery(stream);
+    if (q == cudaSuccess) return GPUOS_OK;
+    if (q != cudaErrorNotReady) return fail(GPUOS_ERR_CUDA, "stream: %s", cudaGetErrorString(q));
+    if (mono_ns() - t0 > limit)
+      return fail(GPUOS_ERR_TIMEOUT, "the stream did not finish within %llu ms (the launch needs every SM)",
+                  (unsigned long long)(limit / 1000000ull));
+    if (++spins < 256) std::this_thread::yield();
+    else std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+}
+
+// Read and clear the sticky error word (the first device error of any call since it was last
+// cleared), stream-ordered on `stream`; *err receives it (0: none).
+static int noalloc_take_sticky(unsigned char* base, cudaStream_t stream, unsigned long long* err) {
+  static thread_local unsigned long long word;
+  word = 0;
+  CK(cudaMemcpyAsync(&word, base + StaticScratch::kSticky, sizeof(word), cudaMemcpyDeviceToHost, stream));
+  CK(cudaMemsetAsync(base + StaticScratch::kSticky, 0, sizeof(word), stream));
+  const int e = noalloc_wait(stream);
+  if (e) return e;
+  *err = word;
+  return GPUOS_OK;
+}
+
 extern "C" int gpuos_ew_batch_noalloc(const GpuosEwRequest* reqs, int nreq, int flags, cudaStream_t stream) {
   using SS = StaticScratch;
   if (nreq < 0 || (nreq > 0 && !reqs)) return fail(GPUOS_ERR_INVALID, "null request array");
@@ -2303,11 +2340,6 @@ extern "C" int gpuos_ew_batch_noalloc(const GpuosEwRequest* reqs, int nreq, int 
     }
   }
   const uint64_t n = h.items.size();
-  if (n == 0) {
-    if (flags & GPUOS_FLUSH_SYNC) CK(cudaStreamSynchronize(stream));
-    return GPUOS_OK;
-  }
-
   int dev = 0, sm_count = 0, smem_optin = 0;
   CK(cudaGetDevice(&dev));
   CK(cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev));
@@ -2318,6 +2350,17 @@ extern "C" int gpuos_ew_batch_noalloc(const GpuosEwRequest* reqs, int nreq, int 
   void* scratch = nullptr;
   size_t scratch_bytes = 0;
   CK(gpuos_internal_noalloc_scratch(smem, &scratch, &scratch_bytes));
+  unsigned char* base = static_cast<unsigned char*>(scratch);
+  if (n == 0) {
+    if (!(flags & GPUOS_FLUSH_SYNC)) return GPUOS_OK;
+    unsigned long long sticky = 0;
+    const int e = noalloc_take_sticky(base, stream, &sticky);
+    if (e) return e;
+    if (sticky)
+      return fail(GPUOS_ERR_DEVICE, "an earlier call without GPUOS_FLUSH_SYNC failed on the device: worker error code "
+                  "%llu detail %llu", sticky >> 32, sticky & 0xffffffffull);
+    return GPUOS_OK;
+  }
   void *op_table = nullptr, *op_alias = nullptr;
   CK(gpuos_internal_table_ptrs(&op_table, &op_alias));
 
@@ -2346,8 +2389,10 @@ extern "C" int gpuos_ew_batch_noalloc(const GpuosEwRequest* reqs, int nreq, int 
     it.batch_seq = seq;
     items[i] = it;
   }
-  unsigned char* base = static_cast<unsigned char*>(scratch);
-  CK(cudaMemcpyAsync(base, img, image_bytes, cudaMemcpyHostToDevice, stream));
+  // everything but the sticky error word, which keeps a failed asynchronous call's error
+  CK(cudaMemcpyAsync(base, img, SS::kSticky, cudaMemcpyHostToDevice, stream));
+  CK(cudaMemcpyAsync(base + SS::kSticky + 32, img + SS::kSticky + 32, image_bytes - SS::kSticky - 32,
+                     cudaMemcpyHostToDevice, stream));
 
   WorkerParams P;
   std::memset(&P, 0, sizeof(P));
@@ -2368,18 +2413,24 @@ extern "C" int gpuos_ew_batch_noalloc(const GpuosEwRequest* reqs, int nreq, int 
   P.stage_bytes = kStageBytesDefault;
   P.compute_threads = 256;
   P.wait_limit_ns = hc->wait_limit_ns;
+  P.sticky_error = reinterpret_cast<unsigned long long*>(base + SS::kSticky);
   CK(gpuos_internal_launch_batch_worker(&P, sm_count, 256 + 64, smem, stream));
   if (!(flags & GPUOS_FLUSH_SYNC)) return GPUOS_OK;
 
-  DevReport rep;
-  Ticket tk;
+  static thread_local DevReport rep;
+  static thread_local Ticket tk;
   CK(cudaMemcpyAsync(&rep, base + SS::kReport, sizeof(rep), cudaMemcpyDeviceToHost, stream));
   CK(cudaMemcpyAsync(&tk, base + SS::kTickets + slot * sizeof(Ticket), sizeof(tk), cudaMemcpyDeviceToHost, stream));
-  CK(cudaStreamSynchronize(stream));
+  unsigned long long sticky = 0;
+  const int we = noalloc_take_sticky(base, stream, &sticky);
+  if (we) return we;
   if (rep.error != 0)
     return fail(GPUOS_ERR_DEVICE, "worker error code %llu detail %llu at tile %llu",
                 (unsigned long long)(rep.error >> 32), (unsigned long long)(rep.error & 0xffffffffull),
                 (unsigned long long)rep.error_item);
+  if (sticky)
+    return fail(GPUOS_ERR_DEVICE, "an earlier call without GPUOS_FLUSH_SYNC failed on the device: worker error code "
+                "%llu detail %llu", sticky >> 32, sticky & 0xffffffffull);
   if (rep.items_done != n || tk.seq != seq)
     return fail(GPUOS_ERR_DEVICE, "worker exited after %llu of %llu tiles", (unsigned long long)rep.items_done,
                 (unsigned long long)n);

@@ -160,7 +160,7 @@ __global__ void ring_worker_kernel(WorkQueue q) {
               q.sync->processed = atomicAdd(&g_processed_count, 0ull);
             }
           }
-          if (now - idle_since > g_ring_idle_limit_ns) s_state = 2;
+          if (ptx::elapsed(now, idle_since) > g_ring_idle_limit_ns) s_state = 2;
         }
       }
     }

@@ -429,13 +429,21 @@ int gpuos_plan_reduce(int red_op, const GpuosOperand* x, const GpuosOperand* out
  * The work runs on the current device, in stream order on `stream`: requests see earlier
  * work on `stream`, later work on `stream` sees their results, and requests of one call that
  * overlap in memory run in submission order.  Without GPUOS_FLUSH_SYNC the call returns once
- * the work is enqueued; with it, the call waits for `stream` and reports a device-side error
- * (GPUOS_ERR_DEVICE).  Every call shares the one scratch array and resets it: calls that
- * overlap on the GPU (issued on different streams, or from different threads) race and
- * corrupt each other.  The first call on a device resolves the array's address and sets up
- * the kernel; make that first call before any stream capture is begun.  The persistent
- * worker of gpuos_rt_init, while running on the same device, holds the SMs this launch needs,
- * so the launch starts once that worker has gone idle (GPUOS_IDLE_QUIESCE_MS). */
+ * the work is enqueued; with it, the call waits for `stream` (at most GPUOS_NOALLOC_WAIT_MS,
+ * default 60000 ms, then GPUOS_ERR_TIMEOUT) and reports a device-side error (GPUOS_ERR_DEVICE).
+ * The first device-side error of a call made without GPUOS_FLUSH_SYNC is kept in the array and
+ * reported, then cleared, by the next call made with it on that device; a call with nreq == 0
+ * and GPUOS_FLUSH_SYNC only does that (a status query).  Every call shares the one scratch
+ * array and resets it: calls that overlap on the GPU (issued on different streams, or from
+ * different threads) race and corrupt each other.  The first call on a device resolves the array's address and sets up
+ * the kernel; make that first call before any stream capture is begun.  The launch puts one
+ * CTA on every SM and its CTAs coordinate with one another, so all of them must be resident at
+ * once: kernels on other streams that hold SMs for longer than GPUOS_DEVICE_WAIT_MS (default
+ * 5000 ms) make it fail with a device-side error instead of running.  The persistent worker of
+ * gpuos_rt_init, while running on the same device, holds those SMs, so the launch starts once
+ * that worker has gone idle (GPUOS_IDLE_QUIESCE_MS); with the idle stop disabled
+ * (gpuos_rt_set_idle_quiesce_ms(rt, -1)) it starts only after gpuos_rt_quiesce or shutdown, and a
+ * synchronous call returns GPUOS_ERR_TIMEOUT meanwhile. */
 #define GPUOS_NOALLOC_MAX_TILES 16384
 #define GPUOS_NOALLOC_MAX_STRIDED 64
 

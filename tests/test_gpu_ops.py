@@ -128,6 +128,29 @@ def test_op_strided_broadcast_mixed(rt, name):
         assert ok, f"{name} R={R} C={C}: {msg}"
 
 
+EDGE = [float("inf"), -float("inf"), float("nan"), 0.0, -0.0, 1e-40, -1e-40, 1e-30, -1e-30, 88.72, 88.73,
+        -88.72, -88.73, -100.0, 100.0, 1e4, -1e4, 3.4e38, -3.4e38, 1.7e38, -1.7e38, 20.0, 20.5, -20.0, 0.5, -0.5]
+
+
+@pytest.mark.parametrize("name", sorted(TRANSCENDENTAL_NAMES))
+def test_transcendental_edge_values(rt, name):
+    """Infinities, NaN, zeros, denormals and values where float intermediates overflow follow
+    PyTorch CPU's vectorised kernels (0 from sigmoid once float exp(-x) overflows, NaN from GELU
+    at +-inf, +inf from GELU for x >= 2**127)."""
+    op = EW[name]
+    p0, p1 = PARAMS.get(name, (0.0, 0.0))
+    x = torch.tensor(EDGE * 2, dtype=torch.float32)
+    y = torch.full_like(x, 1.5)
+    if name in ("LOG", "SQRT"):
+        x = x.abs()
+    out = torch.empty_like(x, device="cuda")
+    rt.submit_elementwise(op, x.cuda(), y.cuda() if op in BINARY else None, out, p0, p1)
+    rt.flush(sync=True)
+    ref = ew_torch(op, x, y if op in BINARY else None, p0, p1)
+    ok, msg = compare(name, out.cpu(), ref, torch.float32, x)
+    assert ok, f"{name}: {msg}"
+
+
 def test_scalar_and_broadcast_operands(rt):
     x = torch.randn(33, 65)
     xd = x.cuda()

@@ -145,3 +145,25 @@ def test_noalloc_rejects_batches_beyond_the_limit(rt):
     assert b"GPUOS_NOALLOC_MAX_TILES" in lib.gpuos_rt_last_error()
     assert not bool(x.any())
     assert lib.gpuos_ew_batch_noalloc(ctypes.byref(r), 1, 4, ctypes.c_void_p(stream.cuda_stream)) == GPUOS_ERR_INVALID
+
+
+def test_noalloc_allocates_no_device_memory(rt):
+    """After a first call (which resolves the array's address), further calls change neither the
+    device's free memory nor the caching allocator's reservation; an empty synchronous call is a
+    status query that reports no earlier device error."""
+    lib = _lib()
+    stream = torch.cuda.Stream()
+    ins, shapes, dtypes, reqs = _workload(13)
+    got = _outputs(shapes, dtypes)
+    _run_noalloc(lib, ins, got, reqs, stream)
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    reserved0 = torch.cuda.memory_reserved()
+    for flags in (GPUOS_FLUSH_SYNC, 0, 0, GPUOS_FLUSH_SYNC):
+        _run_noalloc(lib, ins, got, reqs, stream, flags=flags)
+    rc = lib.gpuos_ew_batch_noalloc(None, 0, GPUOS_FLUSH_SYNC, ctypes.c_void_p(stream.cuda_stream))
+    assert rc == 0, lib.gpuos_rt_last_error()
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+    assert torch.cuda.memory_reserved() == reserved0
