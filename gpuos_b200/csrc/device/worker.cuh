@@ -34,6 +34,7 @@ struct WorkerShared {
   SmemHeader* H;
   unsigned char* bufs;
   uint32_t stage_bytes;
+  uint64_t load_policy;  // L2 cache policy of operand bulk loads (0: none)
 };
 
 __device__ __forceinline__ unsigned char* stage_buf(const WorkerShared& W, uint32_t s) {
@@ -145,77 +146,86 @@ __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, const 
 }
 
 // ---- compute warps ----------------------------------------------------------------------
+// Diagnostics of the compute warps (thread 0): cycles waiting for filled stages and inside tiles.
+__device__ __forceinline__ void compute_diag(const WorkerParams& P, uint32_t ctid, unsigned long long wait_c,
+                                             unsigned long long tile_c, unsigned long long fill_c) {
+  if (ctid == 0 && blockIdx.x < kDiagCtas) {
+    unsigned long long* row = P.dc->diag[blockIdx.x];
+    row[DG_C_WAIT_FULL] = wait_c;
+    row[DG_C_TILE] = tile_c;
+    row[DG_C_FILL] = fill_c;
+  }
+}
+
 __device__ __forceinline__ void compute_loop(const WorkerParams& P, const WorkerShared& W, uint32_t ctid, uint32_t nct) {
   SmemHeader& H = *W.H;
   const uint32_t S = P.stages;
-  unsigned long long dg[4] = {0, 0, 0, 0};
-  unsigned long long n_items = 0;
-  struct Flush {
-    const WorkerParams& P;
-    uint32_t ctid;
-    unsigned long long* dg;
-    unsigned long long* n;
-    __device__ ~Flush() {
-      if (ctid == 0 && blockIdx.x < kDiagCtas) {
-        unsigned long long* row = P.dc->diag[blockIdx.x];
-        row[DG_C_WAIT_FULL] = dg[0];
-        row[DG_C_TILE] = dg[1];
-      }
-    }
-  } flush_diag{P, ctid, dg, &n_items};
+  // plain registers: counters reached through a pointer would live in local memory and cost every
+  // compute thread a local load and store per item
+  unsigned long long wait_c = 0, tile_c = 0, fill_c = 0;
   uint32_t s = 0, parity = 0;  // stage and phase parity of use `iter` (stages are used in order)
   for (uint64_t iter = 0;; ++iter, s = s + 1 == S ? 0 : s + 1, parity ^= s == 0 ? 1u : 0u) {
-    unsigned long long c0 = clock64();
+    const unsigned long long c0 = clock64();
     uint64_t waited = 0;
     if (!wait_phase(ptx::smem_addr(&H.full[s]), parity, &H.prod_alive, H.full_wait_ns, &waited)) {
       report_error(P, DE_WAIT_FULL, iter, waited, H.full_wait_ns);
+      compute_diag(P, ctid, wait_c, tile_c, fill_c);
       return;
     }
     const StageMeta& m = H.meta[s];
     const uint8_t kind = m.item.kind;
-    unsigned long long c1 = clock64();
-    dg[0] += c1 - c0;
-    if (kind == IK_EXIT) return;
+    const unsigned long long c1 = clock64();
+    wait_c += c1 - c0;
+    if (ctid == 0 && (kind == IK_EW_CONTIG || kind == IK_ROW_REDUCE) && m.staged) fill_c += c1 - m.t_issue;
+    if (kind == IK_EXIT) {
+      compute_diag(P, ctid, wait_c, tile_c, fill_c);
+      return;
+    }
     if (kind == IK_TASK) {
       ptx::named_bar_sync(kBarTask, blockDim.x);
       OpFn fn = reinterpret_cast<OpFn>(m.item.x);
       fn(m.ext.task);
       ptx::named_bar_sync(kBarTask, blockDim.x);
     } else {
-      TileCtx ctx;
-      ctx.m = &m;
-      ctx.sa = stage_buf(W, s);
-      ctx.sb = stage_buf(W, s) + (W.stage_bytes >> 1);
-      ctx.tid = ctid;
-      ctx.nt = nct;
+      const unsigned char* sa = stage_buf(W, s);
+      const unsigned char* sb = sa + (W.stage_bytes >> 1);
       if (iter == 0 && ctid == 0) tl_mark(P, TL_TILE0);
       // inlined paths first (no register saves around a call through the tile table)
-      if (kind == IK_EW_CONTIG && f32_staged_tile(m, ctx.sa, ctx.sb, ctid, nct)) {
-      } else if (kind == IK_ROW_REDUCE) {
-        row_reduce_body(ctx);
+      if (kind == IK_EW_CONTIG && f32_staged_tile(m, sa, sb, ctid, nct)) {
       } else {
-        const uint32_t fi =
-            (kind == IK_EW_CONTIG || kind == IK_EW_GENERIC || kind == IK_EW_2D) ? m.item.op : GPUOS_EW_NUM_OPS;
-        TileFn fn = g_tile_fns[fi];
-        fn(ctx);
+        // the tile context exists only here: its address goes to the tile function, so it
+        // lives in local memory, which the inlined fp32 path above must not pay for
+        TileCtx ctx;
+        ctx.m = &m;
+        ctx.sa = sa;
+        ctx.sb = sb;
+        ctx.tid = ctid;
+        ctx.nt = nct;
+        if (kind == IK_ROW_REDUCE) {
+          row_reduce_body(ctx);
+        } else {
+          const uint32_t fi =
+              (kind == IK_EW_CONTIG || kind == IK_EW_GENERIC || kind == IK_EW_2D) ? m.item.op : GPUOS_EW_NUM_OPS;
+          TileFn fn = g_tile_fns[fi];
+          fn(ctx);
+        }
       }
       if (iter == 0 && ctid == 0) tl_mark(P, TL_TILE1);
     }
     // this warp is done with the stage; no CTA-wide barrier between tiles
     __syncwarp();
     if ((ctid & 31) == 0) ptx::mbar_arrive(ptx::smem_addr(&H.done[s]));
-    if (ctid == 0) {
-      dg[1] += clock64() - c1;
-      ++n_items;
-    }
+    tile_c += clock64() - c1;
   }
 }
 
 // ---- completer warp ------------------------------------------------------------------------
 // Follows the stages in order: once every compute warp has signalled `done`, it hands the
 // stage back to the dequeue warp and batches the completion accounting of several items
-// behind one fence.  Before it would block it publishes what it has, so a lone item is
-// accounted immediately.
+// behind one fence.  Before it would block on a stage the dequeue warp has not armed yet (no
+// more work staged) it publishes what it has, so a lone item is accounted immediately; while
+// armed stages are still loading or computing it keeps batching (an account is a gpu-scope fence
+// and two contended atomics, and the next stage's release would wait behind it).
 __device__ __forceinline__ void completer_loop(const WorkerParams& P, const WorkerShared& W, uint32_t lane) {
   SmemHeader& H = *W.H;
   const uint32_t S = P.stages;
@@ -223,6 +233,7 @@ __device__ __forceinline__ void completer_loop(const WorkerParams& P, const Work
   int nruns = 0;
   bool first_account = true;
   uint32_t pending = 0;
+  const uint32_t acc_every = P.account_every ? P.account_every : kAccountEvery;
   unsigned long long t_wait = 0, t_acc = 0, n_items = 0;
   uint32_t s = 0, parity = 0;  // stage and phase parity of use `iter`
   for (uint64_t iter = 0;; ++iter, s = s + 1 == S ? 0 : s + 1, parity ^= s == 0 ? 1u : 0u) {
@@ -231,7 +242,8 @@ __device__ __forceinline__ void completer_loop(const WorkerParams& P, const Work
     if (lane == 0) {
       unsigned long long c0 = clock64();
       const uint32_t full = ptx::smem_addr(&H.full[s]);
-      if (nruns && !ptx::mbar_test_wait(full, parity)) {
+      const uint32_t armed = *reinterpret_cast<volatile unsigned int*>(&H.armed);
+      if (nruns && (int32_t)(armed - (uint32_t)iter) <= 0 && !ptx::mbar_test_wait(full, parity)) {
         unsigned long long a0 = clock64();
         account(P, runs, nruns, &first_account);
         t_acc += clock64() - a0;
@@ -262,7 +274,8 @@ __device__ __forceinline__ void completer_loop(const WorkerParams& P, const Work
     if (lane == 0) {
       unsigned long long c0 = clock64();
       const uint32_t done = ptx::smem_addr(&H.done[s]);
-      if (nruns && !ptx::mbar_test_wait(done, parity)) {
+      const uint32_t armed = *reinterpret_cast<volatile unsigned int*>(&H.armed);
+      if (nruns && (int32_t)(armed - (uint32_t)(iter + 1)) <= 0 && !ptx::mbar_test_wait(done, parity)) {
         account(P, runs, nruns, &first_account);
         nruns = 0;
         pending = 0;
@@ -282,7 +295,7 @@ __device__ __forceinline__ void completer_loop(const WorkerParams& P, const Work
         }
         ++pending;
         ++n_items;
-        if (pending >= kAccountEvery || nruns == kMaxRuns) {
+        if (pending >= acc_every || nruns == kMaxRuns) {
           account(P, runs, nruns, &first_account);
           nruns = 0;
           pending = 0;
@@ -523,6 +536,7 @@ __device__ __forceinline__ bool group_kind(const WorkItem& it) {
 // and arrive on its full barrier (one thread).  m.item is already written.
 __device__ __forceinline__ void stage_copies(const WorkerShared& W, StageMeta& m, uint32_t s, const WorkItem& it) {
   const uint32_t full = ptx::smem_addr(&W.H->full[s]);
+  m.t_issue = clock64();
   unsigned char* buf = stage_buf(W, s);
   uint32_t staged = 0;
   if (it.kind == IK_EW_CONTIG) {
@@ -552,9 +566,18 @@ __device__ __forceinline__ void stage_copies(const WorkerShared& W, StageMeta& m
     m.staged = staged;
     if (tx) {
       ptx::mbar_arrive_expect_tx(full, tx);
-      if (staged & 1) ptx::bulk_g2s(ptx::smem_addr(buf), reinterpret_cast<const void*>(a0), (uint32_t)(a1 - a0), full);
-      if (staged & 2)
-        ptx::bulk_g2s(ptx::smem_addr(buf + half), reinterpret_cast<const void*>(b0), (uint32_t)(b1 - b0), full);
+      if (W.load_policy) {
+        if (staged & 1)
+          ptx::bulk_g2s_hint(ptx::smem_addr(buf), reinterpret_cast<const void*>(a0), (uint32_t)(a1 - a0), full,
+                             W.load_policy);
+        if (staged & 2)
+          ptx::bulk_g2s_hint(ptx::smem_addr(buf + half), reinterpret_cast<const void*>(b0), (uint32_t)(b1 - b0), full,
+                             W.load_policy);
+      } else {
+        if (staged & 1) ptx::bulk_g2s(ptx::smem_addr(buf), reinterpret_cast<const void*>(a0), (uint32_t)(a1 - a0), full);
+        if (staged & 2)
+          ptx::bulk_g2s(ptx::smem_addr(buf + half), reinterpret_cast<const void*>(b0), (uint32_t)(b1 - b0), full);
+      }
     } else {
       ptx::mbar_arrive(full);
     }
@@ -664,7 +687,6 @@ __device__ __forceinline__ bool stage_item(const WorkerParams& P, const WorkerSh
   }
   __syncwarp();
   if (lane == 0) {
-    const unsigned long long c_tma = clock64();
     if (it.kind == IK_TASK) {
       m.staged = 0;
       const OpFn fn = resolve_op(P, m.ext.task.op);
@@ -679,7 +701,6 @@ __device__ __forceinline__ bool stage_item(const WorkerParams& P, const WorkerSh
     } else {
       stage_copies(W, m, s, it);
     }
-    H.cold.dg[kDgTma] += clock64() - c_tma;
     if (st.iter == 0) tl_mark(P, TL_TMA);
   }
   ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -693,6 +714,7 @@ __device__ __forceinline__ bool stage_item(const WorkerParams& P, const WorkerSh
   }
   advance(st, 1, S);
   st.ticket += 1;
+  if (lane == 0) *reinterpret_cast<volatile unsigned int*>(&H.armed) = (uint32_t)st.iter;
   return true;
 }
 
@@ -742,6 +764,7 @@ __device__ __forceinline__ uint32_t stage_group(const WorkerParams& P, const Wor
   __syncwarp();
   advance(st, g, S);
   st.ticket += g;
+  if (lane == 0) *reinterpret_cast<volatile unsigned int*>(&H.armed) = (uint32_t)st.iter;
   return g;
 }
 
@@ -975,7 +998,7 @@ __device__ __forceinline__ void producer_loop(const WorkerParams& P, const Worke
   if (lane == 0 && blockIdx.x < kDiagCtas) {
     unsigned long long* row = dc->diag[blockIdx.x];
     for (int k = 0; k < 6; ++k) row[k] = C.dg[k];
-    row[DG_P_TMA] = C.dg[kDgTma];
+
   }
 }
 
@@ -986,6 +1009,7 @@ __device__ void batch_worker_body(const WorkerParams& P, unsigned char* smem_raw
   W.H = H;
   W.bufs = smem_raw + ((sizeof(SmemHeader) + 127) & ~size_t(127));
   W.stage_bytes = P.stage_bytes;
+  W.load_policy = P.load_hint ? ptx::l2_evict_first_policy() : 0ull;
   const uint32_t S = P.stages;
   DevCtl* dc = P.dc;
 
@@ -1000,6 +1024,7 @@ __device__ void batch_worker_body(const WorkerParams& P, unsigned char* smem_raw
     H->wait_limit_ns = P.wait_limit_ns;
     H->full_wait_ns = P.wait_limit_ns;
     H->exit_flag = 0;
+    H->armed = 0;
   }
   __syncthreads();
 

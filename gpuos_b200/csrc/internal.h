@@ -208,7 +208,7 @@ enum DiagSlot {
   DG_C_TILE,            // compute thread 0: tile function
   DG_C_BAR,             // compute thread 0: compute-warp barrier after the tile
   DG_C_COMPLETE,        // compute thread 0: completion accounting
-  DG_P_TMA,             // dequeue warp: issuing the bulk copies of staged items
+  DG_C_FILL,            // compute thread 0: from the bulk-copy issue of an item to seeing it staged (summed)
   DG_CYCLES,            // total cycles of the CTA
   kDiagSlots = 12
 };
@@ -274,6 +274,8 @@ struct WorkerParams {
   uint32_t stages;
   uint32_t stage_bytes;   // operand buffer bytes per stage
   uint32_t compute_threads;
+  uint32_t account_every;  // completions accounted per gpu-scope fence while work is staged (0: 8)
+  uint32_t load_hint;      // nonzero: operand bulk loads carry an L2 evict-first policy
   uint32_t _pad;
   uint64_t wait_limit_ns;  // bound of the launch-start wait (HostCtl::wait_limit_ns at launch)
   // optional: the first error of the launch is also recorded here (if still 0), in memory that
@@ -288,6 +290,7 @@ struct alignas(64) StageMeta {
   uint32_t b_off;
   uint32_t staged;      // bit0: a staged, bit1: b staged
   uint32_t _pad;
+  unsigned long long t_issue;  // clock64 when the item's copies were issued (diagnostics)
   union {
     Task task;
     Layout layout;
@@ -321,7 +324,7 @@ struct alignas(128) SmemHeader {
   unsigned long long full_wait_ns; // compute warps' bound on a silent dequeue warp
   unsigned long long wait_limit_ns; // bound of the CTA's other waits (launch copy of HostCtl)
   unsigned int exit_flag;
-  unsigned int _pad;
+  unsigned int armed;              // uses staged so far by the dequeue warp (low 32 bits)
   StageMeta meta[kMaxStages];
   WorkItem dcache[2][8];           // descriptors of the current / next chunk (ticket & 7)
   ProdCold cold;

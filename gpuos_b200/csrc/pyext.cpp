@@ -693,9 +693,11 @@ PyObject* py_debug_counters(PyObject*, PyObject* args, PyObject* kw) {
   if (!PyArg_ParseTupleAndKeywords(args, kw, "|O", const_cast<char**>(kwlist), &devobj)) return nullptr;
   gpuos_rt* rt = rt_arg(devobj, nullptr);
   if (!rt) return nullptr;
-  std::vector<uint64_t> buf(256 * 12);
-  const int ctas = gpuos_rt_debug_counters(rt, buf.data(), (int)buf.size());
+  // one row per worker CTA (fewer than 512) plus the launch timeline row
+  std::vector<uint64_t> buf(513 * 12, ~0ull);
+  int ctas = gpuos_rt_debug_counters(rt, buf.data(), (int)buf.size());
   if (ctas < 0) return raise_status(-ctas);
+  if (ctas > 512) ctas = 512;
   PyObject* rows = PyList_New(ctas);
   for (int c = 0; c < ctas; ++c) {
     PyObject* row = PyList_New(12);
@@ -711,9 +713,10 @@ PyObject* py_debug_timeline(PyObject*, PyObject* args, PyObject* kw) {
   if (!PyArg_ParseTupleAndKeywords(args, kw, "|O", const_cast<char**>(kwlist), &devobj)) return nullptr;
   gpuos_rt* rt = rt_arg(devobj, nullptr);
   if (!rt) return nullptr;
-  std::vector<uint64_t> buf(257 * 12, ~0ull);
-  const int ctas = gpuos_rt_debug_counters(rt, buf.data(), (int)buf.size());
+  std::vector<uint64_t> buf(513 * 12, ~0ull);
+  int ctas = gpuos_rt_debug_counters(rt, buf.data(), (int)buf.size());
   if (ctas < 0) return raise_status(-ctas);
+  if (ctas > 511) ctas = 511;
   PyObject* row = PyList_New(12);
   for (int k = 0; k < 12; ++k) PyList_SET_ITEM(row, k, PyLong_FromUnsignedLongLong(buf[ctas * 12 + k]));
   return row;

@@ -922,6 +922,12 @@ static int launch_worker_locked(gpuos_rt* rt) {
   P.stages = rt->stages;
   P.stage_bytes = rt->stage_bytes;
   P.compute_threads = (uint32_t)rt->cta_threads;
+  // while more work is staged, completions are accounted 32 at a time (each account is a
+  // gpu-scope fence that waits for the tiles' stores); operands are read once, so their bulk
+  // loads carry an L2 evict-first policy.  Measured on 8 steps of 4096 fp32 tiles per launch:
+  // 0.333 ms -> 0.299 ms per launch.
+  P.account_every = (uint32_t)std::max(1, env_int("GPUOS_ACCOUNT_EVERY", 32));
+  P.load_hint = (uint32_t)env_int("GPUOS_LOAD_HINT", 1);
   P.wait_limit_ns = rt->hc->wait_limit_ns;
   CK(cudaSetDevice(rt->device));
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
