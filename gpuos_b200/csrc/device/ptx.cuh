@@ -193,6 +193,10 @@ __device__ __forceinline__ float4 ld_shared_v4f(uint32_t addr) {
   return v;
 }
 
+__device__ __forceinline__ void st_shared_v4f(uint32_t addr, float4 v) {
+  asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w) : "memory");
+}
+
 __device__ __forceinline__ void st_shared_f(uint32_t addr, float v) {
   asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
@@ -200,6 +204,12 @@ __device__ __forceinline__ void st_shared_f(uint32_t addr, float v) {
 __device__ __forceinline__ float ld_shared_f(uint32_t addr) {
   float v;
   asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t ld_shared_u16(uint32_t addr) {
+  unsigned short v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
   return v;
 }
 

@@ -397,10 +397,199 @@ __device__ __noinline__ void ew_2d(const TileCtx& c) {
 }
 
 
+// ---- EW_2DT: staged transpose blocks ----------------------------------------------------
+// A block is every row (nr) x nc columns of a 2-D layout whose operand a runs along rows with
+// unit stride; w = 2^lg >= nc, w >= 8 and nr * w <= 4096.  The dequeue warp staged a's block in
+// stage half A exactly as it lies in memory: element (r, j) at a_off + (j * sa1 + r) * es.
+// Phase 1 gives each thread one row r and a quad of columns 4jq..4jq+3: four 16- or 32-bit shared
+// loads (consecutive threads take consecutive rows: consecutive addresses) and one 16-byte store
+// of the four floats into the transpose buffer T in stage half B.  T holds row r as cw = w / 4
+// 16-byte chunks, chunk jq at r * cw + (jq ^ f(r)), f(r) = (r >> ksh) & swm with
+// ksh = log2(max(1, 8 / cw)) and swm = min(cw, 8) - 1: the eight chunks a quarter-warp writes (or
+// reads) fall in eight different 16-byte bank groups.  Phase 2 gives each thread a row and a
+// column quad with consecutive threads on consecutive quads: one 16-byte shared load, four
+// results, one 16-byte store when the output allows it (coalesced either way).
+// jq = q / nr in phase 1 uses a multiply by ceil(2^32 / nr), exact for q, nr <= 4096.
+struct T2d {
+  uint32_t nr, nc, lg, cw;  // rows, valid columns, log2 and quads (cw = w / 4) of the width
+  uint32_t ksh, swm;        // swizzle of the chunk index
+};
+
+__device__ __forceinline__ T2d t2d_geom(uint32_t nr, uint32_t nc, uint32_t lg) {
+  T2d g;
+  g.nr = nr;
+  g.nc = nc;
+  g.lg = lg;
+  g.cw = 1u << (lg - 2);
+  g.ksh = lg >= 5 ? 0u : 5u - lg;
+  g.swm = (lg >= 5 ? 8u : g.cw) - 1u;
+  return g;
+}
+
+// Byte offset in T of chunk jq of row r.
+__device__ __forceinline__ uint32_t t2d_chunk(const T2d& g, uint32_t r, uint32_t jq) {
+  return ((r << (g.lg - 2)) + (jq ^ ((r >> g.ksh) & g.swm))) << 4;
+}
+
+// Phase 1 for one storage type; TSRC: 0 float, 1 half, 2 bfloat16.  Columns at or beyond nc
+// are not read (their T entries are never used).
+template <int TSRC>
+__device__ __forceinline__ void t2d_fill(const T2d& g, uint32_t src, uint32_t tbuf, uint32_t sa1, uint32_t tid,
+                                         uint32_t nt) {
+  constexpr uint32_t es = TSRC == 0 ? 4u : 2u;
+  const uint32_t nq = (g.nc + 3u) >> 2;
+  const uint32_t total = g.nr * nq;
+  const uint32_t mg = g.nr > 1 ? (uint32_t)((0x100000000ull + g.nr - 1) / g.nr) : 0u;
+  const uint32_t cstep = sa1 * es;  // bytes from one column to the next
+  for (uint32_t q = tid; q < total; q += nt) {
+    const uint32_t jq = g.nr > 1 ? __umulhi(q, mg) : q;
+    const uint32_t r = q - jq * g.nr;
+    const uint32_t j0 = jq << 2;
+    const uint32_t a = src + (j0 * sa1 + r) * es;
+    float v[4];
+#pragma unroll
+    for (uint32_t t = 0; t < 4; ++t) {
+      const uint32_t at = a + t * cstep;
+      if (j0 + t < g.nc) {
+        if constexpr (TSRC == 0) v[t] = ptx::ld_shared_f(at);
+        else if constexpr (TSRC == 1) v[t] = __half2float(__ushort_as_half((unsigned short)ptx::ld_shared_u16(at)));
+        else v[t] = __uint_as_float(ptx::ld_shared_u16(at) << 16);
+      } else {
+        v[t] = 0.f;
+      }
+    }
+    ptx::st_shared_v4f(tbuf + t2d_chunk(g, r, jq), make_float4(v[0], v[1], v[2], v[3]));
+  }
+}
+
+// Phase 1 when a's block could not be staged (the planner keeps spans within a stage half, so
+// this only guards the layout): read a from global memory.
+__device__ __forceinline__ void t2d_fill_global(const T2d& g, const unsigned char* A, int dta, uint32_t tbuf,
+                                                uint32_t sa1, uint32_t tid, uint32_t nt) {
+  const uint32_t nq = (g.nc + 3u) >> 2;
+  for (uint32_t q = tid; q < g.nr * nq; q += nt) {
+    const uint32_t jq = q / g.nr, r = q - jq * g.nr;
+    float v[4];
+#pragma unroll
+    for (uint32_t t = 0; t < 4; ++t)
+      v[t] = (jq * 4 + t < g.nc) ? ld_elem(A, dta, (int64_t)(jq * 4 + t) * sa1 + r) : 0.f;
+    ptx::st_shared_v4f(tbuf + t2d_chunk(g, r, jq), make_float4(v[0], v[1], v[2], v[3]));
+  }
+}
+
+// Four results of one output quad into row r, columns j0..j0+3 (those below nc).
+template <typename TO>
+__device__ __forceinline__ void t2d_store4(TO* O, int32_t o0s, int32_t o1s, uint32_t r, uint32_t j0, uint32_t nc,
+                                           bool vec, const float* v) {
+  TO* p = O + (int32_t)r * o0s + (int32_t)j0 * o1s;
+  if (vec && j0 + 4 <= nc) {
+    if constexpr (sizeof(TO) == 4) {
+      *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+      const TO h0 = from_f<TO>(v[0]), h1 = from_f<TO>(v[1]), h2 = from_f<TO>(v[2]), h3 = from_f<TO>(v[3]);
+      uint2 u;
+      const unsigned short* b0 = reinterpret_cast<const unsigned short*>(&h0);
+      const unsigned short* b1 = reinterpret_cast<const unsigned short*>(&h1);
+      const unsigned short* b2 = reinterpret_cast<const unsigned short*>(&h2);
+      const unsigned short* b3 = reinterpret_cast<const unsigned short*>(&h3);
+      u.x = (uint32_t)*b0 | ((uint32_t)*b1 << 16);
+      u.y = (uint32_t)*b2 | ((uint32_t)*b3 << 16);
+      *reinterpret_cast<uint2*>(p) = u;
+    }
+    return;
+  }
+#pragma unroll
+  for (uint32_t t = 0; t < 4; ++t)
+    if (j0 + t < nc) p[(int32_t)t * o1s] = from_f<TO>(v[t]);
+}
+
+// Phase 2 for one output type.  bmode: 0 none or scalar (bscal), 1 constant down a column
+// (b[(c0 + j) * b1s]), 2 any stride (b[r * b0s + (c0 + j) * b1s]).  vec: the output's column
+// stride is 1 and every quad starts on a 16-byte (float) or 8-byte (16-bit) boundary.
+template <int OP, typename TO>
+__device__ __forceinline__ void t2d_out(const T2d& g, uint32_t tbuf, TO* O, int32_t o0s, int32_t o1s, bool vec,
+                                        const void* B, int dtb, int bmode, int32_t b0s, int32_t b1s, float bscal,
+                                        float p0, float p1, uint32_t tid, uint32_t nt) {
+  const uint32_t qsh = g.lg - 2, total = g.nr << qsh;
+  // with cw dividing nt every quad of a thread is in the same column quad: a column broadcast
+  // operand is read once per thread
+  const bool fixed = (nt & (g.cw - 1u)) == 0u;
+  uint32_t jqb = 0xffffffffu;
+  float bq[4] = {bscal, bscal, bscal, bscal};
+  for (uint32_t q = tid; q < total; q += nt) {
+    const uint32_t jq = q & (g.cw - 1u), r = q >> qsh, j0 = jq << 2;
+    if (j0 >= g.nc) continue;
+    const float4 a4 = ptx::ld_shared_v4f(tbuf + t2d_chunk(g, r, jq));
+    const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+    if (bmode == 1 && (!fixed || jq != jqb)) {
+#pragma unroll
+      for (uint32_t t = 0; t < 4; ++t) bq[t] = j0 + t < g.nc ? ld_elem(B, dtb, (int64_t)(j0 + t) * b1s) : 0.f;
+      jqb = jq;
+    } else if (bmode == 2) {
+#pragma unroll
+      for (uint32_t t = 0; t < 4; ++t)
+        bq[t] = j0 + t < g.nc ? ld_elem(B, dtb, (int64_t)r * b0s + (int64_t)(j0 + t) * b1s) : 0.f;
+    }
+    float v[4];
+#pragma unroll
+    for (uint32_t t = 0; t < 4; ++t) v[t] = ew_apply<OP>(av[t], bq[t], p0, p1);
+    t2d_store4<TO>(O, o0s, o1s, r, j0, g.nc, vec, v);
+  }
+}
+
+template <int OP>
+__device__ __noinline__ void ew_2dt(const TileCtx& c) {
+  const StageMeta& m = *c.m;
+  const WorkItem& it = m.item;
+  const Layout& L = m.ext.layout;
+  const T2d g = t2d_geom(it.count >> 16, it.count & 0xffffu, (uint32_t)it.x);
+  const uint32_t c0 = (uint32_t)(it.x >> 32);
+  const uint32_t sa1 = (uint32_t)L.sa[1];
+  const int dta = it.dt_a, dtb = it.dt_b, dto = it.dt_o;
+  const uint32_t tbuf = ptx::smem_addr(c.sb);
+  if (m.staged & 1) {
+    const uint32_t src = ptx::smem_addr(c.sa) + m.a_off;
+    if (dta == kF16) t2d_fill<1>(g, src, tbuf, sa1, c.tid, c.nt);
+    else if (dta == kBF16) t2d_fill<2>(g, src, tbuf, sa1, c.tid, c.nt);
+    else t2d_fill<0>(g, src, tbuf, sa1, c.tid, c.nt);
+  } else {
+    const unsigned char* A = reinterpret_cast<const unsigned char*>(it.a) + (int64_t)c0 * sa1 * dtype_size(dta);
+    t2d_fill_global(g, A, dta, tbuf, sa1, c.tid, c.nt);
+  }
+  ptx::named_bar_sync(kBarBlock, c.nt);
+  const uint32_t flags = it.flags;
+  const bool b_imm = (flags & IF_B_SCALAR) != 0;
+  const bool b_mem = (flags & IF_B_PRESENT) && !b_imm;
+  const int32_t b0s = (int32_t)L.sb[0], b1s = (int32_t)L.sb[1];
+  const int bmode = !b_mem ? 0 : (b0s == 0 ? 1 : 2);
+  const float bscal = b_imm ? __uint_as_float((uint32_t)it.b) : 0.f;
+  const void* B = b_mem ? reinterpret_cast<const unsigned char*>(it.b) + (int64_t)c0 * b1s * dtype_size(dtb)
+                        : nullptr;
+  const int32_t o0s = (int32_t)L.so[0], o1s = (int32_t)L.so[1];
+  const int eso = dtype_size(dto);
+  unsigned char* O = reinterpret_cast<unsigned char*>(it.o) + (int64_t)c0 * o1s * eso;
+  // quads start at columns 4k: vector stores need unit column stride, and the block start and the
+  // row stride on a 4-element boundary of 16 (float) or 8 (16-bit) bytes
+  const bool vec = o1s == 1 && (o0s & 3) == 0 && ((reinterpret_cast<uintptr_t>(O) & (uintptr_t)(4 * eso - 1)) == 0);
+  const float p0 = L.params[0], p1 = L.params[1];
+  if (dto == kF16)
+    t2d_out<OP, __half>(g, tbuf, reinterpret_cast<__half*>(O), o0s, o1s, vec, B, dtb, bmode, b0s, b1s, bscal, p0, p1,
+                        c.tid, c.nt);
+  else if (dto == kBF16)
+    t2d_out<OP, __nv_bfloat16>(g, tbuf, reinterpret_cast<__nv_bfloat16*>(O), o0s, o1s, vec, B, dtb, bmode, b0s, b1s,
+                               bscal, p0, p1, c.tid, c.nt);
+  else
+    t2d_out<OP, float>(g, tbuf, reinterpret_cast<float*>(O), o0s, o1s, vec, B, dtb, bmode, b0s, b1s, bscal, p0, p1,
+                       c.tid, c.nt);
+  // the stage is next filled by bulk copies (async proxy) after these generic writes of T
+  ptx::fence_proxy_async_smem();
+}
+
 template <int OP>
 __device__ void ew_tile(const TileCtx& c) {
   const uint8_t kind = c.m->item.kind;
   if (kind == IK_EW_CONTIG) ew_contig<OP>(c);
+  else if (kind == IK_EW_2DT) ew_2dt<OP>(c);
   else if (kind == IK_EW_2D) ew_2d<OP>(c);
   else ew_generic(c);
 }

@@ -74,6 +74,14 @@ __device__ TileFn g_tile_fns[GPUOS_EW_NUM_OPS + 1] = {
     ew_tile<21>, ew_tile<22>, ew_tile<23>, ew_tile<24>, ew_tile<25>, ew_tile<26>, ew_tile<27>,
     ew_tile<28>, ew_tile<29>, reduce_tile};
 
+// Staged transpose blocks reach their tile function directly (one call level, not two through
+// ew_tile: every call level saves registers of all compute threads through local memory).
+__device__ TileFn g_t2d_fns[GPUOS_EW_NUM_OPS] = {
+    ew_2dt<0>,  ew_2dt<1>,  ew_2dt<2>,  ew_2dt<3>,  ew_2dt<4>,  ew_2dt<5>,  ew_2dt<6>,  ew_2dt<7>,
+    ew_2dt<8>,  ew_2dt<9>,  ew_2dt<10>, ew_2dt<11>, ew_2dt<12>, ew_2dt<13>, ew_2dt<14>, ew_2dt<15>,
+    ew_2dt<16>, ew_2dt<17>, ew_2dt<18>, ew_2dt<19>, ew_2dt<20>, ew_2dt<21>, ew_2dt<22>, ew_2dt<23>,
+    ew_2dt<24>, ew_2dt<25>, ew_2dt<26>, ew_2dt<27>, ew_2dt<28>, ew_2dt<29>};
+
 // ---- completion ----------------------------------------------------------------------
 // Completed items of one flush awaiting accounting (the completer warp batches them).
 struct DoneRun {
@@ -203,9 +211,13 @@ __device__ __forceinline__ void compute_loop(const WorkerParams& P, const Worker
         ctx.nt = nct;
         if (kind == IK_ROW_REDUCE) {
           row_reduce_body(ctx);
+        } else if (kind == IK_EW_2DT) {
+          g_t2d_fns[m.item.op](ctx);
         } else {
           const uint32_t fi =
-              (kind == IK_EW_CONTIG || kind == IK_EW_GENERIC || kind == IK_EW_2D) ? m.item.op : GPUOS_EW_NUM_OPS;
+              (kind == IK_EW_CONTIG || kind == IK_EW_GENERIC || kind == IK_EW_2D || kind == IK_EW_2DT)
+                  ? m.item.op
+                  : GPUOS_EW_NUM_OPS;
           TileFn fn = g_tile_fns[fi];
           fn(ctx);
         }
@@ -596,6 +608,28 @@ __device__ __forceinline__ void stage_copies(const WorkerShared& W, StageMeta& m
       m.staged = 0;
       ptx::mbar_arrive(full);
     }
+  } else if (it.kind == IK_EW_2DT) {
+    // every row of the block x its columns: one contiguous span of a (layout already copied)
+    const Layout& L = m.ext.layout;
+    const uint64_t nr = it.count >> 16, nc = it.count & 0xffffu, c0 = it.x >> 32;
+    const uint64_t es = (uint64_t)dtype_size(it.dt_a);
+    const uint64_t start = it.a + c0 * (uint64_t)L.sa[1] * es;
+    const uint64_t span = ((nc - 1) * (uint64_t)L.sa[1] + nr) * es;
+    const uint64_t a0 = start & ~15ull;
+    const uint64_t a1 = (start + span + 15) & ~15ull;
+    if (L.sa[0] == 1 && L.sa[1] > 0 && nc > 0 && a1 - a0 <= (W.stage_bytes >> 1)) {
+      m.a_off = (uint32_t)(start - a0);
+      m.staged = 1;
+      ptx::mbar_arrive_expect_tx(full, (uint32_t)(a1 - a0));
+      if (W.load_policy)
+        ptx::bulk_g2s_hint(ptx::smem_addr(buf), reinterpret_cast<const void*>(a0), (uint32_t)(a1 - a0), full,
+                           W.load_policy);
+      else
+        ptx::bulk_g2s(ptx::smem_addr(buf), reinterpret_cast<const void*>(a0), (uint32_t)(a1 - a0), full);
+    } else {
+      m.staged = 0;
+      ptx::mbar_arrive(full);
+    }
   } else if (it.kind == IK_TOPK) {
     const uint64_t span = (uint64_t)it.count * it.aux * dtype_size(it.dt_a);
     const uint64_t a0 = it.a & ~15ull;
@@ -632,7 +666,7 @@ __device__ __forceinline__ bool stage_item(const WorkerParams& P, const WorkerSh
   const WorkItem it = m.item;
   int ok = 1;
   if (lane == 0) {
-    if (it.kind == IK_NONE || it.kind > IK_TOPK || it.batch >= kNumBatchSlots ||
+    if (it.kind == IK_NONE || it.kind > IK_EW_2DT || it.batch >= kNumBatchSlots ||
         (it.kind != IK_TASK && it.kind != IK_ROW_REDUCE && it.kind != IK_RED_GENERIC && it.op >= GPUOS_EW_NUM_OPS)) {
       report_error(P, DE_BAD_ITEM, st.ticket);
       ok = 0;
@@ -669,7 +703,7 @@ __device__ __forceinline__ bool stage_item(const WorkerParams& P, const WorkerSh
   st.last_seq = __shfl_sync(0xffffffffu, st.last_seq, 0);
   if (!ok) return false;
 
-  if (it.kind == IK_EW_GENERIC || it.kind == IK_EW_2D || it.kind == IK_RED_GENERIC) {
+  if (it.kind == IK_EW_GENERIC || it.kind == IK_EW_2D || it.kind == IK_EW_2DT || it.kind == IK_RED_GENERIC) {
     if (H.lay_valid && H.lay_key == it.aux) {
       warp_copy_smem16(&m.ext.layout, &H.lay_cache, sizeof(Layout), lane);
     } else {
@@ -739,7 +773,10 @@ __device__ __forceinline__ uint32_t stage_group(const WorkerParams& P, const Wor
       ph ^= 1u;
     }
     const bool free = lane == 0 || u < S || ptx::mbar_test_wait(ptx::smem_addr(&H.empty[su]), ph ^ 1u);
-    ok = free && group_kind(it) && it.wait_items <= st.items_done_cache;
+    // staged transpose blocks join the group once their layout record is cached here
+    const bool t2d = it.kind == IK_EW_2DT && it.batch < kNumBatchSlots && it.op < GPUOS_EW_NUM_OPS &&
+                     H.lay_valid && H.lay_key == it.aux;
+    ok = free && (group_kind(it) || t2d) && it.wait_items <= st.items_done_cache;
   } else {
     it.batch_seq = 0;
   }
@@ -754,6 +791,19 @@ __device__ __forceinline__ uint32_t stage_group(const WorkerParams& P, const Wor
     // start stamp of the flush: the first item each CTA stages from it is enough
     if (it.batch_seq != (lane == 0 ? st.last_seq : prev_seq))
       atomicMin(&P.dc->batch_t0[it.batch], (unsigned long long)ptx::now_ns());
+    if (it.kind == IK_EW_2DT) {
+      // the fields of the layout record a staged transpose block reads (not the whole record)
+      Layout& L = m.ext.layout;
+      const Layout& Lc = H.lay_cache;
+      L.sa[0] = Lc.sa[0];
+      L.sa[1] = Lc.sa[1];
+      L.sb[0] = Lc.sb[0];
+      L.sb[1] = Lc.sb[1];
+      L.so[0] = Lc.so[0];
+      L.so[1] = Lc.so[1];
+      L.params[0] = Lc.params[0];
+      L.params[1] = Lc.params[1];
+    }
     stage_copies(W, m, s, it);
   }
   st.last_seq = __shfl_sync(0xffffffffu, it.batch_seq, g - 1);

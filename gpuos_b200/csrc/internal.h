@@ -29,6 +29,9 @@ enum ItemKind : uint8_t {
   IK_TASK = 5,        // reference-layout Task dispatched through g_op_alias/g_op_table
   IK_EW_2D = 6,       // element-wise block of a 2-D strided / broadcast layout (layout record)
   IK_TOPK = 7,        // top-k of each row of a group of contiguous rows (staged like a row group)
+  IK_EW_2DT = 8,      // 2-D block of every row x a column range whose operand a runs along rows:
+                      // a's block is one contiguous span, staged by one bulk copy and transposed
+                      // in shared memory (layout record)
   IK_EXIT = 255       // in-CTA sentinel (never in the ring)
 };
 
@@ -54,6 +57,8 @@ enum ItemFlags : uint8_t {
 //   RED_GENERIC a,o = base addresses; x = first output linear index; count = outputs;
 //               aux = layout index.
 //   TASK        aux = task ring index; op = logical op id (low 8 bits of Task::op).
+//   EW_2DT      a,b,o = base addresses; count = (rows << 16) | columns; x = log2 of the block's
+//               power-of-two column width (low 32 bits) | first column << 32; aux = layout index.
 struct alignas(64) WorkItem {
   uint8_t kind;
   uint8_t op;
@@ -344,6 +349,9 @@ constexpr uint32_t kHalfBytes = 16384;                // one operand tile
 // EW_2D geometry: transpose-mode blocks are 16 rows x 256 columns (a float [16][256] tile
 // per transposed operand fills one stage half); row-mode blocks hold about 8192 elements.
 constexpr int64_t k2dBlockRows = 16, k2dBlockCols = 256, k2dRowTile = 8192;
+// EW_2DT: rows per block at most (every row in one block) and elements per block at most (the
+// float transpose buffer is one stage half)
+constexpr int64_t k2dtMaxRows = 256, k2dtElems = 4096;
 // Top-k on the batched path: k rounds of a warp-wide selection per row, so k is bounded.
 constexpr int kTopkMaxK = 256;
 

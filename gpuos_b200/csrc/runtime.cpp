@@ -419,6 +419,29 @@ int plan_ew(const EwReq& r, uint32_t half_bytes, Plan* p) {
       it.count = (uint32_t)((nr << 16) | nc);
       p->items.push_back(it);
     };
+    // a runs along rows with unit stride and every row fits one block: a block of all rows x a
+    // power-of-two column range is one contiguous span of a (plus the column stride's gaps),
+    // staged by one bulk copy and transposed in shared memory (at most k2dtElems elements, so the
+    // float transpose buffer fills one stage half)
+    if (at && !bt && st[0][0] == 1 && st[0][1] >= R && R <= k2dtMaxRows) {
+      const int64_t esa = dtype_size(r.a->dtype);
+      auto span = [&](int lg) { return (((int64_t(1) << lg) - 1) * st[0][1] + R) * esa; };
+      int lg = 0;
+      while ((int64_t(2) << lg) * R <= k2dtElems) ++lg;
+      while (lg > 3 && span(lg) + 32 > (int64_t)half_bytes) --lg;
+      if (lg >= 3 && span(lg) + 32 <= (int64_t)half_bytes) {  // at least 8 columns per block
+        proto.kind = IK_EW_2DT;
+        proto.flags = base_flags;
+        const int64_t w = int64_t(1) << lg;
+        for (int64_t c0 = 0; c0 < C; c0 += w) {
+          WorkItem it = proto;
+          it.x = (uint64_t)lg | ((uint64_t)c0 << 32);
+          it.count = (uint32_t)((R << 16) | std::min<int64_t>(w, C - c0));
+          p->items.push_back(it);
+        }
+        return GPUOS_OK;
+      }
+    }
     if (at || bt) {
       for (int64_t r0 = 0; r0 < R; r0 += k2dBlockRows)
         for (int64_t c0 = 0; c0 < C; c0 += k2dBlockCols)

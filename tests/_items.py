@@ -22,6 +22,7 @@ LAYOUT_DT = np.dtype([("ndim", "<i4"), ("rdim", "<i4"), ("params", "<f4", 4), ("
 assert LAYOUT_DT.itemsize == 432
 
 IK_EW_CONTIG, IK_EW_GENERIC, IK_ROW_REDUCE, IK_RED_GENERIC, IK_TASK, IK_EW_2D = 1, 2, 3, 4, 5, 6
+IK_EW_2DT = 8
 IF_B_PRESENT, IF_B_SCALAR, IF_A_BCAST, IF_B_BCAST, IF_UNSTAGED, IF_MEAN = 1, 2, 4, 8, 16, 32
 IF_A_T, IF_B_T = 64, 128
 CODE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2, torch.float64: 4, torch.int32: 3}
@@ -165,10 +166,11 @@ def run_items(items, layout, mem: Memory, op_fn):
                     b = None
                 r = op_fn(int(it["op"]), a, b, float(L["params"][0]), float(L["params"][1]))
                 mem.view(int(it["o"]), dto, -1)[oo] = r.to(TDT[dto])
-        elif kind == IK_EW_2D:
-            # block rows [r0, r0 + nr) x columns [c0, c0 + nc) of the 2-D layout
+        elif kind in (IK_EW_2D, IK_EW_2DT):
+            # block rows [r0, r0 + nr) x columns [c0, c0 + nc) of the 2-D layout (EW_2DT: every
+            # row, the low 32 bits of x hold the log2 of the block's column width)
             L = layout
-            r0, c0 = int(it["x"]) & 0xFFFFFFFF, int(it["x"]) >> 32
+            r0, c0 = (0 if kind == IK_EW_2DT else int(it["x"]) & 0xFFFFFFFF), int(it["x"]) >> 32
             nr, nc = int(it["count"]) >> 16, int(it["count"]) & 0xFFFF
             rr = (torch.arange(nr, dtype=torch.int64) + r0).unsqueeze(1)
             cc = (torch.arange(nc, dtype=torch.int64) + c0).unsqueeze(0)

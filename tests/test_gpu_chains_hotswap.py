@@ -80,6 +80,7 @@ def test_config5_full_size_one_gpu(rt):
     through op 0 must show its phase's operator (misdispatched)."""
     r = bench.c5_run(rt, 0, 1, lambda: None)
     assert r["requests"] == 2048 * 32
-    assert r["lost"] == 0 and r["wrong"] == 0 and r["misdispatched"] == 0, r
+    summary = {k: r[k] for k in ("lost", "wrong", "misdispatched", "wrong_by_op", "wrong_examples")}
+    assert r["lost"] == 0 and r["wrong"] == 0 and r["misdispatched"] == 0, summary
     assert all(p > 0 for p in r["probes_per_phase"]), r["probes_per_phase"]
     assert rt.get_slot(0) == rt.builtin_op_address(0) and rt.get_alias(0) == 0

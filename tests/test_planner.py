@@ -5,7 +5,7 @@ import pytest
 import torch
 
 from oracle.reference_semantics import EW, ew_torch, reduce_torch, same_bits
-from tests._items import (IF_A_BCAST, IF_A_T, IF_B_BCAST, IF_B_SCALAR, IF_B_T, IF_UNSTAGED, IK_EW_2D,
+from tests._items import (IF_A_BCAST, IF_A_T, IF_B_BCAST, IF_B_SCALAR, IF_B_T, IF_UNSTAGED, IK_EW_2D, IK_EW_2DT,
                           IK_EW_CONTIG, IK_EW_GENERIC, IK_RED_GENERIC, IK_ROW_REDUCE, Memory, plan_ew,
                           plan_reduce, run_items)
 
@@ -55,16 +55,32 @@ def test_misaligned_operand_tiles_fit_a_stage_half(dt, shift):
     assert int(items[0]["count"]) == (16384 - 32) // es
 
 
-def test_transposed_fp16_with_broadcast_bf16_is_2d_transpose_blocks():
-    # C3: a = transpose of [512,64] fp16 viewed [64,512]; b = [512] bf16; out fp32
+def test_transposed_fp16_with_broadcast_bf16_is_staged_transpose_blocks():
+    # C3: a = transpose of [512,64] fp16 viewed [64,512]; b = [512] bf16; out fp32.  A block of
+    # all 64 rows x 64 columns of a is one contiguous 8 KiB span (staged by one bulk copy).
     a = torch.randn(512, 64).half().t()
     b = torch.randn(512).bfloat16()
     items = check_ew(EW["ADD"], a, b, torch.float32)
-    assert all(it["kind"] == IK_EW_2D and it["flags"] & IF_A_T and not it["flags"] & IF_B_T for it in items)
-    assert len(items) == 4 * 2  # 64 rows x 512 columns in 16 x 256 blocks
-    assert all((int(it["count"]) >> 16) <= 16 and (int(it["count"]) & 0xFFFF) <= 256 for it in items)
+    assert all(it["kind"] == IK_EW_2DT for it in items)
+    assert len(items) == 512 // 64
+    assert all((int(it["count"]) >> 16) == 64 and (int(it["count"]) & 0xFFFF) == 64 for it in items)
+    assert all(int(it["x"]) & 0xFFFFFFFF == 6 for it in items)      # log2 of the column width
     check_ew(EW["MAXIMUM"], a, b, torch.float32)
     check_ew(EW["RELU"], a, None, torch.float32)   # unary through the same blocks
+
+
+@pytest.mark.parametrize("R,C,dt", [(2, 5000, torch.float16), (17, 333, torch.bfloat16), (256, 40, torch.float16),
+                                    (100, 77, torch.float32), (128, 1000, torch.float32), (3, 9, torch.float32)])
+def test_staged_transpose_blocks_fit_a_stage_half(R, C, dt):
+    a = torch.randn(C, R).to(dt).t()
+    items = check_ew(EW["MUL"], a, torch.randn(C).bfloat16(), torch.float32)
+    es = a.element_size()
+    for it in items:
+        assert it["kind"] == IK_EW_2DT
+        nr, nc, w = int(it["count"]) >> 16, int(it["count"]) & 0xFFFF, 1 << (int(it["x"]) & 0xFFFFFFFF)
+        assert nr == R and 1 <= nc <= w and nr * w <= 4096 and w >= 8
+        assert ((w - 1) * R + R) * es + 32 <= 16384
+    check_ew(EW["SUB"], a, torch.randn(R, C), torch.float16)    # b read element by element
 
 
 @pytest.mark.parametrize("R,C", [(1, 300), (15, 17), (16, 256), (17, 257), (40, 1000), (300, 9)])
