@@ -20,7 +20,9 @@ Printed JSON line (rank 0):
             launch is reported beside it
   baselines GPU per-op torch eager (same stream of requests as individual launches) and
             the CPU path (PyTorch CPU eager over the same requests on the host cores)
-  latency   p50/p99 submit->done of single 4096-element requests (sync flush each)
+  latency   p50/p99 submit->done of single 4096-element requests: back to back (sync flush
+            each), and open loop at 25/50/80% of that rate (asynchronous flushes, polled)
+  copy ceiling  the e2e step's H2D and D2H copies alone (what e2e can reach over PCIe)
 
 --impl reference runs the reference's CPU path (PyTorch CPU eager over the identical
 request stream, all host threads) and prints the same metric.
@@ -231,6 +233,27 @@ def cpu_threads():
         return os.cpu_count() or 1
 
 
+def bind_to_gpu_cores(index: int):
+    """Restrict this process to the CPU cores NVML reports as local to GPU `index`; returns the
+    previous CPU set (None when NVML or the mapping is unavailable)."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        phys = int(vis.split(",")[index]) if vis else index
+        h = pynvml.nvmlDeviceGetHandleByIndex(phys)
+        words = ((os.cpu_count() or 64) + 63) // 64
+        masks = pynvml.nvmlDeviceGetCpuAffinity(h, words)
+        before = os.sched_getaffinity(0)
+        cpus = {64 * i + bit for i, m in enumerate(masks) for bit in range(64) if (m >> bit) & 1} & before
+        if cpus and cpus != before:
+            os.sched_setaffinity(0, cpus)
+            return before
+    except Exception:
+        pass
+    return None
+
+
 def time_cpu_path(cpu: CpuPath, warm_passes: int, min_passes: int, seconds: float, warm_seconds: float = 3.0):
     """Steady-state rate of the CPU path: warm-up until both `warm_passes` passes and
     `warm_seconds` have gone by (process pool, page faults, clocks), then time passes until both
@@ -278,6 +301,40 @@ def run_reference(args, rank, world):
 
 
 # ---- secondary workloads (one GPU): the request streams of the other configurations ----------
+def open_loop_latency(g, x, y, z, capacity_per_s: float, samples: int, fracs=(0.25, 0.5, 0.8)):
+    """p50/p99 submit->done of single 4096-element requests arriving on a fixed schedule at a
+    stated fraction of the back-to-back request rate (an open loop: an arrival does not wait
+    for earlier requests).  Each request is one submit_add plus an asynchronous flush; its
+    completion is seen by polling the highest completed flush ticket between arrivals, so a
+    latency includes up to one polling pass (about a microsecond)."""
+    out = {}
+    for frac in fracs:
+        period = 1e9 / (capacity_per_s * frac)
+        pending, lat = [], []
+        n = 0
+        t0 = time.perf_counter_ns()
+        nxt = t0
+        while len(lat) < samples:
+            now = time.perf_counter_ns()
+            if n < samples and now >= nxt:
+                g.submit_add(x, y, z)
+                pending.append((g.flush(), now))
+                n += 1
+                nxt += period
+            if pending:
+                done = g.completed()
+                now = time.perf_counter_ns()
+                while pending and pending[0][0] <= done:
+                    lat.append((now - pending[0][1]) / 1e3)
+                    pending.pop(0)
+        lat.sort()
+        out[f"{int(frac * 100)}%"] = {"offered_req_per_s": round(capacity_per_s * frac),
+                                      "p50": lat[len(lat) // 2], "p99": lat[int(len(lat) * 0.99)]}
+    out["what"] = ("open loop: single 4096-element fp32 add requests on a fixed schedule at the stated fraction "
+                   "of the back-to-back rate, submit_add + asynchronous flush each, completion polled")
+    return out
+
+
 def ulp_distance(got: torch.Tensor, ref: torch.Tensor) -> torch.Tensor:
     """|ulp distance| between two float32 tensors (same sign ordering as the integers)."""
     def key(t):
@@ -828,11 +885,15 @@ def main():
         return
 
     dist = None
+    host_cpus = None
     if world > 1:
         import torch.distributed as dist
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
+        # each rank's submit loop on the cores of its GPU's NUMA node (pinned buffers and the
+        # mapped queue words local to the link the GPU reads them over)
+        host_cpus = bind_to_gpu_cores(local)
     else:
         torch.cuda.set_device(0)
     dev = torch.cuda.current_device()
@@ -1060,6 +1121,33 @@ def main():
                        "how": f"{nchunk} chunks per step; H2D, worker and D2H overlap across chunks; two device "
                               "buffer sets alternate so the next step's H2D queues behind this one's"}
 
+        # ---- the e2e step's copies alone (no requests, no worker): the same pinned H2D of a and
+        # b and D2H of out, both directions on their own streams -- the ceiling e2e can reach on
+        # this host's PCIe links ----
+        torch.cuda.synchronize()
+        barrier()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(cur)
+        cs.wait_stream(cur)
+        ds.wait_stream(cur)
+        for step in range(args.steps):
+            k = step % 2
+            with torch.cuda.stream(cs):
+                sets[k][0].copy_(hA, non_blocking=True)
+                sets[k][1].copy_(hB, non_blocking=True)
+            with torch.cuda.stream(ds):
+                hO.copy_(sets[1 - k][2], non_blocking=True)
+        cur.wait_stream(cs)
+        cur.wait_stream(ds)
+        c1.record(cur)
+        c1.synchronize()
+        copy_ms = max_over_ranks(c0.elapsed_time(c1))
+        line["e2e"]["copy_only_ceiling"] = {
+            "value": job_rate(R * args.steps, world, copy_ms), "unit": UNIT,
+            "e2e_over_ceiling": line["e2e"]["value"] / job_rate(R * args.steps, world, copy_ms),
+            "what": "the e2e step's H2D (a, b) and D2H (out) copies alone, H2D and D2H on separate streams, "
+                    "max over ranks"}
+
         # ---- latency: single 4096-element requests, sync flush each ----
         g.set_idle_quiesce_ms(200)
         lat = []
@@ -1074,6 +1162,8 @@ def main():
         lat.sort()
         line["latency_us"] = {"p50": lat[len(lat) // 2], "p99": lat[int(len(lat) * 0.99)],
                               "load": "one 4096-element request per sync flush, back to back"}
+        line["latency_us"]["at_load"] = open_loop_latency(g, x1, y1, z1, 1e6 / lat[len(lat) // 2],
+                                                          args.latency_samples)
 
         # ---- the same step through the bulk submitter (one submit_many call per step) ----
         g.set_idle_quiesce_ms(200 if args.worker_mode == "persistent" else 0)
@@ -1114,15 +1204,20 @@ def main():
                                       "what": "same requests as individual torch.add/mul(out=) launches"}
         line["speedup_vs_gpu_eager"] = value / (eager * world)
 
-        # ---- CPU path (rank 0, single GPU run only) ----
-        if rank == 0 and world == 1:
+        # ---- CPU path (rank 0; with several GPUs a shorter window, the other ranks waiting at
+        # the closing barrier) ----
+        if rank == 0:
+            if host_cpus:
+                os.sched_setaffinity(0, host_cpus)  # the CPU path gets every host core again
             threads = cpu_threads()
             cpu = CpuPath(A.clone(), B.clone(), torch.empty_like(A), ops_l, threads)
-            steps, dt = time_cpu_path(cpu, args.warmup, args.steps, args.cpu_seconds)
+            secs = args.cpu_seconds if world == 1 else min(args.cpu_seconds, 4.0)
+            steps, dt = time_cpu_path(cpu, args.warmup, args.steps, secs)
             cpu.close()
             line["cpu_baseline"] = {"value": R * steps / dt, "unit": UNIT, "cores": threads, "kind": "port",
                                     "sample": f"{steps} passes x {R} requests in {dt:.1f} s after >= 3 s of "
-                                              f"warm-up (PyTorch CPU eager)"}
+                                              f"warm-up (PyTorch CPU eager), rank 0"
+                                              + ("" if world == 1 else f" while the other {world - 1} ranks wait")}
     g.shutdown()
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -85,7 +85,8 @@ def _worker_rdc(force: bool, verbose: bool) -> str:
 def _jit_obj(force: bool, verbose: bool) -> str:
     src = os.path.join(CSRC, "jit.cpp")
     out = os.path.join(BUILD, "jit.o")
-    if force or _newer(out, [src, os.path.join(CSRC, "jit.h"), os.path.join(INCLUDE, "gpuos_b200.h")]):
+    if force or _newer(out, [src, os.path.join(CSRC, "jit.h"), os.path.join(INCLUDE, "gpuos_b200.h"),
+                             os.path.join(CSRC, "device", "ew_math.inc")]):
         _run(["g++", "-O2", "-std=c++17", "-fPIC", "-Wall", "-Wno-deprecated-declarations", "-I" + INCLUDE,
               "-I" + CSRC, "-I" + os.path.join(CUDA_HOME, "include"), "-c", src, "-o", out], verbose)
     return out

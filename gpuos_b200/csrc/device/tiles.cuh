@@ -222,6 +222,15 @@ __device__ __forceinline__ bool f32_staged_tile(const StageMeta& m, const unsign
     GPUOS_F32_CASE(GPUOS_EW_CLAMP_MIN)
     GPUOS_F32_CASE(GPUOS_EW_CLAMP_MAX)
     GPUOS_F32_CASE(GPUOS_EW_LEAKY_RELU)
+    GPUOS_F32_CASE(GPUOS_EW_SQRT)
+    GPUOS_F32_CASE(GPUOS_EW_HARDSIGMOID)
+    GPUOS_F32_CASE(GPUOS_EW_HARDSWISH)
+    GPUOS_F32_CASE(GPUOS_EW_EXP)
+    GPUOS_F32_CASE(GPUOS_EW_LOG)
+    GPUOS_F32_CASE(GPUOS_EW_TANH)
+    GPUOS_F32_CASE(GPUOS_EW_ELU)
+    GPUOS_F32_CASE(GPUOS_EW_SOFTPLUS)
+    GPUOS_F32_CASE(GPUOS_EW_GELU)
 #undef GPUOS_F32_CASE
     default:
       return false;
@@ -508,14 +517,15 @@ __device__ __forceinline__ void t2d_store4(TO* O, int32_t o0s, int32_t o1s, uint
 // stride is 1 and every quad starts on a 16-byte (float) or 8-byte (16-bit) boundary.
 template <int OP, typename TO>
 __device__ __forceinline__ void t2d_out(const T2d& g, uint32_t tbuf, TO* O, int32_t o0s, int32_t o1s, bool vec,
-                                        const void* B, int dtb, int bmode, int32_t b0s, int32_t b1s, float bscal,
-                                        float p0, float p1, uint32_t tid, uint32_t nt) {
+                                        const void* B, int dtb, int bmode, int32_t b0s, int32_t b1s,
+                                        const float* bpre, bool have_b, float p0, float p1, uint32_t tid,
+                                        uint32_t nt) {
   const uint32_t qsh = g.lg - 2, total = g.nr << qsh;
   // with cw dividing nt every quad of a thread is in the same column quad: a column broadcast
-  // operand is read once per thread
+  // operand is read once per thread (before phase 1, `bpre`, when `have_b`)
   const bool fixed = (nt & (g.cw - 1u)) == 0u;
-  uint32_t jqb = 0xffffffffu;
-  float bq[4] = {bscal, bscal, bscal, bscal};
+  uint32_t jqb = have_b ? (tid & (g.cw - 1u)) : 0xffffffffu;
+  float bq[4] = {bpre[0], bpre[1], bpre[2], bpre[3]};
   for (uint32_t q = tid; q < total; q += nt) {
     const uint32_t jq = q & (g.cw - 1u), r = q >> qsh, j0 = jq << 2;
     if (j0 >= g.nc) continue;
@@ -547,6 +557,32 @@ __device__ __noinline__ void ew_2dt(const TileCtx& c) {
   const uint32_t sa1 = (uint32_t)L.sa[1];
   const int dta = it.dt_a, dtb = it.dt_b, dto = it.dt_o;
   const uint32_t tbuf = ptx::smem_addr(c.sb);
+  const uint32_t flags = it.flags;
+  const bool b_imm = (flags & IF_B_SCALAR) != 0;
+  const bool b_mem = (flags & IF_B_PRESENT) && !b_imm;
+  const int32_t b0s = (int32_t)L.sb[0], b1s = (int32_t)L.sb[1];
+  const int bmode = !b_mem ? 0 : (b0s == 0 ? 1 : 2);
+  const float bscal = b_imm ? __uint_as_float((uint32_t)it.b) : 0.f;
+  const void* B = b_mem ? reinterpret_cast<const unsigned char*>(it.b) + (int64_t)c0 * b1s * dtype_size(dtb)
+                        : nullptr;
+  // a broadcast row operand: each thread's four columns are fixed (cw divides nt), so their
+  // loads are issued now and land while phase 1 runs
+  // (raw bits: converting here would wait for the loads before phase 1)
+  uint32_t braw[4] = {0u, 0u, 0u, 0u};
+  bool have_b = false;
+  if (bmode == 1 && (c.nt & (g.cw - 1u)) == 0u) {
+    const uint32_t j0 = (c.tid & (g.cw - 1u)) << 2;
+    if (dtb == kF32) {
+#pragma unroll
+      for (uint32_t t = 0; t < 4; ++t)
+        if (j0 + t < g.nc) braw[t] = reinterpret_cast<const uint32_t*>(B)[(int64_t)(j0 + t) * b1s];
+    } else {
+#pragma unroll
+      for (uint32_t t = 0; t < 4; ++t)
+        if (j0 + t < g.nc) braw[t] = reinterpret_cast<const unsigned short*>(B)[(int64_t)(j0 + t) * b1s];
+    }
+    have_b = true;
+  }
   if (m.staged & 1) {
     const uint32_t src = ptx::smem_addr(c.sa) + m.a_off;
     if (dta == kF16) t2d_fill<1>(g, src, tbuf, sa1, c.tid, c.nt);
@@ -557,14 +593,6 @@ __device__ __noinline__ void ew_2dt(const TileCtx& c) {
     t2d_fill_global(g, A, dta, tbuf, sa1, c.tid, c.nt);
   }
   ptx::named_bar_sync(kBarBlock, c.nt);
-  const uint32_t flags = it.flags;
-  const bool b_imm = (flags & IF_B_SCALAR) != 0;
-  const bool b_mem = (flags & IF_B_PRESENT) && !b_imm;
-  const int32_t b0s = (int32_t)L.sb[0], b1s = (int32_t)L.sb[1];
-  const int bmode = !b_mem ? 0 : (b0s == 0 ? 1 : 2);
-  const float bscal = b_imm ? __uint_as_float((uint32_t)it.b) : 0.f;
-  const void* B = b_mem ? reinterpret_cast<const unsigned char*>(it.b) + (int64_t)c0 * b1s * dtype_size(dtb)
-                        : nullptr;
   const int32_t o0s = (int32_t)L.so[0], o1s = (int32_t)L.so[1];
   const int eso = dtype_size(dto);
   unsigned char* O = reinterpret_cast<unsigned char*>(it.o) + (int64_t)c0 * o1s * eso;
@@ -572,15 +600,23 @@ __device__ __noinline__ void ew_2dt(const TileCtx& c) {
   // row stride on a 4-element boundary of 16 (float) or 8 (16-bit) bytes
   const bool vec = o1s == 1 && (o0s & 3) == 0 && ((reinterpret_cast<uintptr_t>(O) & (uintptr_t)(4 * eso - 1)) == 0);
   const float p0 = L.params[0], p1 = L.params[1];
+  float bpre[4] = {bscal, bscal, bscal, bscal};
+  if (have_b) {
+#pragma unroll
+    for (uint32_t t = 0; t < 4; ++t)
+      bpre[t] = dtb == kF32 ? __uint_as_float(braw[t])
+                : dtb == kBF16 ? __uint_as_float(braw[t] << 16)
+                               : __half2float(__ushort_as_half((unsigned short)braw[t]));
+  }
   if (dto == kF16)
-    t2d_out<OP, __half>(g, tbuf, reinterpret_cast<__half*>(O), o0s, o1s, vec, B, dtb, bmode, b0s, b1s, bscal, p0, p1,
-                        c.tid, c.nt);
+    t2d_out<OP, __half>(g, tbuf, reinterpret_cast<__half*>(O), o0s, o1s, vec, B, dtb, bmode, b0s, b1s, bpre, have_b, p0,
+                        p1, c.tid, c.nt);
   else if (dto == kBF16)
     t2d_out<OP, __nv_bfloat16>(g, tbuf, reinterpret_cast<__nv_bfloat16*>(O), o0s, o1s, vec, B, dtb, bmode, b0s, b1s,
-                               bscal, p0, p1, c.tid, c.nt);
+                               bpre, have_b, p0, p1, c.tid, c.nt);
   else
-    t2d_out<OP, float>(g, tbuf, reinterpret_cast<float*>(O), o0s, o1s, vec, B, dtb, bmode, b0s, b1s, bscal, p0, p1,
-                       c.tid, c.nt);
+    t2d_out<OP, float>(g, tbuf, reinterpret_cast<float*>(O), o0s, o1s, vec, B, dtb, bmode, b0s, b1s, bpre, have_b,
+                       p0, p1, c.tid, c.nt);
   // the stage is next filled by bulk copies (async proxy) after these generic writes of T
   ptx::fence_proxy_async_smem();
 }

@@ -232,6 +232,31 @@ bool ident_ok(const std::string& s) {
 // access of the reference's operators (persistent_kernel.cu:20-31, 60-78): offsets from
 // per-dimension sizes and strides (broadcast dims carry stride 0), f32/f16/bf16 storage, math
 // in float, round-to-nearest-even stores.
+// The built-in operators' math (the same text the worker is compiled from), so that an operator
+// compiled here can call gpuos::ew_apply<GPUOS_EW_...>(a, b, p0, p1) and round exactly as the
+// built-in operator does (fused chains).  It goes ahead of the prelude's macros, which would
+// otherwise turn its float math functions into double-precision ones.
+#define GPUOS_EW_MATH(...) #__VA_ARGS__
+const char* const kEwMath =
+#include "device/ew_math.inc"
+    ;
+#undef GPUOS_EW_MATH
+
+std::string ew_math_source() {
+  std::string s;
+#define GX_CODE(n) s += "constexpr int GPUOS_EW_" #n " = " + std::to_string((int)GPUOS_EW_##n) + ";\n";
+  GX_CODE(ADD) GX_CODE(MUL) GX_CODE(SUB) GX_CODE(DIV) GX_CODE(MAXIMUM) GX_CODE(MINIMUM) GX_CODE(POW)
+  GX_CODE(COPY) GX_CODE(RELU) GX_CODE(SIGMOID) GX_CODE(TANH) GX_CODE(EXP) GX_CODE(LOG) GX_CODE(SQRT)
+  GX_CODE(ABS) GX_CODE(HARDSIGMOID) GX_CODE(HARDSWISH) GX_CODE(GELU) GX_CODE(GELU_TANH) GX_CODE(SIN)
+  GX_CODE(COS) GX_CODE(LEAKY_RELU) GX_CODE(CLAMP) GX_CODE(CLAMP_MIN) GX_CODE(CLAMP_MAX) GX_CODE(ELU)
+  GX_CODE(SOFTPLUS) GX_CODE(NEG) GX_CODE(ADD_ALPHA) GX_CODE(SUB_ALPHA)
+#undef GX_CODE
+  s += "namespace gpuos {\n";
+  s += kEwMath;
+  s += "\n}  // namespace gpuos\n";
+  return s;
+}
+
 const char* kPrelude = R"PRELUDE(
 typedef long long gx_i64;
 struct TensorRef { void* data; int dtype; int ndim; gx_i64 sizes[8]; gx_i64 strides[8]; };
@@ -342,7 +367,8 @@ int ew_source(int id, const std::string& expr, int arity, std::string* src, std:
     return GPUOS_ERR_INVALID;
   }
   const std::string n = std::to_string(id);
-  std::string s = kPrelude;
+  std::string s = ew_math_source();
+  s += kPrelude;
   s += "extern \"C\" __device__ void gpuos_jit_op_" + n + "(const Task& t) {\n";
   s += "  const gx_i64 N = t.numel;\n";
   s += "  for (gx_i64 i = threadIdx.x; i < N; i += blockDim.x) {\n";

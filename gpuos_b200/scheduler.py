@@ -8,7 +8,13 @@ threads_per_block=256, size_threshold=1 << 16, auto_flush_ms=2.0)``, ``GPUOSSche
 * Every in-scope op runs on the GPU through a built-in operator of the runtime; nothing
   needs an NVRTC compile, so the reference's ``GPUOS_SCHEDULER_DISABLE_JIT`` switch
   (scheduler.py:19, default on, which sent everything except add/sub/mul/div back to
-  eager) no longer gates which ops are scheduled.
+  eager) no longer gates which ops are scheduled.  With ``GPUOS_SCHEDULER_DISABLE_JIT=0`` it
+  turns on fusion, as in the reference (scheduler.py:145-160, 376-396): a chain of fp32
+  element-wise ops, each taking the previous one's result, is compiled into one NVRTC operator
+  (the built-in operators' own math, so the chain rounds as the unfused ops do) and written
+  into the tensor returned for the chain's last op; results of the chain that are still
+  referenced when it is submitted are written too (the reference wrote into a fresh tensor and
+  lost them).
 * Results are written into the tensor returned to the caller (the reference's fused path
   wrote into a fresh tensor and lost them, scheduler.py:380).
 * Dependencies: the runtime orders scheduled requests that read or write the same memory
@@ -25,10 +31,14 @@ threads_per_block=256, size_threshold=1 << 16, auto_flush_ms=2.0)``, ``GPUOSSche
 """
 from __future__ import annotations
 
+import collections
 import contextlib
+import math
 import os
+import struct
 import threading
 import time
+import weakref
 from typing import Any, Optional, Set
 
 import torch
@@ -62,6 +72,33 @@ def _storage_key(t: torch.Tensor) -> int:
     return t.data_ptr() - t.storage_offset() * t.element_size()
 
 
+def _f32_literal(v) -> Optional[str]:
+    """Exact C++ literal of a Python number rounded to float32 (None for inf / nan)."""
+    f = struct.unpack("f", struct.pack("f", float(v)))[0]
+    if not math.isfinite(f):
+        return None
+    return float(f).hex() + "f"
+
+
+class _Chain:
+    """A deferred chain of fp32 element-wise ops: the root reads A (and B), every later op the
+    previous result.  `steps` holds (expression of the value after the step, built-in op of a
+    one-op chain, weak reference to the step's result tensor)."""
+
+    def __init__(self, a, b, expr: str, single, out):
+        self.a, self.b = a, b
+        self.arity = 2 if b is not None else 1
+        self.out = out
+        self.steps = [(expr, single, weakref.ref(out))]
+
+    def extend(self, code: int, b_lit: str, p0: str, p1: str, out) -> None:
+        prev = self.steps[-1][0]
+        self.steps.append((f"gpuos::ew_apply<{code}>({prev}, {b_lit}, {p0}, {p1})", None, weakref.ref(out)))
+        self.out = out
+
+
+_MAX_CHAIN = 16
+
 # op overload -> (route, name): 1 binary, 2 unary, 3 parametric unary, 4 reduction, 5 top-k,
 # 0 not ours
 _ROUTES: dict = {}
@@ -83,9 +120,17 @@ class _GPUOSSchedulerMode(TorchDispatchMode):
         self.size_threshold = size_threshold
         self.auto_flush_ms = auto_flush_ms
         self.pending = pending  # storages read or written by requests not yet known complete
-        self.fused = {}  # kept for API compatibility (expression fusion is not used)
+        self.fused = {}  # kept for API compatibility (the chain being fused is self.chain)
         self.scheduled = 0
         self.fallbacks = 0
+        # per aten op name: requests submitted to the runtime / ops left to PyTorch
+        self.scheduled_ops: collections.Counter = collections.Counter()
+        self.fallback_ops: collections.Counter = collections.Counter()
+        # fusion (GPUOS_SCHEDULER_DISABLE_JIT=0): the chain being built, not yet submitted
+        self.fuse = os.environ.get("GPUOS_SCHEDULER_DISABLE_JIT", "1") in ("0", "false", "False")
+        self.chain: Optional[_Chain] = None
+        self.fused_chains = 0
+        self.fused_ops = 0
         self._stop = False
         self._bg: Optional[threading.Thread] = None
         if auto_flush_ms and auto_flush_ms > 0:
@@ -123,6 +168,7 @@ class _GPUOSSchedulerMode(TorchDispatchMode):
         return walk(args) or walk(kwargs)
 
     def _sync_flush(self):
+        self.flush_fused()
         gpuos_ext.flush(sync=True)
         self.pending.clear()
 
@@ -176,6 +222,7 @@ class _GPUOSSchedulerMode(TorchDispatchMode):
             dtype = a.dtype  # a floating tensor keeps its dtype against a Python number
         if dtype not in _FLOATS:
             return None
+        ours = out is None
         if out is None:
             if shape == a.shape and dtype == a.dtype and a.is_contiguous():
                 out = torch.empty_like(a)  # the same contiguous tensor, allocated faster
@@ -183,6 +230,16 @@ class _GPUOSSchedulerMode(TorchDispatchMode):
                 out = torch.empty(shape, dtype=dtype, device=a.device)
         elif not (isinstance(out, torch.Tensor) and out.is_cuda and out.dtype in _FLOATS):
             return None
+        if (self.fuse and ours and dtype == torch.float32 and a.dtype == torch.float32 and p0 == 0.0
+                and (b.dtype == torch.float32 and b.shape == a.shape if b_t else name != "aten::pow.Tensor_Scalar")):
+            lit = "B" if b_t else _f32_literal(b)
+            if lit is not None:
+                # the root of a chain: submitted when the chain ends
+                self.chain = _Chain(a, b if b_t else None, f"gpuos::ew_apply<{op}>(A, {lit}, 0.f, 0.f)",
+                                    (op, b if b_t else float(b), 0.0, 0.0), out)
+                self._mark(a, b if b_t else None, out)
+                self.scheduled += 1
+                return out
         gpuos_ext.submit_elementwise(op, a, b if b_t else float(b), out, p0, 0.0)
         self._mark(a, b if b_t else None, out)
         self.scheduled += 1
@@ -190,13 +247,95 @@ class _GPUOSSchedulerMode(TorchDispatchMode):
 
     def _schedule_unary(self, op, x, p0=0.0, p1=0.0):
         out = torch.empty_like(x, memory_format=torch.contiguous_format)
+        if self.fuse and x.dtype == torch.float32:
+            l0, l1 = _f32_literal(p0), _f32_literal(p1)
+            if l0 is not None and l1 is not None:
+                self.chain = _Chain(x, None, f"gpuos::ew_apply<{op}>(A, 0.f, {l0}, {l1})", (op, None, p0, p1), out)
+                self._mark(x, out)
+                self.scheduled += 1
+                return out
         gpuos_ext.submit_elementwise(op, x, None, out, p0, p1)
         self._mark(x, out)
         self.scheduled += 1
         return out
 
+    # -- fusion ---------------------------------------------------------------------------
+    def _unary_code(self, kind, name, args, kwargs):
+        """(op code, p0, p1) of a unary or parametric op on args[0], or None."""
+        if kind == 2:
+            return _UNARY[name], 0.0, 0.0
+        return self._parametric_code(name, args, kwargs)
+
+    def _try_extend(self, kind, name, args, kwargs):
+        """Append this op to the chain when it is an fp32 element-wise op of the chain's last
+        result (the very tensor returned for it) and nothing else; returns its result or None."""
+        c = self.chain
+        if (not args or args[0] is not c.out or len(c.steps) >= _MAX_CHAIN or torch.is_grad_enabled()
+                or kwargs.get("out") is not None):
+            return None
+        if kind in (2, 3):
+            rc = self._unary_code(kind, name, args, kwargs)
+            if rc is None:
+                return None
+            op, p0, p1 = rc
+            lits = ("0.f", _f32_literal(p0), _f32_literal(p1))
+        elif kind == 1 and len(args) >= 2 and name != "aten::pow.Tensor_Scalar":
+            b = args[1]
+            if isinstance(b, torch.Tensor):
+                if b.dim() != 0 or b.is_cuda:
+                    return None
+                b = b.item()
+            alpha = kwargs.get("alpha")
+            if not self._ok_scalar(b) or (alpha is not None and alpha != 1):
+                return None
+            op = _BINARY[name]
+            lits = (_f32_literal(b), "0.f", "0.f")
+        else:
+            return None
+        if any(v is None for v in lits):
+            return None
+        out = torch.empty_like(c.out)
+        c.extend(op, *lits, out)
+        self._mark(out)
+        self.scheduled += 1
+        return out
+
+    def _submit_steps(self, c: _Chain, k: int, out) -> None:
+        """Submit the value after step k of chain c into `out`."""
+        expr, single, _ = c.steps[k]
+        if k == 0:
+            op, b, p0, p1 = single
+            gpuos_ext.submit_elementwise(op, c.a, b, out, p0, p1)
+            return
+        slot = gpuos_ext.register_elementwise(f"fused|{c.arity}|{expr}", expr, c.arity, backend="nvrtc",
+                                              device=out.device)
+        if c.arity == 2:
+            gpuos_ext.submit_binary(slot, c.a, c.b, out)
+        else:
+            gpuos_ext.submit_unary(slot, c.a, out)
+
+    def flush_fused(self):
+        """Submit the chain being built: its last result, plus every earlier result of it that
+        is still referenced."""
+        c, self.chain = self.chain, None
+        if c is None:
+            return
+        last = len(c.steps) - 1
+        self._submit_steps(c, last, c.out)
+        for k in range(last):
+            t = c.steps[k][2]()
+            if t is not None:
+                self._submit_steps(c, k, t)
+        if last > 0:
+            self.fused_chains += 1
+            self.fused_ops += last + 1
+
     def _try_parametric(self, name, args, kwargs):
-        x = args[0]
+        code = self._parametric_code(name, args, kwargs)
+        return None if code is None else self._schedule_unary(code[0], args[0], code[1], code[2])
+
+    def _parametric_code(self, name, args, kwargs):
+        """(op code, p0, p1) of a parametric unary op, or None when its arguments are not ours."""
         kw = kwargs or {}
 
         def arg(i, key, default):
@@ -206,35 +345,35 @@ class _GPUOSSchedulerMode(TorchDispatchMode):
 
         if name == "aten::gelu":
             approx = arg(1, "approximate", "none")
-            return self._schedule_unary(_E.EW_GELU_TANH if approx == "tanh" else _E.EW_GELU, x)
+            return (_E.EW_GELU_TANH if approx == "tanh" else _E.EW_GELU, 0.0, 0.0)
         if name == "aten::leaky_relu":
-            return self._schedule_unary(_E.EW_LEAKY_RELU, x, float(arg(1, "negative_slope", 0.01)))
+            return (_E.EW_LEAKY_RELU, float(arg(1, "negative_slope", 0.01)), 0.0)
         if name == "aten::hardtanh":
-            return self._schedule_unary(_E.EW_CLAMP, x, float(arg(1, "min_val", -1.0)), float(arg(2, "max_val", 1.0)))
+            return (_E.EW_CLAMP, float(arg(1, "min_val", -1.0)), float(arg(2, "max_val", 1.0)))
         if name == "aten::elu":
             alpha, scale, iscale = arg(1, "alpha", 1.0), arg(2, "scale", 1), arg(3, "input_scale", 1)
             if scale != 1 or iscale != 1:
                 return None
-            return self._schedule_unary(_E.EW_ELU, x, float(alpha))
+            return (_E.EW_ELU, float(alpha), 0.0)
         if name == "aten::softplus":
-            return self._schedule_unary(_E.EW_SOFTPLUS, x, float(arg(1, "beta", 1.0)), float(arg(2, "threshold", 20.0)))
+            return (_E.EW_SOFTPLUS, float(arg(1, "beta", 1.0)), float(arg(2, "threshold", 20.0)))
         if name == "aten::clamp":
             lo, hi = arg(1, "min", None), arg(2, "max", None)
             if isinstance(lo, torch.Tensor) or isinstance(hi, torch.Tensor):
                 return None
             if lo is not None and hi is not None:
-                return self._schedule_unary(_E.EW_CLAMP, x, float(lo), float(hi))
+                return (_E.EW_CLAMP, float(lo), float(hi))
             if lo is not None:
-                return self._schedule_unary(_E.EW_CLAMP_MIN, x, float(lo))
+                return (_E.EW_CLAMP_MIN, float(lo), 0.0)
             if hi is not None:
-                return self._schedule_unary(_E.EW_CLAMP_MAX, x, float(hi))
+                return (_E.EW_CLAMP_MAX, float(hi), 0.0)
             return None
         if name == "aten::clamp_min":
             v = arg(1, "min", None)
-            return None if isinstance(v, torch.Tensor) or v is None else self._schedule_unary(_E.EW_CLAMP_MIN, x, float(v))
+            return None if isinstance(v, torch.Tensor) or v is None else (_E.EW_CLAMP_MIN, float(v), 0.0)
         if name == "aten::clamp_max":
             v = arg(1, "max", None)
-            return None if isinstance(v, torch.Tensor) or v is None else self._schedule_unary(_E.EW_CLAMP_MAX, x, float(v))
+            return None if isinstance(v, torch.Tensor) or v is None else (_E.EW_CLAMP_MAX, float(v), 0.0)
         return None
 
     def _try_reduce(self, name, args, kwargs):
@@ -302,6 +441,12 @@ class _GPUOSSchedulerMode(TorchDispatchMode):
     def __torch_dispatch__(self, func, types, args=(), kwargs=None):
         kind, name = _route(func)
         kwargs = kwargs or {}
+        if self.chain is not None:
+            res = self._try_extend(kind, name, args, kwargs) if kind in (1, 2, 3) else None
+            if res is not None:
+                self.scheduled_ops[name] += 1
+                return res
+            self.flush_fused()  # anything else sees the chain's results in place
         res = None
         if kind and not torch.is_grad_enabled():
             if kind == 1:
@@ -318,16 +463,15 @@ class _GPUOSSchedulerMode(TorchDispatchMode):
                 else:
                     res = self._try_topk(args, kwargs)
         if res is not None:
+            self.scheduled_ops[name] += 1
             return res
         # Not scheduled: make sure no pending request reads or writes what this op touches.
         if self._touches_pending(args, kwargs):
             self._sync_flush()
         self.fallbacks += 1
+        self.fallback_ops[name] += 1
         return func(*args, **kwargs)
 
-    def flush_fused(self):
-        """Kept for API compatibility: requests are submitted as they are dispatched."""
-        self.fused.clear()
 
 
 class GPUOSScheduler:
@@ -348,20 +492,28 @@ class GPUOSScheduler:
         return self
 
     def flush(self, sync: bool = False):
+        if self._mode is not None:
+            self._mode.flush_fused()
         gpuos_ext.flush(sync=sync)
         if sync:
             self._pending.clear()
 
     @property
     def stats(self):
+        """Totals plus per-op counts: ``scheduled_ops`` / ``fallback_ops`` map an aten op name
+        (``"aten::gelu"``) to the requests submitted to the runtime / the calls left to PyTorch."""
         m = self._mode
-        return {"scheduled": m.scheduled if m else 0, "fallbacks": m.fallbacks if m else 0}
+        return {"scheduled": m.scheduled if m else 0, "fallbacks": m.fallbacks if m else 0,
+                "scheduled_ops": dict(m.scheduled_ops) if m else {},
+                "fallback_ops": dict(m.fallback_ops) if m else {},
+                "fused_chains": m.fused_chains if m else 0, "fused_ops": m.fused_ops if m else 0}
 
     def __exit__(self, exc_type, exc, tb):
         try:
             if self._mode is not None:
                 self._mode.close()
                 self._mode.__exit__(exc_type, exc, tb)
+                self._mode.flush_fused()
         finally:
             gpuos_ext.flush(sync=True)
             self._pending.clear()
