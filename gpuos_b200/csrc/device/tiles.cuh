@@ -91,7 +91,7 @@ __device__ __forceinline__ void store8(unsigned char* base, int dt, uint32_t i, 
 
 // ---- EW_CONTIG -------------------------------------------------------------------------
 template <int OP>
-__device__ __noinline__ void ew_contig(const TileCtx& c) {
+__device__ __forceinline__ void ew_contig(const TileCtx& c) {
   const WorkItem& it = c.m->item;
   const uint32_t n = it.count;
   const float p0 = item_p0(it), p1 = item_p1(it);
@@ -185,16 +185,36 @@ __device__ __forceinline__ void f32_staged_loop(uint32_t sA, uint32_t sB, bool b
   }
 }
 
-// Runs the tile and returns true when it qualifies (see above); false leaves it to the table.
-__device__ __forceinline__ bool f32_staged_tile(const StageMeta& m, const unsigned char* sa,
-                                                const unsigned char* sb, uint32_t tid, uint32_t nt) {
+// The ops whose fp32 contiguous tiles run inlined (the cases of f32_staged_tile's switch).
+constexpr uint32_t kF32InlineOps =
+    (1u << GPUOS_EW_ADD) | (1u << GPUOS_EW_MUL) | (1u << GPUOS_EW_SUB) | (1u << GPUOS_EW_DIV) |
+    (1u << GPUOS_EW_MAXIMUM) | (1u << GPUOS_EW_MINIMUM) | (1u << GPUOS_EW_COPY) | (1u << GPUOS_EW_RELU) |
+    (1u << GPUOS_EW_ABS) | (1u << GPUOS_EW_NEG) | (1u << GPUOS_EW_ADD_ALPHA) | (1u << GPUOS_EW_SUB_ALPHA) |
+    (1u << GPUOS_EW_CLAMP) | (1u << GPUOS_EW_CLAMP_MIN) | (1u << GPUOS_EW_CLAMP_MAX) | (1u << GPUOS_EW_LEAKY_RELU) |
+    (1u << GPUOS_EW_SQRT) | (1u << GPUOS_EW_HARDSIGMOID) | (1u << GPUOS_EW_HARDSWISH) | (1u << GPUOS_EW_EXP) |
+    (1u << GPUOS_EW_LOG) | (1u << GPUOS_EW_TANH) | (1u << GPUOS_EW_ELU) | (1u << GPUOS_EW_SOFTPLUS) |
+    (1u << GPUOS_EW_GELU);
+
+// Whether an item is one of those tiles: fp32 a and out, contiguous (no broadcast), a staged
+// (and b staged, scalar or absent), 16-byte aligned.
+__device__ __forceinline__ bool f32_inline_ok(const StageMeta& m) {
   const WorkItem& it = m.item;
   const uint32_t flags = it.flags;
+  if (it.kind != IK_EW_CONTIG || it.op >= 32 || !((kF32InlineOps >> it.op) & 1u)) return false;
   if (it.dt_a != kF32 || it.dt_o != kF32 || (flags & (IF_A_BCAST | IF_B_BCAST)) || !(m.staged & 1)) return false;
+  const bool b_vec = (flags & IF_B_PRESENT) && !(flags & IF_B_SCALAR);
+  if (b_vec && (it.dt_b != kF32 || !(m.staged & 2))) return false;
+  return !((m.a_off & 15u) || (b_vec && (m.b_off & 15u)) || (it.o & 15ull));
+}
+
+// Runs the tile and returns true when it qualifies (f32_inline_ok); false leaves it to the table.
+__device__ __forceinline__ bool f32_staged_tile(const StageMeta& m, const unsigned char* sa,
+                                                const unsigned char* sb, uint32_t tid, uint32_t nt) {
+  if (!f32_inline_ok(m)) return false;
+  const WorkItem& it = m.item;
+  const uint32_t flags = it.flags;
   const bool b_imm = (flags & IF_B_SCALAR) != 0;
   const bool b_vec = (flags & IF_B_PRESENT) && !b_imm;
-  if (b_vec && (it.dt_b != kF32 || !(m.staged & 2))) return false;
-  if ((m.a_off & 15u) || (b_vec && (m.b_off & 15u)) || (it.o & 15ull)) return false;
   const float bscal = ((flags & IF_B_PRESENT) && b_imm) ? __uint_as_float((uint32_t)it.b) : 0.f;
   const uint32_t sA = ptx::smem_addr(sa + m.a_off);
   const uint32_t sB = b_vec ? ptx::smem_addr(sb + m.b_off) : 0u;
@@ -400,7 +420,7 @@ __device__ __forceinline__ void ew_2d_body(const TileCtx& c, F&& apply) {
 }
 
 template <int OP>
-__device__ __noinline__ void ew_2d(const TileCtx& c) {
+__device__ __forceinline__ void ew_2d(const TileCtx& c) {
   const float p0 = c.m->ext.layout.params[0], p1 = c.m->ext.layout.params[1];
   ew_2d_body(c, [=](float a, float b) { return ew_apply<OP>(a, b, p0, p1); });
 }
@@ -448,7 +468,9 @@ __device__ __forceinline__ void t2d_fill(const T2d& g, uint32_t src, uint32_t tb
   constexpr uint32_t es = TSRC == 0 ? 4u : 2u;
   const uint32_t nq = (g.nc + 3u) >> 2;
   const uint32_t total = g.nr * nq;
-  const uint32_t mg = g.nr > 1 ? (uint32_t)((0x100000000ull + g.nr - 1) / g.nr) : 0u;
+  // ceil(2^32 / nr) = floor((2^32 - 1) / nr) + 1 for nr >= 2: a 32-bit division (a 64-bit one is a
+  // long software routine, run by every thread of every block)
+  const uint32_t mg = g.nr > 1 ? 0xffffffffu / g.nr + 1u : 0u;
   const uint32_t cstep = sa1 * es;  // bytes from one column to the next
   for (uint32_t q = tid; q < total; q += nt) {
     const uint32_t jq = g.nr > 1 ? __umulhi(q, mg) : q;
@@ -548,7 +570,7 @@ __device__ __forceinline__ void t2d_out(const T2d& g, uint32_t tbuf, TO* O, int3
 }
 
 template <int OP>
-__device__ __noinline__ void ew_2dt(const TileCtx& c) {
+__device__ __forceinline__ void ew_2dt(const TileCtx& c) {
   const StageMeta& m = *c.m;
   const WorkItem& it = m.item;
   const Layout& L = m.ext.layout;
@@ -621,15 +643,6 @@ __device__ __noinline__ void ew_2dt(const TileCtx& c) {
   ptx::fence_proxy_async_smem();
 }
 
-template <int OP>
-__device__ void ew_tile(const TileCtx& c) {
-  const uint8_t kind = c.m->item.kind;
-  if (kind == IK_EW_CONTIG) ew_contig<OP>(c);
-  else if (kind == IK_EW_2DT) ew_2dt<OP>(c);
-  else if (kind == IK_EW_2D) ew_2d<OP>(c);
-  else ew_generic(c);
-}
-
 // ---- reductions ------------------------------------------------------------------------
 
 // Rows of one item; every row is read by all 32 lanes of a warp on consecutive elements (no
@@ -696,10 +709,9 @@ __device__ __forceinline__ void row_reduce_body(const TileCtx& c) {
   });
 }
 
-__device__ __noinline__ void row_reduce_tile(const TileCtx& c) { row_reduce_body(c); }
 
 // Arbitrary reduced axes: one output element per thread, serial over the reduced extent.
-__device__ __noinline__ void red_generic_tile(const TileCtx& c) {
+__device__ __forceinline__ void red_generic_tile(const TileCtx& c) {
   const WorkItem& it = c.m->item;
   const Layout& L = c.m->ext.layout;
   const void* A = reinterpret_cast<const void*>(it.a);
@@ -744,7 +756,7 @@ __device__ __forceinline__ uint32_t topk_key(float v, bool largest) {
 // (key << 32 | ~index, so equal values prefer the lower index); round q takes the warp-wide
 // maximum below round q-1's winner, so k rounds give the k preferred elements in order and
 // nothing has to be marked.  Values are copied bit for bit (they keep x's dtype).
-__device__ __noinline__ void topk_tile(const TileCtx& c) {
+__device__ __forceinline__ void topk_tile(const TileCtx& c) {
   const WorkItem& it = c.m->item;
   const uint32_t rows = it.count, n = it.aux, k = (uint32_t)it.x;
   const bool largest = ((it.x >> 32) & 1u) != 0;
@@ -782,11 +794,5 @@ __device__ __noinline__ void topk_tile(const TileCtx& c) {
   }
 }
 
-__device__ void reduce_tile(const TileCtx& c) {
-  const uint8_t kind = c.m->item.kind;
-  if (kind == IK_ROW_REDUCE) row_reduce_tile(c);
-  else if (kind == IK_TOPK) topk_tile(c);
-  else red_generic_tile(c);
-}
 
 }  // namespace gpuos

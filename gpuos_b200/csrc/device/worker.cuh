@@ -65,23 +65,6 @@ __device__ __forceinline__ OpFn resolve_op(const WorkerParams& P, int op) {
   return reinterpret_cast<OpFn>(*reinterpret_cast<volatile unsigned long long*>(&P.op_table[phys]));
 }
 
-// Tile functions of the batched path: one per element-wise op, then the reductions.
-// One indirect call per work item dispatches through this table.
-__device__ TileFn g_tile_fns[GPUOS_EW_NUM_OPS + 1] = {
-    ew_tile<0>,  ew_tile<1>,  ew_tile<2>,  ew_tile<3>,  ew_tile<4>,  ew_tile<5>,  ew_tile<6>,
-    ew_tile<7>,  ew_tile<8>,  ew_tile<9>,  ew_tile<10>, ew_tile<11>, ew_tile<12>, ew_tile<13>,
-    ew_tile<14>, ew_tile<15>, ew_tile<16>, ew_tile<17>, ew_tile<18>, ew_tile<19>, ew_tile<20>,
-    ew_tile<21>, ew_tile<22>, ew_tile<23>, ew_tile<24>, ew_tile<25>, ew_tile<26>, ew_tile<27>,
-    ew_tile<28>, ew_tile<29>, reduce_tile};
-
-// Staged transpose blocks reach their tile function directly (one call level, not two through
-// ew_tile: every call level saves registers of all compute threads through local memory).
-__device__ TileFn g_t2d_fns[GPUOS_EW_NUM_OPS] = {
-    ew_2dt<0>,  ew_2dt<1>,  ew_2dt<2>,  ew_2dt<3>,  ew_2dt<4>,  ew_2dt<5>,  ew_2dt<6>,  ew_2dt<7>,
-    ew_2dt<8>,  ew_2dt<9>,  ew_2dt<10>, ew_2dt<11>, ew_2dt<12>, ew_2dt<13>, ew_2dt<14>, ew_2dt<15>,
-    ew_2dt<16>, ew_2dt<17>, ew_2dt<18>, ew_2dt<19>, ew_2dt<20>, ew_2dt<21>, ew_2dt<22>, ew_2dt<23>,
-    ew_2dt<24>, ew_2dt<25>, ew_2dt<26>, ew_2dt<27>, ew_2dt<28>, ew_2dt<29>};
-
 // ---- completion ----------------------------------------------------------------------
 // Completed items of one flush awaiting accounting (the completer warp batches them).
 struct DoneRun {
@@ -165,6 +148,106 @@ __device__ __forceinline__ void compute_diag(const WorkerParams& P, uint32_t cti
   }
 }
 
+// ---- runs of table-dispatched tiles ----------------------------------------------------
+// A tile reached through a function table is a call, and every call saves and restores the
+// callee-saved registers of all compute threads through local memory.  The table therefore
+// holds run functions: one call processes the stage it was made for and every following stage
+// whose item belongs to the same run function, so the call is paid once per run of items (the
+// consecutive tickets of one request that this CTA claimed as a chunk) instead of once per
+// item.  A run returns with the full phase of the next stage complete (kRunNext), or after a
+// wait that expired, the error reported (kRunError).
+struct RunState {
+  const WorkerParams* P;
+  SmemHeader* H;
+  unsigned char* bufs;
+  uint32_t stage_bytes, S;
+  uint32_t s, parity;  // stage and phase parity of use `iter`
+  uint64_t iter;
+  uint32_t tid, nt;
+  int status;
+};
+constexpr int kRunNext = 0, kRunError = 1;
+
+// The run function of an item (its index in g_run_fns), one per tile kind and op so that each
+// holds a single tile body (with several bodies inlined side by side the register allocation
+// spills): [0, N) contiguous tiles of op k, N the generic reductions and top-k, N + 1 + k staged
+// transpose blocks, 2N + 1 + k 2-D blocks, 3N + 1 the generic stride walk; -1 for the items the
+// compute loop runs itself (N = GPUOS_EW_NUM_OPS).
+constexpr int kRunT2d = GPUOS_EW_NUM_OPS + 1, kRun2d = 2 * GPUOS_EW_NUM_OPS + 1, kRunGeneric = 3 * GPUOS_EW_NUM_OPS + 1;
+__device__ __forceinline__ int run_index(const StageMeta& m) {
+  const uint8_t kind = m.item.kind;
+  const int op = (int)m.item.op;
+  if (kind == IK_EW_CONTIG) return f32_inline_ok(m) ? -1 : op;
+  if (kind == IK_EW_2DT) return kRunT2d + op;
+  if (kind == IK_EW_2D) return kRun2d + op;
+  if (kind == IK_EW_GENERIC) return kRunGeneric;
+  if (kind == IK_RED_GENERIC || kind == IK_TOPK) return GPUOS_EW_NUM_OPS;
+  return -1;
+}
+
+// Ends the tile of stage s (this warp's done arrival), moves to the next stage and waits for
+// it to fill; true when its item belongs to run `idx` too.
+__device__ __forceinline__ bool run_advance(RunState& r, uint32_t& s, uint32_t& parity, uint64_t& iter, int idx) {
+  SmemHeader& H = *r.H;
+  __syncwarp();
+  if ((r.tid & 31) == 0) ptx::mbar_arrive(ptx::smem_addr(&H.done[s]));
+  ++iter;
+  s = s + 1 == r.S ? 0 : s + 1;
+  if (s == 0) parity ^= 1u;
+  uint64_t waited = 0;
+  if (!wait_phase(ptx::smem_addr(&H.full[s]), parity, &H.prod_alive, H.full_wait_ns, &waited)) {
+    report_error(*r.P, DE_WAIT_FULL, iter, waited, H.full_wait_ns);
+    r.status = kRunError;
+    return false;
+  }
+  r.status = kRunNext;
+  return run_index(H.meta[s]) == idx;
+}
+
+__device__ __forceinline__ TileCtx run_ctx(const RunState& r, uint32_t s) {
+  TileCtx c;
+  c.m = &r.H->meta[s];
+  c.sa = r.bufs + (size_t)s * r.stage_bytes;
+  c.sb = c.sa + (r.stage_bytes >> 1);
+  c.tid = r.tid;
+  c.nt = r.nt;
+  return c;
+}
+
+// One run function: `BODY` runs the tile of one stage; the run goes on while the next item has
+// the same run index.
+#define GPUOS_RUN_LOOP(IDX, BODY)                                  \
+  uint32_t s = r.s, parity = r.parity;                             \
+  uint64_t iter = r.iter;                                          \
+  do {                                                             \
+    const TileCtx c = run_ctx(r, s);                               \
+    BODY;                                                          \
+  } while (run_advance(r, s, parity, iter, (IDX)));                \
+  r.s = s;                                                         \
+  r.parity = parity;                                               \
+  r.iter = iter;
+
+template <int OP>
+__device__ __noinline__ void contig_run(RunState& r) { GPUOS_RUN_LOOP(OP, ew_contig<OP>(c)) }
+template <int OP>
+__device__ __noinline__ void t2d_run(RunState& r) { GPUOS_RUN_LOOP(kRunT2d + OP, ew_2dt<OP>(c)) }
+template <int OP>
+__device__ __noinline__ void e2d_run(RunState& r) { GPUOS_RUN_LOOP(kRun2d + OP, ew_2d<OP>(c)) }
+__device__ __noinline__ void generic_run(RunState& r) { GPUOS_RUN_LOOP(kRunGeneric, ew_generic(c)) }
+__device__ __noinline__ void reduce_run(RunState& r) {
+  GPUOS_RUN_LOOP(GPUOS_EW_NUM_OPS, if (c.m->item.kind == IK_TOPK) topk_tile(c); else red_generic_tile(c))
+}
+#undef GPUOS_RUN_LOOP
+
+typedef void (*RunFn)(RunState&);
+#define GPUOS_RUN10(F, b) F<b + 0>, F<b + 1>, F<b + 2>, F<b + 3>, F<b + 4>, F<b + 5>, F<b + 6>, F<b + 7>, F<b + 8>, F<b + 9>
+#define GPUOS_RUN30(F) GPUOS_RUN10(F, 0), GPUOS_RUN10(F, 10), GPUOS_RUN10(F, 20)
+static_assert(GPUOS_EW_NUM_OPS == 30, "one run function per op in each group of g_run_fns");
+__device__ RunFn g_run_fns[3 * GPUOS_EW_NUM_OPS + 2] = {GPUOS_RUN30(contig_run), reduce_run, GPUOS_RUN30(t2d_run),
+                                                        GPUOS_RUN30(e2d_run), generic_run};
+#undef GPUOS_RUN30
+#undef GPUOS_RUN10
+
 __device__ __forceinline__ void compute_loop(const WorkerParams& P, const WorkerShared& W, uint32_t ctid, uint32_t nct) {
   SmemHeader& H = *W.H;
   const uint32_t S = P.stages;
@@ -172,14 +255,19 @@ __device__ __forceinline__ void compute_loop(const WorkerParams& P, const Worker
   // compute thread a local load and store per item
   unsigned long long wait_c = 0, tile_c = 0, fill_c = 0;
   uint32_t s = 0, parity = 0;  // stage and phase parity of use `iter` (stages are used in order)
-  for (uint64_t iter = 0;; ++iter, s = s + 1 == S ? 0 : s + 1, parity ^= s == 0 ? 1u : 0u) {
+  uint64_t iter = 0;
+  bool ready = false;  // a run already waited for stage s to fill
+  for (;;) {
     const unsigned long long c0 = clock64();
-    uint64_t waited = 0;
-    if (!wait_phase(ptx::smem_addr(&H.full[s]), parity, &H.prod_alive, H.full_wait_ns, &waited)) {
-      report_error(P, DE_WAIT_FULL, iter, waited, H.full_wait_ns);
-      compute_diag(P, ctid, wait_c, tile_c, fill_c);
-      return;
+    if (!ready) {
+      uint64_t waited = 0;
+      if (!wait_phase(ptx::smem_addr(&H.full[s]), parity, &H.prod_alive, H.full_wait_ns, &waited)) {
+        report_error(P, DE_WAIT_FULL, iter, waited, H.full_wait_ns);
+        compute_diag(P, ctid, wait_c, tile_c, fill_c);
+        return;
+      }
     }
+    ready = false;
     const StageMeta& m = H.meta[s];
     const uint8_t kind = m.item.kind;
     const unsigned long long c1 = clock64();
@@ -197,37 +285,55 @@ __device__ __forceinline__ void compute_loop(const WorkerParams& P, const Worker
     } else {
       const unsigned char* sa = stage_buf(W, s);
       const unsigned char* sb = sa + (W.stage_bytes >> 1);
-      if (iter == 0 && ctid == 0) tl_mark(P, TL_TILE0);
-      // inlined paths first (no register saves around a call through the tile table)
+      const bool first = iter == 0;
+      if (first && ctid == 0) tl_mark(P, TL_TILE0);
+      // inlined paths first (no register saves around a call)
       if (kind == IK_EW_CONTIG && f32_staged_tile(m, sa, sb, ctid, nct)) {
-      } else {
-        // the tile context exists only here: its address goes to the tile function, so it
-        // lives in local memory, which the inlined fp32 path above must not pay for
+      } else if (kind == IK_ROW_REDUCE) {
         TileCtx ctx;
         ctx.m = &m;
         ctx.sa = sa;
         ctx.sb = sb;
         ctx.tid = ctid;
         ctx.nt = nct;
-        if (kind == IK_ROW_REDUCE) {
-          row_reduce_body(ctx);
-        } else if (kind == IK_EW_2DT) {
-          g_t2d_fns[m.item.op](ctx);
-        } else {
-          const uint32_t fi =
-              (kind == IK_EW_CONTIG || kind == IK_EW_GENERIC || kind == IK_EW_2D || kind == IK_EW_2DT)
-                  ? m.item.op
-                  : GPUOS_EW_NUM_OPS;
-          TileFn fn = g_tile_fns[fi];
-          fn(ctx);
+        row_reduce_body(ctx);
+      } else {
+        // a run of table tiles: it ends every tile it runs and leaves stage s filled
+        const int idx = run_index(m);
+        RunState r;
+        r.P = &P;
+        r.H = &H;
+        r.bufs = W.bufs;
+        r.stage_bytes = W.stage_bytes;
+        r.S = S;
+        r.s = s;
+        r.parity = parity;
+        r.iter = iter;
+        r.tid = ctid;
+        r.nt = nct;
+        r.status = kRunNext;
+        g_run_fns[idx < 0 ? GPUOS_EW_NUM_OPS : idx](r);
+        if (first && ctid == 0) tl_mark(P, TL_TILE1);
+        s = r.s;
+        parity = r.parity;
+        iter = r.iter;
+        tile_c += clock64() - c1;
+        if (r.status == kRunError) {
+          compute_diag(P, ctid, wait_c, tile_c, fill_c);
+          return;
         }
+        ready = true;
+        continue;
       }
-      if (iter == 0 && ctid == 0) tl_mark(P, TL_TILE1);
+      if (first && ctid == 0) tl_mark(P, TL_TILE1);
     }
     // this warp is done with the stage; no CTA-wide barrier between tiles
     __syncwarp();
     if ((ctid & 31) == 0) ptx::mbar_arrive(ptx::smem_addr(&H.done[s]));
     tile_c += clock64() - c1;
+    ++iter;
+    s = s + 1 == S ? 0 : s + 1;
+    if (s == 0) parity ^= 1u;
   }
 }
 
@@ -818,6 +924,13 @@ __device__ __forceinline__ uint32_t stage_group(const WorkerParams& P, const Wor
   return g;
 }
 
+// Tickets per CTA share of `ahead` published tickets: ahead / (2 x grid), in 32 bits (a 64-bit
+// division is a long software routine); at least kChunk whenever the quotient would be.
+__device__ __forceinline__ uint64_t chunk_share(uint64_t ahead) {
+  const uint32_t d = 2u * gridDim.x;
+  return ahead >= (uint64_t)kChunk * d ? (uint64_t)kChunk : (uint64_t)((uint32_t)ahead / d);
+}
+
 __device__ __forceinline__ void producer_loop(const WorkerParams& P, const WorkerShared& W, uint32_t lane) {
   SmemHeader& H = *W.H;
   ProdCold& C = H.cold;
@@ -878,7 +991,7 @@ __device__ __forceinline__ void producer_loop(const WorkerParams& P, const Worke
           // Claim a chunk: several tickets per atomic while plenty of published work lies
           // ahead, single tickets near the end of the published work (load balance).
           const uint64_t ahead = st.tail_cache > st.chunk_end ? st.tail_cache - st.chunk_end : 0;
-          uint64_t k = ahead / (2ull * gridDim.x);
+          uint64_t k = chunk_share(ahead);
           k = k < 1 ? 1 : (k > kChunk ? kChunk : k);
           if (st.iter == 0 && st.chunk_end == 0) tl_mark(P, TL_CLAIM);
           st.ticket = atomicAdd(&dc->head, k);
@@ -890,7 +1003,7 @@ __device__ __forceinline__ void producer_loop(const WorkerParams& P, const Worke
         // that goes idle never holds a chunk ahead (this chunk would have to be published).
         const uint64_t ahead = st.tail_cache > st.chunk_end ? st.tail_cache - st.chunk_end : 0;
         if (st.chunk_end <= st.tail_cache && ahead >= 2ull * gridDim.x) {
-          uint64_t k = ahead / (2ull * gridDim.x);
+          uint64_t k = chunk_share(ahead);
           k = k > kChunk ? kChunk : k;
           st.n_ticket = atomicAdd(&dc->head, k);
           st.n_end = st.n_ticket + k;
