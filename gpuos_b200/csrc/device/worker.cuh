@@ -216,16 +216,21 @@ __device__ __forceinline__ TileCtx run_ctx(const RunState& r, uint32_t s) {
 
 // One run function: `BODY` runs the tile of one stage; the run goes on while the next item has
 // the same run index.
+// The state is copied into registers first: read through the reference, every field would be
+// reloaded from the caller's local memory after each inline-asm memory clobber (a global-latency
+// load per field per item, most of them L1 misses beside a large shared-memory carve-out).
 #define GPUOS_RUN_LOOP(IDX, BODY)                                  \
-  uint32_t s = r.s, parity = r.parity;                             \
-  uint64_t iter = r.iter;                                          \
+  RunState rl = r;                                                 \
+  uint32_t s = rl.s, parity = rl.parity;                           \
+  uint64_t iter = rl.iter;                                         \
   do {                                                             \
-    const TileCtx c = run_ctx(r, s);                               \
+    const TileCtx c = run_ctx(rl, s);                              \
     BODY;                                                          \
-  } while (run_advance(r, s, parity, iter, (IDX)));                \
+  } while (run_advance(rl, s, parity, iter, (IDX)));               \
   r.s = s;                                                         \
   r.parity = parity;                                               \
-  r.iter = iter;
+  r.iter = iter;                                                   \
+  r.status = rl.status;
 
 template <int OP>
 __device__ __noinline__ void contig_run(RunState& r) { GPUOS_RUN_LOOP(OP, ew_contig<OP>(c)) }
