@@ -30,6 +30,47 @@ __device__ __forceinline__ float4 ew_apply4(float4 a, float4 b, float p0, float 
                      ew_apply<OP>(a.z, b.z, p0, p1), ew_apply<OP>(a.w, b.w, p0, p1));
 }
 
+// The ops whose fp32 contiguous tiles run inlined (the cases of f32_staged_tile's switch).
+constexpr uint32_t kF32InlineOps =
+    (1u << GPUOS_EW_ADD) | (1u << GPUOS_EW_MUL) | (1u << GPUOS_EW_SUB) | (1u << GPUOS_EW_DIV) |
+    (1u << GPUOS_EW_MAXIMUM) | (1u << GPUOS_EW_MINIMUM) | (1u << GPUOS_EW_COPY) | (1u << GPUOS_EW_RELU) |
+    (1u << GPUOS_EW_ABS) | (1u << GPUOS_EW_NEG) | (1u << GPUOS_EW_ADD_ALPHA) | (1u << GPUOS_EW_SUB_ALPHA) |
+    (1u << GPUOS_EW_CLAMP) | (1u << GPUOS_EW_CLAMP_MIN) | (1u << GPUOS_EW_CLAMP_MAX) | (1u << GPUOS_EW_LEAKY_RELU) |
+    (1u << GPUOS_EW_SQRT) | (1u << GPUOS_EW_HARDSIGMOID) | (1u << GPUOS_EW_HARDSWISH) | (1u << GPUOS_EW_EXP) |
+    (1u << GPUOS_EW_LOG) | (1u << GPUOS_EW_TANH) | (1u << GPUOS_EW_ELU) | (1u << GPUOS_EW_SOFTPLUS) |
+    (1u << GPUOS_EW_GELU);
+
+// The ops of kSharedOps on four values, the op chosen at run time: one copy of the staged
+// transpose block's loops then serves all of them (OP = kDynOp).  Per-op copies of the loops
+// missed in the instruction cache whenever consecutive blocks had different ops (config 3:
+// "no instruction" was the largest stall reason, 32 % of stalls, with four ops interleaved).
+// Division keeps a body per op: its IEEE slow path needs registers that make the shared body
+// spill.  (Two shared bodies, simple ops and float-math ops, spilled less but measured slower
+// on the mixed stream: consecutive tiles alternating between the two bodies miss again.)
+constexpr int kDynOp = -1;
+constexpr uint32_t kSharedOps = kF32InlineOps & ~(1u << GPUOS_EW_DIV);
+__device__ __forceinline__ void ew_apply4_sw(uint32_t op, const float* a, const float* b, float p0, float p1,
+                                             float* v) {
+  switch (op) {
+#define GPUOS_SW(k)                                                    \
+  case k: {                                                            \
+    _Pragma("unroll") for (int t = 0; t < 4; ++t) v[t] = ew_apply<k>(a[t], b[t], p0, p1); \
+  } break;
+    GPUOS_SW(GPUOS_EW_ADD) GPUOS_SW(GPUOS_EW_MUL) GPUOS_SW(GPUOS_EW_SUB)
+    GPUOS_SW(GPUOS_EW_MAXIMUM) GPUOS_SW(GPUOS_EW_MINIMUM) GPUOS_SW(GPUOS_EW_COPY) GPUOS_SW(GPUOS_EW_RELU)
+    GPUOS_SW(GPUOS_EW_ABS) GPUOS_SW(GPUOS_EW_NEG) GPUOS_SW(GPUOS_EW_ADD_ALPHA) GPUOS_SW(GPUOS_EW_SUB_ALPHA)
+    GPUOS_SW(GPUOS_EW_CLAMP) GPUOS_SW(GPUOS_EW_CLAMP_MIN) GPUOS_SW(GPUOS_EW_CLAMP_MAX) GPUOS_SW(GPUOS_EW_LEAKY_RELU)
+    GPUOS_SW(GPUOS_EW_SQRT) GPUOS_SW(GPUOS_EW_HARDSIGMOID) GPUOS_SW(GPUOS_EW_HARDSWISH) GPUOS_SW(GPUOS_EW_EXP)
+    GPUOS_SW(GPUOS_EW_LOG) GPUOS_SW(GPUOS_EW_TANH) GPUOS_SW(GPUOS_EW_ELU) GPUOS_SW(GPUOS_EW_SOFTPLUS)
+    GPUOS_SW(GPUOS_EW_GELU)
+#undef GPUOS_SW
+    default:
+#pragma unroll
+      for (int t = 0; t < 4; ++t) v[t] = a[t];
+  }
+}
+
+
 // ---- 16-bit vector helpers: 8 elements per 16 bytes ----------------------------------
 __device__ __forceinline__ void unpack8(uint4 raw, int dt, float* f) {
   const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
@@ -185,16 +226,6 @@ __device__ __forceinline__ void f32_staged_loop(uint32_t sA, uint32_t sB, bool b
   }
 }
 
-// The ops whose fp32 contiguous tiles run inlined (the cases of f32_staged_tile's switch).
-constexpr uint32_t kF32InlineOps =
-    (1u << GPUOS_EW_ADD) | (1u << GPUOS_EW_MUL) | (1u << GPUOS_EW_SUB) | (1u << GPUOS_EW_DIV) |
-    (1u << GPUOS_EW_MAXIMUM) | (1u << GPUOS_EW_MINIMUM) | (1u << GPUOS_EW_COPY) | (1u << GPUOS_EW_RELU) |
-    (1u << GPUOS_EW_ABS) | (1u << GPUOS_EW_NEG) | (1u << GPUOS_EW_ADD_ALPHA) | (1u << GPUOS_EW_SUB_ALPHA) |
-    (1u << GPUOS_EW_CLAMP) | (1u << GPUOS_EW_CLAMP_MIN) | (1u << GPUOS_EW_CLAMP_MAX) | (1u << GPUOS_EW_LEAKY_RELU) |
-    (1u << GPUOS_EW_SQRT) | (1u << GPUOS_EW_HARDSIGMOID) | (1u << GPUOS_EW_HARDSWISH) | (1u << GPUOS_EW_EXP) |
-    (1u << GPUOS_EW_LOG) | (1u << GPUOS_EW_TANH) | (1u << GPUOS_EW_ELU) | (1u << GPUOS_EW_SOFTPLUS) |
-    (1u << GPUOS_EW_GELU);
-
 // Whether an item is one of those tiles: fp32 a and out, contiguous (no broadcast), a staged
 // (and b staged, scalar or absent), 16-byte aligned.
 __device__ __forceinline__ bool f32_inline_ok(const StageMeta& m) {
@@ -221,6 +252,8 @@ __device__ __forceinline__ bool f32_staged_tile(const StageMeta& m, const unsign
   float* O = reinterpret_cast<float*>(it.o);
   const uint32_t n = it.count;
   const float p0 = item_p0(it), p1 = item_p1(it);
+  // one body per op: a body shared by all ops (the op switched per four values, as the staged
+  // transpose blocks do) measured slower here (config-2 stream 0.64 -> 0.78 ms)
   switch (it.op) {
 #define GPUOS_F32_CASE(OPC) \
   case OPC:                 \
@@ -541,7 +574,7 @@ template <int OP, typename TO>
 __device__ __forceinline__ void t2d_out(const T2d& g, uint32_t tbuf, TO* O, int32_t o0s, int32_t o1s, bool vec,
                                         const void* B, int dtb, int bmode, int32_t b0s, int32_t b1s,
                                         const float* bpre, bool have_b, float p0, float p1, uint32_t tid,
-                                        uint32_t nt) {
+                                        uint32_t nt, uint32_t dop) {
   const uint32_t qsh = g.lg - 2, total = g.nr << qsh;
   // with cw dividing nt every quad of a thread is in the same column quad: a column broadcast
   // operand is read once per thread (before phase 1, `bpre`, when `have_b`)
@@ -563,8 +596,12 @@ __device__ __forceinline__ void t2d_out(const T2d& g, uint32_t tbuf, TO* O, int3
         bq[t] = j0 + t < g.nc ? ld_elem(B, dtb, (int64_t)r * b0s + (int64_t)(j0 + t) * b1s) : 0.f;
     }
     float v[4];
+    if constexpr (OP == kDynOp) {
+      ew_apply4_sw(dop, av, bq, p0, p1, v);
+    } else {
 #pragma unroll
-    for (uint32_t t = 0; t < 4; ++t) v[t] = ew_apply<OP>(av[t], bq[t], p0, p1);
+      for (uint32_t t = 0; t < 4; ++t) v[t] = ew_apply<OP>(av[t], bq[t], p0, p1);
+    }
     t2d_store4<TO>(O, o0s, o1s, r, j0, g.nc, vec, v);
   }
 }
@@ -632,13 +669,13 @@ __device__ __forceinline__ void ew_2dt(const TileCtx& c) {
   }
   if (dto == kF16)
     t2d_out<OP, __half>(g, tbuf, reinterpret_cast<__half*>(O), o0s, o1s, vec, B, dtb, bmode, b0s, b1s, bpre, have_b, p0,
-                        p1, c.tid, c.nt);
+                        p1, c.tid, c.nt, it.op);
   else if (dto == kBF16)
     t2d_out<OP, __nv_bfloat16>(g, tbuf, reinterpret_cast<__nv_bfloat16*>(O), o0s, o1s, vec, B, dtb, bmode, b0s, b1s,
-                               bpre, have_b, p0, p1, c.tid, c.nt);
+                               bpre, have_b, p0, p1, c.tid, c.nt, it.op);
   else
     t2d_out<OP, float>(g, tbuf, reinterpret_cast<float*>(O), o0s, o1s, vec, B, dtb, bmode, b0s, b1s, bpre, have_b,
-                       p0, p1, c.tid, c.nt);
+                       p0, p1, c.tid, c.nt, it.op);
   // the stage is next filled by bulk copies (async proxy) after these generic writes of T
   ptx::fence_proxy_async_smem();
 }

@@ -171,14 +171,17 @@ constexpr int kRunNext = 0, kRunError = 1;
 // The run function of an item (its index in g_run_fns), one per tile kind and op so that each
 // holds a single tile body (with several bodies inlined side by side the register allocation
 // spills): [0, N) contiguous tiles of op k, N the generic reductions and top-k, N + 1 + k staged
-// transpose blocks, 2N + 1 + k 2-D blocks, 3N + 1 the generic stride walk; -1 for the items the
-// compute loop runs itself (N = GPUOS_EW_NUM_OPS).
-constexpr int kRunT2d = GPUOS_EW_NUM_OPS + 1, kRun2d = 2 * GPUOS_EW_NUM_OPS + 1, kRunGeneric = 3 * GPUOS_EW_NUM_OPS + 1;
+// transpose blocks of op k, 2N + 1 + k 2-D blocks, 3N + 1 the generic stride walk, 3N + 2 staged
+// transpose blocks of the ops of kSharedOps (one shared body, the op switched per quad of
+// values: per-op bodies missed in the instruction cache when consecutive blocks changed op); -1
+// for the items the compute loop runs itself (N = GPUOS_EW_NUM_OPS).
+constexpr int kRunT2d = GPUOS_EW_NUM_OPS + 1, kRun2d = 2 * GPUOS_EW_NUM_OPS + 1,
+              kRunGeneric = 3 * GPUOS_EW_NUM_OPS + 1, kRunT2dShared = 3 * GPUOS_EW_NUM_OPS + 2;
 __device__ __forceinline__ int run_index(const StageMeta& m) {
   const uint8_t kind = m.item.kind;
   const int op = (int)m.item.op;
   if (kind == IK_EW_CONTIG) return f32_inline_ok(m) ? -1 : op;
-  if (kind == IK_EW_2DT) return kRunT2d + op;
+  if (kind == IK_EW_2DT) return op < 32 && ((kSharedOps >> op) & 1u) ? kRunT2dShared : kRunT2d + op;
   if (kind == IK_EW_2D) return kRun2d + op;
   if (kind == IK_EW_GENERIC) return kRunGeneric;
   if (kind == IK_RED_GENERIC || kind == IK_TOPK) return GPUOS_EW_NUM_OPS;
@@ -239,6 +242,7 @@ __device__ __noinline__ void t2d_run(RunState& r) { GPUOS_RUN_LOOP(kRunT2d + OP,
 template <int OP>
 __device__ __noinline__ void e2d_run(RunState& r) { GPUOS_RUN_LOOP(kRun2d + OP, ew_2d<OP>(c)) }
 __device__ __noinline__ void generic_run(RunState& r) { GPUOS_RUN_LOOP(kRunGeneric, ew_generic(c)) }
+__device__ __noinline__ void t2d_shared_run(RunState& r) { GPUOS_RUN_LOOP(kRunT2dShared, ew_2dt<kDynOp>(c)) }
 __device__ __noinline__ void reduce_run(RunState& r) {
   GPUOS_RUN_LOOP(GPUOS_EW_NUM_OPS, if (c.m->item.kind == IK_TOPK) topk_tile(c); else red_generic_tile(c))
 }
@@ -248,8 +252,8 @@ typedef void (*RunFn)(RunState&);
 #define GPUOS_RUN10(F, b) F<b + 0>, F<b + 1>, F<b + 2>, F<b + 3>, F<b + 4>, F<b + 5>, F<b + 6>, F<b + 7>, F<b + 8>, F<b + 9>
 #define GPUOS_RUN30(F) GPUOS_RUN10(F, 0), GPUOS_RUN10(F, 10), GPUOS_RUN10(F, 20)
 static_assert(GPUOS_EW_NUM_OPS == 30, "one run function per op in each group of g_run_fns");
-__device__ RunFn g_run_fns[3 * GPUOS_EW_NUM_OPS + 2] = {GPUOS_RUN30(contig_run), reduce_run, GPUOS_RUN30(t2d_run),
-                                                        GPUOS_RUN30(e2d_run), generic_run};
+__device__ RunFn g_run_fns[3 * GPUOS_EW_NUM_OPS + 3] = {GPUOS_RUN30(contig_run), reduce_run, GPUOS_RUN30(t2d_run),
+                                                        GPUOS_RUN30(e2d_run), generic_run, t2d_shared_run};
 #undef GPUOS_RUN30
 #undef GPUOS_RUN10
 
