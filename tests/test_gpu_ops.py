@@ -162,6 +162,26 @@ def test_transcendental_edge_values(rt, name):
     assert ok, f"{name}: {msg}"
 
 
+def test_pow_special_values(rt):
+    """pow over every pair of special and ordinary values (zeros of both signs, +-1, +-inf, NaN,
+    denormals, huge, integer / odd / even / non-integer exponents, |y| >= 2**24): the C99 special
+    cases PyTorch CPU follows, ordinary values within 2 ulp, signed zeros and infinities exact."""
+    vals = [0.0, -0.0, 1.0, -1.0, 0.5, -0.5, 2.0, -2.0, 3.0, -3.0, 2.5, -2.5, float("inf"), -float("inf"),
+            float("nan"), 1e-40, -1e-40, 1e30, -1e30, 16777216.0, -16777216.0, 1e10, -1e10, 127.0, -149.0, 0.1]
+    x = torch.tensor([a for a in vals for _ in vals], dtype=torch.float32)
+    y = torch.tensor([b for _ in vals for b in vals], dtype=torch.float32)
+    out = torch.empty(x.numel(), device="cuda")
+    rt.submit_elementwise(EW["POW"], x.cuda(), y.cuda(), out)
+    rt.flush(sync=True)
+    got, ref = out.cpu(), torch.pow(x, y)
+    ok, msg = compare("POW", got, ref, torch.float32, x)
+    assert ok, msg
+    special = ~torch.isfinite(ref) | (ref == 0)
+    assert same_bits(got[special], ref[special]), [(float(a), float(b), float(g), float(r)) for a, b, g, r in
+                                                     zip(x[special], y[special], got[special], ref[special])
+                                                     if not same_bits(g.reshape(1), r.reshape(1))][:8]
+
+
 # transcendental ops evaluated with CUDA's float functions (the others are rounded from double)
 FLOAT_TRANSCENDENTALS = ["EXP", "LOG", "TANH", "ELU", "SOFTPLUS", "GELU"]
 
