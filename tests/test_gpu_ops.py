@@ -44,7 +44,7 @@ TRANSCENDENTAL_NAMES = {k for k, v in EW.items() if v in TRANSCENDENTAL}
 # PyTorch CPU's float GELU, (x * 0.5) * (1 + erf(x / sqrt 2)), is up to 6.2 |x| 2**-24 away
 # from the float64 value where 1 + erf cancels (thousands of ulp of the small result there); the
 # runtime evaluates the same float expression with CUDA's erff, and over every float input the
-# two are within 7.2 |x| 2**-24 (test_float_transcendentals_every_input).  For GELU the bound is
+# two are within 7.2 |x| 2**-24 (test_unary_ops_every_input).  For GELU the bound is
 # therefore |difference| <= 8 |x| 2**-24 (or the usual ulp bound); for 16-bit outputs one ulp of
 # the output type on top of it.
 CANCELLING = {"GELU", "GELU_TANH"}
@@ -184,6 +184,12 @@ def test_pow_special_values(rt):
 
 # transcendental ops evaluated with CUDA's float functions (the others are rounded from double)
 FLOAT_TRANSCENDENTALS = ["EXP", "LOG", "TANH", "ELU", "SOFTPLUS", "GELU"]
+# unary ops whose bound over every float input is also proven: sigmoid (double, 2 ulp), sqrt
+# (IEEE; PyTorch CPU's vectorised sqrt is not always correctly rounded: 1 ulp) and the exact ops
+# (every bit, signed zeros included; NaN against NaN)
+EVERY_INPUT_BOUND = {name: MAX_ULP_F32 for name in FLOAT_TRANSCENDENTALS}
+EVERY_INPUT_BOUND.update({"SIGMOID": MAX_ULP_F32, "SQRT": 1, "RELU": 0, "ABS": 0, "NEG": 0, "HARDSWISH": 0,
+                          "HARDSIGMOID": 0, "LEAKY_RELU": 0, "CLAMP": 0})
 
 
 def _key(bits):
@@ -192,11 +198,13 @@ def _key(bits):
     return torch.where(u < 0, -(u & 0x7FFFFFFF), u)
 
 
-@pytest.mark.parametrize("name", FLOAT_TRANSCENDENTALS)
-def test_float_transcendentals_every_input(rt, name):
+@pytest.mark.parametrize("name", sorted(EVERY_INPUT_BOUND))
+def test_unary_ops_every_input(rt, name):
     """Every one of the 2**32 float inputs (NaNs, infinities, denormals included) against PyTorch
-    CPU: at most 2 ulp (GELU: 8 |x| 2**-24 or 2 ulp), which proves the bound rather than sampling
-    it.  Chunks of 2**27 inputs: GPU result, PyTorch CPU result, compared on the GPU."""
+    CPU: transcendentals at most 2 ulp (GELU: 8 |x| 2**-24 or 2 ulp), sqrt 1 ulp, the exact ops
+    bit for bit, which proves the bound rather than sampling it.  Chunks of 2**27 inputs: GPU
+    result, PyTorch CPU result, compared on the GPU."""
+    bound = EVERY_INPUT_BOUND[name]
     op = EW[name]
     p0, p1 = PARAMS.get(name, (0.0, 0.0))
     chunk = 1 << 27
@@ -209,16 +217,20 @@ def test_float_transcendentals_every_input(rt, name):
         rt.flush(sync=True)
         ref = ew_torch(op, x, None, p0, p1).cuda()
         gn, rn = torch.isnan(od), torch.isnan(ref)
-        d = (_key(od.view(torch.int32)) - _key(ref.view(torch.int32))).abs()
+        if bound == 0:  # bit for bit: the raw patterns (a signed zero counts)
+            d = (od.view(torch.int32) != ref.view(torch.int32)).long()
+        else:
+            d = (_key(od.view(torch.int32)) - _key(ref.view(torch.int32))).abs()
         d = torch.where(gn & rn, torch.zeros_like(d), d)
         d = torch.where(gn ^ rn, torch.full_like(d, 1 << 40), d)
         if name == "GELU":
             close = ((od - ref).abs() <= xd.abs() * GELU_SLACK) & ~(gn ^ rn)
             d = torch.where(close, torch.zeros_like(d), d)
         m = int(d.max())
-        if m > MAX_ULP_F32:
+        if m > bound:
             i = int(d.argmax())
-            pytest.fail(f"{name}: {m} ulp at x={float(xd[i])!r}: got {float(od[i])!r}, PyTorch {float(ref[i])!r}")
+            pytest.fail(f"{name}: {m} (bound {bound}) at x={float(xd[i])!r}: got {float(od[i])!r}, "
+                        f"PyTorch {float(ref[i])!r}")
         worst = max(worst, m)
         del xd, ref, d, gn, rn
     STATS[f"{name}/every_input"] = worst
