@@ -14,6 +14,7 @@
 #include <Python.h>
 
 #include <ATen/core/Tensor.h>
+#include <ATen/ops/empty_like.h>
 #include <c10/cuda/CUDAStream.h>
 #include <torch/csrc/autograd/python_variable.h>
 
@@ -256,6 +257,53 @@ PyObject* py_submit_elementwise(PyObject*, PyObject* const* args, Py_ssize_t nar
   if (bt == 1) keep(dout, args[2]);
   keep(dout, args[3]);
   Py_RETURN_NONE;
+}
+
+// submit_ew_new(op, a, b_or_None_or_number) -> out: an element-wise request whose output is a new
+// contiguous tensor like `a` (same dtype, shape and device), allocated here.  The scheduler's
+// common case (operands of one dtype and shape) in one call: allocating from Python through the
+// dispatcher costs about as much as the rest of the dispatch.
+PyObject* py_submit_ew_new(PyObject*, PyObject* const* args, Py_ssize_t nargs) {
+  if (nargs != 3) {
+    PyErr_SetString(PyExc_TypeError, "expected (op, a, b)");
+    return nullptr;
+  }
+  const long op = PyLong_AsLong(args[0]);
+  if (op == -1 && PyErr_Occurred()) return nullptr;
+  if (!THPVariable_Check(args[1])) {
+    PyErr_SetString(PyExc_TypeError, "a must be a tensor");
+    return nullptr;
+  }
+  GpuosOperand a, b, out;
+  const int da = to_operand(args[1], &a, "a");
+  if (da < 0) return nullptr;
+  int b_scalar = 0;
+  double b_val = 0.0;
+  bool b_present = false;
+  const int bt = parse_b(args[2], &b, &b_scalar, &b_val, &b_present);
+  if (bt < 0) return nullptr;
+  PyObject* o = THPVariable_Wrap(at::empty_like(THPVariable_Unpack(args[1]), at::MemoryFormat::Contiguous));
+  if (!o) return nullptr;
+  const int dout = to_operand(o, &out, "out");
+  if (dout < 0) {
+    Py_DECREF(o);
+    return nullptr;
+  }
+  gpuos_rt* rt = rt_for(dout);
+  if (!rt) {
+    Py_DECREF(o);
+    return nullptr;
+  }
+  const float params[2] = {0.f, 0.f};
+  const int st = gpuos_rt_submit_ew(rt, (int)op, &a, bt == 1 ? &b : nullptr, b_scalar, b_val, &out, params, 2);
+  if (st) {
+    Py_DECREF(o);
+    return raise_status(st);
+  }
+  keep(dout, args[1]);
+  if (bt == 1) keep(dout, args[2]);
+  keep(dout, o);
+  return o;
 }
 
 bool parse_axes(PyObject* seq, std::vector<int>* axes) {
@@ -1263,6 +1311,8 @@ PyMethodDef kMethods[] = {
     {"submit_mul", (PyCFunction)(void (*)(void))py_submit_mul, METH_FASTCALL, "out = a * b (pending until flush)"},
     {"submit_sub", (PyCFunction)(void (*)(void))py_submit_sub, METH_FASTCALL, "out = a - b (pending until flush)"},
     {"submit_div", (PyCFunction)(void (*)(void))py_submit_div, METH_FASTCALL, "out = a / b (pending until flush)"},
+    {"submit_ew_new", (PyCFunction)(void (*)(void))py_submit_ew_new, METH_FASTCALL,
+     "submit_ew_new(op, a, b) -> out: element-wise request into a new contiguous tensor like a"},
     {"submit_elementwise", (PyCFunction)(void (*)(void))py_submit_elementwise, METH_FASTCALL,
      "submit_elementwise(op, a, b, out, p0=0.0, p1=0.0)"},
     {"submit_topk_rows", py_submit_topk_rows, METH_VARARGS,

@@ -99,6 +99,25 @@ class _Chain:
 
 _MAX_CHAIN = 16
 
+def _submit_new(op: int, a, b):
+    """Submit op(a[, b]) into a new contiguous tensor like a, allocated by the extension."""
+    return gpuos_ext.submit_ew_new(op, a, b)
+
+
+def _same_layout_operands(a, b, size_threshold: int) -> bool:
+    """Both CUDA tensors of one floating dtype, shape and device, contiguous, within the size
+    threshold."""
+    return (type(a) is torch.Tensor and type(b) is torch.Tensor and a.is_cuda and a.dtype is b.dtype
+            and a.dtype in _FLOATS and a.shape == b.shape and a.numel() <= size_threshold
+            and a.is_contiguous() and b.is_contiguous() and a.device == b.device)
+
+
+def _one_operand(x, size_threshold: int) -> bool:
+    """A CUDA tensor of a floating dtype within the size threshold and the rank limit."""
+    return (type(x) is torch.Tensor and x.is_cuda and x.dtype in _FLOATS and x.numel() <= size_threshold
+            and x.dim() <= 8)
+
+
 # op overload -> (route, name): 1 binary, 2 unary, 3 parametric unary, 4 reduction, 5 top-k,
 # 0 not ours
 _ROUTES: dict = {}
@@ -115,6 +134,13 @@ def _route(func):
 
 
 class _GPUOSSchedulerMode(TorchDispatchMode):
+    @classmethod
+    def _should_skip_dynamo(cls) -> bool:
+        # PyTorch otherwise wraps __torch_dispatch__ in a per-call guard that keeps torch.compile
+        # from tracing into it (about 3 us of every op's ~8.5 us here); nothing compiled runs
+        # through this mode
+        return False
+
     def __init__(self, *, size_threshold: int, auto_flush_ms: Optional[float], pending: Set[int]):
         super().__init__()
         self.size_threshold = size_threshold
@@ -440,6 +466,30 @@ class _GPUOSSchedulerMode(TorchDispatchMode):
 
     def __torch_dispatch__(self, func, types, args=(), kwargs=None):
         kind, name = _route(func)
+        # fast path: a tensor-tensor op with operands of one dtype, shape and device, both
+        # contiguous (the mixed-op stream's common case): no broadcasting, promotion or keyword
+        # handling
+        if kind == 1 and not kwargs and self.chain is None and not self.fuse and len(args) == 2:
+            a, b = args
+            if _same_layout_operands(a, b, self.size_threshold) and not torch.is_grad_enabled():
+                out = _submit_new(_BINARY[name], a, b)
+                pend = self.pending
+                pend.add(a.data_ptr() - a.storage_offset() * a.element_size())
+                pend.add(b.data_ptr() - b.storage_offset() * b.element_size())
+                pend.add(out.data_ptr())
+                self.scheduled += 1
+                self.scheduled_ops[name] += 1
+                return out
+        elif kind == 2 and not kwargs and self.chain is None and not self.fuse and len(args) == 1:
+            x = args[0]
+            if _one_operand(x, self.size_threshold) and not torch.is_grad_enabled():
+                out = _submit_new(_UNARY[name], x, None)
+                pend = self.pending
+                pend.add(x.data_ptr() - x.storage_offset() * x.element_size())
+                pend.add(out.data_ptr())
+                self.scheduled += 1
+                self.scheduled_ops[name] += 1
+                return out
         kwargs = kwargs or {}
         if self.chain is not None:
             res = self._try_extend(kind, name, args, kwargs) if kind in (1, 2, 3) else None
