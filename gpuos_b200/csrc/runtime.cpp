@@ -678,14 +678,29 @@ class HazardMap {
   }
   static bool box_overlap(const Range& box, const Range& r) { return !box.empty() && box.lo < r.hi && r.lo < box.hi; }
 
+  // A range already among the last entries of a block's chain (a write covers a read of the same
+  // range) is not added again: a tensor read by many requests of a segment would otherwise grow
+  // its blocks' chains by one entry per request, and every later query in those blocks would
+  // scan them (quadratic in the segment's requests).
+  bool recent(int32_t i, const Range& r, bool write) const {
+    for (int k = 0; i >= 0 && k < 8; ++k, i = pool_[i].next)
+      if (pool_[i].lo == r.lo && pool_[i].hi == r.hi && (pool_[i].write || !write)) return true;
+    return false;
+  }
+
   void index(const Range& r, bool write) {
     const uint64_t b0 = r.lo >> kShift, b1 = (r.hi - 1) >> kShift;
     if (b1 - b0 > kMaxBlocks) {
+      for (size_t k = large_.size(), n = 0; k > 0 && n < 8; --k, ++n) {
+        const Ent& e = large_[k - 1];
+        if (e.lo == r.lo && e.hi == r.hi && (e.write || !write)) return;
+      }
       large_.push_back(Ent{r.lo, r.hi, write, -1});
       return;
     }
     for (uint64_t blk = b0; blk <= b1; ++blk) {
       Slot* s = find_or_add(blk);
+      if (recent(s->head, r, write)) continue;
       pool_.push_back(Ent{r.lo, r.hi, write, s->head});
       s->head = (int32_t)pool_.size() - 1;
     }
