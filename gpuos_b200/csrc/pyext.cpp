@@ -259,13 +259,13 @@ PyObject* py_submit_elementwise(PyObject*, PyObject* const* args, Py_ssize_t nar
   Py_RETURN_NONE;
 }
 
-// submit_ew_new(op, a, b_or_None_or_number) -> out: an element-wise request whose output is a new
+// submit_ew_new(op, a, b_or_None_or_number[, p0[, p1]]) -> out: an element-wise request whose output is a new
 // contiguous tensor like `a` (same dtype, shape and device), allocated here.  The scheduler's
 // common case (operands of one dtype and shape) in one call: allocating from Python through the
 // dispatcher costs about as much as the rest of the dispatch.
 PyObject* py_submit_ew_new(PyObject*, PyObject* const* args, Py_ssize_t nargs) {
-  if (nargs != 3) {
-    PyErr_SetString(PyExc_TypeError, "expected (op, a, b)");
+  if (nargs < 3 || nargs > 5) {
+    PyErr_SetString(PyExc_TypeError, "expected (op, a, b[, p0[, p1]])");
     return nullptr;
   }
   const long op = PyLong_AsLong(args[0]);
@@ -294,7 +294,14 @@ PyObject* py_submit_ew_new(PyObject*, PyObject* const* args, Py_ssize_t nargs) {
     Py_DECREF(o);
     return nullptr;
   }
-  const float params[2] = {0.f, 0.f};
+  float params[2] = {0.f, 0.f};
+  for (int i = 0; i < 2 && 3 + i < nargs; ++i) {
+    params[i] = (float)PyFloat_AsDouble(args[3 + i]);
+    if (PyErr_Occurred()) {
+      Py_DECREF(o);
+      return nullptr;
+    }
+  }
   const int st = gpuos_rt_submit_ew(rt, (int)op, &a, bt == 1 ? &b : nullptr, b_scalar, b_val, &out, params, 2);
   if (st) {
     Py_DECREF(o);
@@ -1312,7 +1319,7 @@ PyMethodDef kMethods[] = {
     {"submit_sub", (PyCFunction)(void (*)(void))py_submit_sub, METH_FASTCALL, "out = a - b (pending until flush)"},
     {"submit_div", (PyCFunction)(void (*)(void))py_submit_div, METH_FASTCALL, "out = a / b (pending until flush)"},
     {"submit_ew_new", (PyCFunction)(void (*)(void))py_submit_ew_new, METH_FASTCALL,
-     "submit_ew_new(op, a, b) -> out: element-wise request into a new contiguous tensor like a"},
+     "submit_ew_new(op, a, b[, p0[, p1]]) -> out: element-wise request into a new contiguous tensor like a"},
     {"submit_elementwise", (PyCFunction)(void (*)(void))py_submit_elementwise, METH_FASTCALL,
      "submit_elementwise(op, a, b, out, p0=0.0, p1=0.0)"},
     {"submit_topk_rows", py_submit_topk_rows, METH_VARARGS,

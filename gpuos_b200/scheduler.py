@@ -480,6 +480,18 @@ class _GPUOSSchedulerMode(TorchDispatchMode):
                 self.scheduled += 1
                 self.scheduled_ops[name] += 1
                 return out
+        elif kind == 3 and self.chain is None and not self.fuse and args:
+            x = args[0]
+            if _one_operand(x, self.size_threshold) and not torch.is_grad_enabled():
+                code = self._parametric_code(name, args, kwargs or {})
+                if code is not None:
+                    out = gpuos_ext.submit_ew_new(code[0], x, None, code[1], code[2])
+                    pend = self.pending
+                    pend.add(x.data_ptr() - x.storage_offset() * x.element_size())
+                    pend.add(out.data_ptr())
+                    self.scheduled += 1
+                    self.scheduled_ops[name] += 1
+                    return out
         elif kind == 2 and not kwargs and self.chain is None and not self.fuse and len(args) == 1:
             x = args[0]
             if _one_operand(x, self.size_threshold) and not torch.is_grad_enabled():
