@@ -1,8 +1,8 @@
 """The config-5 pattern on one GPU: dependent chains of element-wise requests (each request
 reads the previous request's output of its chain, within a flush and across flushes) run
 while op slot 0 is switched online to multiply and then routed through the alias table and
-rolled back (test/online_switch.cpp, test/dual_slot_switch.cpp; BASELINE config 5 spreads the
-chains over 8 GPUs, one runtime each).  Probe Tasks through slot 0 in every phase must show
+rolled back (test/online_switch.cpp, test/dual_slot_switch.cpp; the full workload spreads the
+chains over up to 8 GPUs, one runtime each, in bench.py --workload c5).  Probe Tasks through slot 0 in every phase must show
 that phase's operator (no misdispatch) and every chain must end exactly at its PyTorch CPU
 value (no lost or reordered request)."""
 import pytest
