@@ -198,3 +198,22 @@ def test_inputs_from_kernels_queued_behind_a_full_worker(rt):
     finally:
         rt.shutdown()
         rt.init(capacity=8192, threads_per_block=256)
+
+
+def test_submit_ew_new_allocates_the_output(rt):
+    """submit_ew_new returns a new contiguous output like `a` holding op(a, b): a tensor or a
+    number as b, the two operator parameters, a non-contiguous a (the output is contiguous)."""
+    g = torch.Generator().manual_seed(21)
+    x = torch.randn(33, 257, generator=g)
+    y = torch.randn(33, 257, generator=g)
+    xd, yd = x.cuda(), y.cuda()
+    o1 = rt.submit_ew_new(rt.EW_MUL, xd, yd)
+    o2 = rt.submit_ew_new(rt.EW_ADD, xd, 0.5)
+    o3 = rt.submit_ew_new(rt.EW_LEAKY_RELU, xd, None, 0.2)
+    o4 = rt.submit_ew_new(rt.EW_CLAMP, xd.t(), None, -0.5, 0.25)
+    rt.flush(sync=True)
+    assert o4.is_contiguous() and o4.shape == (257, 33) and o1.dtype == torch.float32
+    assert same_bits(o1.cpu(), x * y)
+    assert same_bits(o2.cpu(), x + 0.5)
+    assert same_bits(o3.cpu(), torch.nn.functional.leaky_relu(x, 0.2))
+    assert same_bits(o4.cpu(), torch.clamp(x.t(), -0.5, 0.25))
