@@ -608,11 +608,15 @@ def c5_run(g, rank, world, barrier, chains=2048, depth=32, n=4096, n_probe=2, re
         fences = []
         phase = 0
         jit_addr = None
+        # per-request row views made before the timed region (indexing a tensor per request
+        # would cost the submit loop about as much as the submit itself)
+        rows = [list(Yd[k].unbind(0)) for k in range(depth + 1)]
+        yrows = [list(YG.unbind(0)), list(YP.unbind(0))]
         torch.cuda.synchronize()
         barrier()
         t0 = time.perf_counter()
         for k in range(depth):
-            row_in, row_out = Yd[k], Yd[k + 1]
+            row_in, row_out = rows[k], rows[k + 1]
             segs = [[]]
             for j, gi in plan[k]:
                 if phase + len(segs) - 1 < len(C5_SWITCH) and gi >= C5_SWITCH[phase + len(segs) - 1]:
@@ -638,7 +642,7 @@ def c5_run(g, rank, world, barrier, chains=2048, depth=32, n=4096, n_probe=2, re
                 ts = []
                 for j in seg:
                     kd = kl[j][k]
-                    y = (YP[j] if uses_p[kd] else YG[j]) if binary[kd] else None
+                    y = yrows[uses_p[kd]][j] if binary[kd] else None
                     ts.append(time.perf_counter_ns())
                     sub_ew(codes[kd], row_in[j], y, row_out[j], *params[kd])
                 for _ in range(n_probe if seg else 0):
