@@ -112,6 +112,17 @@ def _same_layout_operands(a, b, size_threshold: int) -> bool:
             and a.is_contiguous() and b.is_contiguous() and a.device == b.device)
 
 
+def _has_cuda_tensor(args, kwargs) -> bool:
+    """Whether a CUDA tensor is among the arguments (lists and tuples included)."""
+    def walk(o) -> bool:
+        if isinstance(o, torch.Tensor):
+            return o.is_cuda
+        if isinstance(o, (list, tuple)):
+            return any(walk(i) for i in o)
+        return False
+    return walk(args) or any(walk(v) for v in kwargs.values())
+
+
 def _one_operand(x, size_threshold: int) -> bool:
     """A CUDA tensor of a floating dtype within the size threshold and the rank limit."""
     return (type(x) is torch.Tensor and x.is_cuda and x.dtype in _FLOATS and x.numel() <= size_threshold
@@ -530,6 +541,12 @@ class _GPUOSSchedulerMode(TorchDispatchMode):
         # Not scheduled: make sure no pending request reads or writes what this op touches.
         if self._touches_pending(args, kwargs):
             self._sync_flush()
+        if not func.is_view and (self.pending or gpuos_ext.worker_alive()) and _has_cuda_tensor(args, kwargs):
+            # A kernel of this op may need SMs that the resident worker holds; left alone, the
+            # worker gives them back only at its idle stop (200 ms).  Finish the runtime's work and
+            # stop the worker now: the next flush relaunches it (tens of microseconds).
+            self._sync_flush()
+            gpuos_ext.quiesce()
         self.fallbacks += 1
         self.fallback_ops[name] += 1
         return func(*args, **kwargs)
