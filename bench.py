@@ -846,18 +846,20 @@ def run_config(args):
     }
     g.shutdown()
     if args.workload == "c2" and not args.no_extras:
-        line["scheduler_e2e"] = c2_scheduler(args, extra)
+        line["scheduler_e2e"] = c2_scheduler(args, extra, native=True)
+        line["scheduler_e2e_python_mode"] = c2_scheduler(args, extra, native=False)
     print(json.dumps(line), flush=True)
 
 
-def c2_scheduler(args, extra):
+def c2_scheduler(args, extra, native):
     """The same 16384 requests as PyTorch calls under scheduler_context(size_threshold=1<<15,
-    auto_flush_ms=2.0), then flush(sync=True): requests/s through the dispatch plugin."""
+    auto_flush_ms=2.0), then flush(sync=True): requests/s through the dispatch plugin (the C++
+    dispatcher intercept when `native`, else the Python dispatch mode)."""
     from gpuos_b200.scheduler import scheduler_context
     ops, kinds, X, Y, sizes, offs = (extra[k] for k in ("ops", "kinds", "X", "Y", "sizes", "offs"))
     calls = [(ops[kinds[k]][5], X[off:off + n], Y[off:off + n]) for k, (n, off) in enumerate(zip(sizes, offs))]
     times = []
-    with torch.no_grad(), scheduler_context(size_threshold=1 << 15, auto_flush_ms=2.0) as s:
+    with torch.no_grad(), scheduler_context(size_threshold=1 << 15, auto_flush_ms=2.0, native=native) as s:
         for _ in range(1 + max(1, args.steps // 4)):
             t0 = time.perf_counter()
             outs = [fn(x, y) for fn, x, y in calls]
@@ -868,6 +870,7 @@ def c2_scheduler(args, extra):
     dt = statistics.median(times[1:])
     return {"value": len(calls) / dt, "unit": UNIT, "ms_per_step": dt * 1e3,
             "scheduled": stats.get("scheduled"), "fallbacks": stats.get("fallbacks"),
+            "intercept": "C++ dispatcher fallback" if s.native else "Python dispatch mode",
             "what": "same requests as PyTorch calls under scheduler_context, host wall clock per pass"}
 
 

@@ -126,12 +126,13 @@ def _torch_flags() -> tuple[list[str], list[str]]:
 
 def _ext(force: bool, verbose: bool) -> str:
     src = os.path.join(CSRC, "pyext.cpp")
-    if force or _newer(EXT, [src, os.path.join(INCLUDE, "gpuos_b200.h"), LIB]):
+    icp = os.path.join(CSRC, "intercept.cpp")
+    if force or _newer(EXT, [src, icp, os.path.join(CSRC, "intercept.h"), os.path.join(INCLUDE, "gpuos_b200.h"), LIB]):
         cflags, lflags = _torch_flags()
         py_inc = sysconfig.get_paths()["include"]
         _run(["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-w",
-              "-I" + py_inc, "-I" + INCLUDE, "-I" + os.path.join(CUDA_HOME, "include"), *cflags,
-              src, "-o", EXT, "-L" + LIBDIR, "-lgpuos_b200", "-Wl,-rpath,$ORIGIN/lib", *lflags], verbose)
+              "-I" + py_inc, "-I" + INCLUDE, "-I" + CSRC, "-I" + os.path.join(CUDA_HOME, "include"), *cflags,
+              src, icp, "-o", EXT, "-L" + LIBDIR, "-lgpuos_b200", "-Wl,-rpath,$ORIGIN/lib", *lflags], verbose)
     return EXT
 
 

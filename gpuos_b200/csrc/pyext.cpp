@@ -29,10 +29,11 @@
 #include <vector>
 
 #include "gpuos_b200.h"
+#include "intercept.h"
 
 namespace {
 
-constexpr int kMaxDev = 64;
+constexpr int kMaxDev = gpuos_py::kMaxDev;
 
 struct DevRefs {
   std::vector<PyObject*> pending;
@@ -69,9 +70,10 @@ void drop_refs(std::vector<PyObject*>& v) {
 
 void release_completed(int dev) {
   gpuos_rt* rt = g_rt[dev];
+  const uint64_t done = rt ? gpuos_rt_completed(rt) : ~0ull;
+  gpuos_py::intercept_release(dev, done);  // tensors held by the dispatcher intercept's requests
   DevRefs& R = g_refs[dev];
   if (R.inflight.empty()) return;
-  const uint64_t done = rt ? gpuos_rt_completed(rt) : ~0ull;
   std::vector<PyObject*> dead;
   while (!R.inflight.empty() && R.inflight.front().first <= done) {
     auto& v = R.inflight.front().second;
@@ -82,6 +84,7 @@ void release_completed(int dev) {
 }
 
 void release_all(int dev) {
+  gpuos_py::intercept_release_all(dev);
   DevRefs& R = g_refs[dev];
   std::vector<PyObject*> dead;
   dead.swap(R.pending);
@@ -370,7 +373,8 @@ int flush_device(int dev, bool sync, uint64_t* seq_out) {
   if (!rt) return 0;
   cudaStream_t dep = c10::cuda::getCurrentCUDAStream((c10::DeviceIndex)dev).stream();
   uint64_t seq = 0;
-  int st = gpuos_rt_flush(rt, GPUOS_FLUSH_DEP, dep, &seq);
+  // through the intercept: its references are tied to this flush in the same step
+  int st = gpuos_py::intercept_flush(dev, rt, GPUOS_FLUSH_DEP, dep, &seq);
   if (st) return st;
   move_pending(dev, seq);
   if (sync && seq) {
@@ -649,6 +653,60 @@ PyObject* py_sync_enabled(PyObject*, PyObject*) {
   for (int d = 0; d < kMaxDev; ++d)
     if (g_rt[d]) Py_RETURN_TRUE;
   Py_RETURN_FALSE;
+}
+
+// ---- the dispatcher intercept of scheduler_context (intercept.cpp) ------------------------
+PyObject* py_intercept_enable(PyObject*, PyObject* args) {
+  long long thr;
+  if (!PyArg_ParseTuple(args, "L", &thr)) return nullptr;
+  std::string err;
+  bool ok = false;
+  try {
+    ok = gpuos_py::intercept_enable(thr, &err);
+  } catch (const std::exception& e) {
+    err = e.what();
+  }
+  if (!ok) return PyErr_Format(PyExc_RuntimeError, "intercept unavailable: %s", err.c_str());
+  Py_RETURN_NONE;
+}
+
+PyObject* py_intercept_disable(PyObject*, PyObject*) {
+  gpuos_py::intercept_disable();
+  Py_RETURN_NONE;
+}
+
+PyObject* py_intercept_enabled(PyObject*, PyObject*) { return PyBool_FromLong(gpuos_py::intercept_enabled()); }
+
+PyObject* py_intercept_clear_pending(PyObject*, PyObject*) {
+  gpuos_py::intercept_clear_pending();
+  Py_RETURN_NONE;
+}
+
+PyObject* counts_dict(const std::vector<std::pair<std::string, int64_t>>& v) {
+  PyObject* d = PyDict_New();
+  if (!d) return nullptr;
+  for (const auto& kv : v) {
+    PyObject* n = PyLong_FromLongLong(kv.second);
+    if (!n || PyDict_SetItemString(d, kv.first.c_str(), n) < 0) {
+      Py_XDECREF(n);
+      Py_DECREF(d);
+      return nullptr;
+    }
+    Py_DECREF(n);
+  }
+  return d;
+}
+
+PyObject* py_intercept_stats(PyObject*, PyObject*) {
+  const gpuos_py::InterceptStats s = gpuos_py::intercept_stats();
+  PyObject* so = counts_dict(s.scheduled_ops);
+  PyObject* fo = so ? counts_dict(s.fallback_ops) : nullptr;
+  if (!fo) {
+    Py_XDECREF(so);
+    return nullptr;
+  }
+  return Py_BuildValue("{s:L,s:L,s:N,s:N}", "scheduled", (long long)s.scheduled, "fallbacks", (long long)s.fallbacks,
+                       "scheduled_ops", so, "fallback_ops", fo);
 }
 
 PyObject* py_sync_wait(PyObject*, PyObject* args, PyObject* kw) {
@@ -1383,12 +1441,25 @@ PyMethodDef kMethods[] = {
     {"sync_wait", (PyCFunction)(void (*)(void))py_sync_wait, METH_VARARGS | METH_KEYWORDS,
      "sync_wait(target, timeout_ms=30000)"},
     {"sync_enabled", py_sync_enabled, METH_NOARGS, "zero-copy sync available"},
+    {"intercept_enable", py_intercept_enable, METH_VARARGS,
+     "intercept_enable(size_threshold): route this thread's ATen calls through the C++ scheduler intercept"},
+    {"intercept_disable", py_intercept_disable, METH_NOARGS, "stop intercepting this thread's ATen calls"},
+    {"intercept_enabled", py_intercept_enabled, METH_NOARGS, "whether this thread's ATen calls are intercepted"},
+    {"intercept_stats", py_intercept_stats, METH_NOARGS,
+     "intercept counters: scheduled, fallbacks, scheduled_ops, fallback_ops"},
+    {"intercept_clear_pending", py_intercept_clear_pending, METH_NOARGS,
+     "forget the intercept's pending storages (after a synchronous flush)"},
     {nullptr, nullptr, 0, nullptr}};
 
 PyModuleDef kModule = {PyModuleDef_HEAD_INIT, "_gpuos_ext", "B200 persistent micro-op runtime binding", -1,
                        kMethods};
 
 }  // namespace
+
+namespace gpuos_py {
+gpuos_rt* runtime(int dev) { return dev >= 0 && dev < kMaxDev ? g_rt[dev] : nullptr; }
+void busy_add(int dev, int delta) { g_busy[dev].fetch_add(delta); }
+}  // namespace gpuos_py
 
 PyMODINIT_FUNC PyInit__gpuos_ext(void) {
   PyObject* m = PyModule_Create(&kModule);

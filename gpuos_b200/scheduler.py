@@ -28,6 +28,10 @@ threads_per_block=256, size_threshold=1 << 16, auto_flush_ms=2.0)``, ``GPUOSSche
 * Operands: CUDA float32/float16/bfloat16 tensors (any strides, broadcast) or Python
   numbers; anything else (integer tensors, grad mode, CPU tensors, tensors above
   ``size_threshold`` elements) is left to PyTorch, as in the reference.
+* Two interchangeable intercepts (``native=``): the C++ one (a boxed fallback on a dispatcher
+  key included for the entering thread, csrc/intercept.cpp; the default) routes the same ops
+  by the same rules as the Python ``TorchDispatchMode`` below without a Python call per op.
+  Fusion (``GPUOS_SCHEDULER_DISABLE_JIT=0``) is built on the Python mode, which it then selects.
 """
 from __future__ import annotations
 
@@ -37,7 +41,6 @@ import math
 import os
 import struct
 import threading
-import time
 import weakref
 from typing import Any, Optional, Set
 
@@ -64,6 +67,9 @@ _UNARY = {
 _PARAMETRIC = {"aten::gelu", "aten::leaky_relu", "aten::hardtanh", "aten::elu", "aten::softplus",
                "aten::clamp", "aten::clamp_min", "aten::clamp_max"}
 _REDUCE = {"aten::sum.dim_IntList", "aten::mean.dim", "aten::sum", "aten::mean"}
+# allocations that launch no kernel (views are recognised by func.is_view)
+_NO_KERNEL = {"aten::empty.memory_format", "aten::empty_like", "aten::empty_strided", "aten::new_empty",
+              "aten::new_empty_strided"}
 
 
 def _storage_key(t: torch.Tensor) -> int:
@@ -144,6 +150,29 @@ def _route(func):
     return r
 
 
+class _AutoFlusher:
+    """Periodic asynchronous flush of pending requests (scheduler.py:40-51), for either intercept."""
+
+    def __init__(self, period_ms: Optional[float]):
+        self._stop = threading.Event()
+        self._bg: Optional[threading.Thread] = None
+        if period_ms and period_ms > 0:
+            self._bg = threading.Thread(target=self._run, args=(period_ms / 1000.0,), daemon=True)
+            self._bg.start()
+
+    def _run(self, period: float):
+        while not self._stop.wait(period):
+            try:
+                gpuos_ext.flush(sync=False)
+            except Exception:
+                pass
+
+    def close(self):
+        self._stop.set()
+        if self._bg:
+            self._bg.join(timeout=1.0)
+
+
 class _GPUOSSchedulerMode(TorchDispatchMode):
     @classmethod
     def _should_skip_dynamo(cls) -> bool:
@@ -164,29 +193,14 @@ class _GPUOSSchedulerMode(TorchDispatchMode):
         self.scheduled_ops: collections.Counter = collections.Counter()
         self.fallback_ops: collections.Counter = collections.Counter()
         # fusion (GPUOS_SCHEDULER_DISABLE_JIT=0): the chain being built, not yet submitted
-        self.fuse = os.environ.get("GPUOS_SCHEDULER_DISABLE_JIT", "1") in ("0", "false", "False")
+        self.fuse = _fusion_requested()
         self.chain: Optional[_Chain] = None
         self.fused_chains = 0
         self.fused_ops = 0
-        self._stop = False
-        self._bg: Optional[threading.Thread] = None
-        if auto_flush_ms and auto_flush_ms > 0:
-            self._bg = threading.Thread(target=self._flusher, daemon=True)
-            self._bg.start()
+        self._flusher = _AutoFlusher(auto_flush_ms)
 
     def close(self):
-        self._stop = True
-        if self._bg:
-            self._bg.join(timeout=1.0)
-
-    def _flusher(self):
-        # periodic asynchronous flush of pending requests (scheduler.py:40-51)
-        while not self._stop:
-            time.sleep(self.auto_flush_ms / 1000.0)
-            try:
-                gpuos_ext.flush(sync=False)
-            except Exception:
-                pass
+        self._flusher.close()
 
     # -- dependency tracking ----------------------------------------------------------
     def _touches_pending(self, args, kwargs) -> bool:
@@ -541,7 +555,8 @@ class _GPUOSSchedulerMode(TorchDispatchMode):
         # Not scheduled: make sure no pending request reads or writes what this op touches.
         if self._touches_pending(args, kwargs):
             self._sync_flush()
-        if not func.is_view and (self.pending or gpuos_ext.worker_alive()) and _has_cuda_tensor(args, kwargs):
+        if (not func.is_view and name not in _NO_KERNEL and (self.pending or gpuos_ext.worker_alive())
+                and _has_cuda_tensor(args, kwargs)):
             # A kernel of this op may need SMs that the resident worker holds; left alone, the
             # worker gives them back only at its idle stop (200 ms).  Finish the runtime's work and
             # stop the worker now: the next flush relaunches it (tens of microseconds).
@@ -553,21 +568,42 @@ class _GPUOSSchedulerMode(TorchDispatchMode):
 
 
 
+def _fusion_requested() -> bool:
+    return os.environ.get("GPUOS_SCHEDULER_DISABLE_JIT", "1") in ("0", "false", "False")
+
+
 class GPUOSScheduler:
+    """``native``: True routes ops through the C++ intercept, False through the Python
+    ``TorchDispatchMode``; None (default) takes the C++ one unless fusion is requested.  If the
+    C++ intercept cannot be enabled (its dispatcher key taken in this process) the Python mode
+    is used."""
+
     def __init__(self, *, capacity: int = 8192, threads_per_block: int = 256, size_threshold: int = 1 << 16,
-                 auto_flush_ms: Optional[float] = 2.0):
+                 auto_flush_ms: Optional[float] = 2.0, native: Optional[bool] = None):
         self.capacity = capacity
         self.threads_per_block = threads_per_block
         self.size_threshold = size_threshold
         self.auto_flush_ms = auto_flush_ms
+        if native and _fusion_requested():
+            raise ValueError("fusion (GPUOS_SCHEDULER_DISABLE_JIT=0) runs on the Python dispatch mode: native=False")
+        self.native = (not _fusion_requested()) if native is None else bool(native)
         self._mode: Optional[_GPUOSSchedulerMode] = None
+        self._flusher: Optional[_AutoFlusher] = None
         self._pending: Set[int] = set()
 
     def __enter__(self):
         gpuos_ext.init(self.capacity, self.threads_per_block)
-        self._mode = _GPUOSSchedulerMode(size_threshold=self.size_threshold, auto_flush_ms=self.auto_flush_ms,
-                                         pending=self._pending)
-        self._cm = self._mode.__enter__()
+        if self.native:
+            try:
+                gpuos_ext.intercept_enable(self.size_threshold)
+            except RuntimeError:
+                self.native = False
+        if self.native:
+            self._flusher = _AutoFlusher(self.auto_flush_ms)
+        else:
+            self._mode = _GPUOSSchedulerMode(size_threshold=self.size_threshold, auto_flush_ms=self.auto_flush_ms,
+                                             pending=self._pending)
+            self._cm = self._mode.__enter__()
         return self
 
     def flush(self, sync: bool = False):
@@ -576,11 +612,17 @@ class GPUOSScheduler:
         gpuos_ext.flush(sync=sync)
         if sync:
             self._pending.clear()
+            if self.native:
+                gpuos_ext.intercept_clear_pending()
 
     @property
     def stats(self):
         """Totals plus per-op counts: ``scheduled_ops`` / ``fallback_ops`` map an aten op name
         (``"aten::gelu"``) to the requests submitted to the runtime / the calls left to PyTorch."""
+        if self.native:
+            st = gpuos_ext.intercept_stats()
+            st.update(fused_chains=0, fused_ops=0)
+            return st
         m = self._mode
         return {"scheduled": m.scheduled if m else 0, "fallbacks": m.fallbacks if m else 0,
                 "scheduled_ops": dict(m.scheduled_ops) if m else {},
@@ -589,13 +631,19 @@ class GPUOSScheduler:
 
     def __exit__(self, exc_type, exc, tb):
         try:
-            if self._mode is not None:
+            if self.native:
+                if self._flusher is not None:
+                    self._flusher.close()
+                gpuos_ext.intercept_disable()
+            elif self._mode is not None:
                 self._mode.close()
                 self._mode.__exit__(exc_type, exc, tb)
                 self._mode.flush_fused()
         finally:
             gpuos_ext.flush(sync=True)
             self._pending.clear()
+            if self.native:
+                gpuos_ext.intercept_clear_pending()
             gpuos_ext.shutdown()
 
     def flush_fused(self):
@@ -605,8 +653,8 @@ class GPUOSScheduler:
 
 @contextlib.contextmanager
 def scheduler_context(*, capacity: int = 8192, threads_per_block: int = 256, size_threshold: int = 1 << 16,
-                      auto_flush_ms: Optional[float] = 2.0):
+                      auto_flush_ms: Optional[float] = 2.0, native: Optional[bool] = None):
     sched = GPUOSScheduler(capacity=capacity, threads_per_block=threads_per_block, size_threshold=size_threshold,
-                           auto_flush_ms=auto_flush_ms)
+                           auto_flush_ms=auto_flush_ms, native=native)
     with sched:
         yield sched

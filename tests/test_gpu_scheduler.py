@@ -1,7 +1,9 @@
 """scheduler_context on the GPU: the config-2 mixed-op stream, config-3 strided / broadcast /
 mixed-dtype pointwise and config-4 reductions go through the persistent runtime (no
 PyTorch fallback for in-scope ops) and match PyTorch CPU eager; dependencies between
-scheduled and unscheduled ops are honoured."""
+scheduled and unscheduled ops are honoured.  Every test runs through both intercepts: the C++
+dispatcher fallback (native, the default) and the Python dispatch mode."""
+import contextlib
 import math
 
 import pytest
@@ -13,12 +15,19 @@ from oracle.reference_semantics import same_bits, ulp_diff
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture()
-def sched(rt):
+@pytest.fixture(params=[True, False], ids=["native", "python"])
+def sched(rt, request):
     # scheduler_context initialises and shuts the runtime down itself
     rt.shutdown()
     from gpuos_b200.scheduler import scheduler_context
-    yield scheduler_context
+
+    @contextlib.contextmanager
+    def ctx(**kw):
+        with scheduler_context(native=request.param, **kw) as s:
+            assert s.native is request.param  # the intercept asked for is the one in use
+            yield s
+
+    yield ctx
     rt.init(capacity=8192, threads_per_block=256)
 
 
@@ -220,3 +229,62 @@ def test_dependencies_and_fallbacks(sched):
     assert torch.allclose(w.cpu(), zr.sum(), rtol=1e-5)
     assert torch.allclose(m.cpu(), zr @ zr, rtol=1e-4)
     assert same_bits(v.cpu(), (x * 2.0 + 1.0) + 1.0)
+
+
+def test_composite_parts_are_scheduled(sched):
+    """relu6 and hardtanh-based ops decompose into scheduled parts; chains of scheduled ops need
+    no flush in between."""
+    g = torch.Generator().manual_seed(21)
+    x = torch.randn(3, 700, generator=g) * 4
+    xd = x.cuda()
+    with torch.no_grad(), sched(auto_flush_ms=None) as s:
+        a = F.relu6(xd)
+        b = F.hardtanh(a * 0.5 - 1.0, -0.25, 0.75)
+        s.flush(sync=True)
+        st = s.stats
+    assert st["scheduled_ops"].get("aten::hardtanh") == 2
+    assert "aten::hardtanh" not in st["fallback_ops"]
+    assert same_bits(a.cpu(), F.relu6(x))
+    assert same_bits(b.cpu(), F.hardtanh(F.relu6(x) * 0.5 - 1.0, -0.25, 0.75))
+
+
+def test_grad_mode_leaves_ops_to_pytorch(sched):
+    """Forward ops with grad mode on are PyTorch's (autograd records them); the backward pass runs
+    with grad mode off, so its element-wise ops may be scheduled."""
+    g = torch.Generator().manual_seed(22)
+    x = torch.randn(1000, generator=g)
+    w = x.cuda().requires_grad_()
+    with sched(auto_flush_ms=None) as s:
+        y = torch.sigmoid(w) * 3.0
+        y.sum().backward()
+        s.flush(sync=True)
+        st = s.stats
+    assert st["fallback_ops"].get("aten::sigmoid") == 1
+    assert "aten::sigmoid" not in st["scheduled_ops"]
+    sg = torch.sigmoid(x)
+    assert torch.allclose(w.grad.cpu(), 3.0 * sg * (1 - sg), rtol=1e-5, atol=1e-7)
+
+
+def test_large_kernel_after_scheduled_ops(sched):
+    """An unscheduled kernel that needs the SMs runs after scheduled ops without waiting for
+    the worker's idle stop, and sees their results."""
+    import time
+    g = torch.Generator().manual_seed(23)
+    x = torch.randn(4096, generator=g)
+    w = torch.randn(2048, 2048, generator=g)
+    xd, wd = x.cuda(), w.cuda()
+    (wd @ wd).sum().item()   # cuBLAS set up before the timed loop
+    with torch.no_grad(), sched(auto_flush_ms=2.0) as s:
+        times = []
+        for _ in range(3):
+            y = torch.relu(xd * 2.0)
+            t0 = time.perf_counter()
+            m = wd @ wd
+            torch.cuda.synchronize()
+            times.append(time.perf_counter() - t0)
+            r = y[:2048] @ wd        # unscheduled, reads a scheduled result
+        s.flush(sync=True)
+    assert max(times) < 0.05, times    # the worker's idle stop is 200 ms
+    assert same_bits(y.cpu(), torch.relu(x * 2.0))
+    assert torch.allclose(m.cpu(), w @ w, rtol=1e-3, atol=1e-2)
+    assert torch.allclose(r.cpu(), torch.relu(x * 2.0)[:2048] @ w, rtol=1e-3, atol=1e-2)

@@ -89,14 +89,16 @@ def test_topk_rejects_bad_requests(rt):
         rt.submit_topk_rows(x.t(), v[:, :5].contiguous(), i[:, :5].contiguous(), 5, True)
 
 
-def test_scheduler_routes_topk(rt):
+@pytest.mark.parametrize("native", [True, False], ids=["native", "python"])
+def test_scheduler_routes_topk(rt, native):
     rt.shutdown()
     from gpuos_b200.scheduler import scheduler_context
     g = torch.Generator().manual_seed(7)
     x = distinct(32, 500, torch.float32, g)
     xd = x.cuda()
     try:
-        with torch.no_grad(), scheduler_context(size_threshold=1 << 16) as s:
+        with torch.no_grad(), scheduler_context(size_threshold=1 << 16, native=native) as s:
+            assert s.native is native
             before = s.stats["scheduled"]
             v, i = torch.topk(xd, 10)
             v2, i2 = torch.topk(xd * 2, 7, largest=False)

@@ -1,0 +1,111 @@
+"""The C++ dispatcher intercept of scheduler_context (csrc/intercept.cpp) without a GPU: with no
+runtime every op is left to PyTorch, results are PyTorch's own, the counters name ops as the
+Python dispatch mode does (an op PyTorch decomposes at the autograd level counts as its parts),
+only the entering thread is intercepted, and autograd still works underneath.
+Reference: pytorch_ext/scheduler.py:162-373 (the intercept), :399-466 (stats via the mode)."""
+import threading
+
+import torch
+import torch.nn.functional as F
+
+from gpuos_b200 import gpuos_ext as E
+
+
+def _run(fn):
+    E.intercept_enable(1 << 16)
+    try:
+        out = fn()
+        return out, E.intercept_stats()
+    finally:
+        E.intercept_disable()
+
+
+def test_cpu_ops_pass_through_and_are_counted():
+    x, y = torch.ones(5), torch.full((5,), 2.0)
+
+    def body():
+        with torch.no_grad():
+            return torch.relu(x + y)
+
+    w, st = _run(body)
+    assert torch.equal(w, torch.full((5,), 3.0))
+    assert st["scheduled"] == 0 and st["scheduled_ops"] == {}
+    assert st["fallback_ops"] == {"aten::add.Tensor": 1, "aten::relu": 1}
+    assert st["fallbacks"] == 2
+    assert not E.intercept_enabled()
+
+
+def test_composite_ops_count_as_their_parts():
+    """relu6 and linear decompose at the autograd level: the intercept sees hardtanh, t and mm,
+    as a dispatch mode below autograd does."""
+    g = torch.Generator().manual_seed(3)
+    x, w = torch.randn(4, 6, generator=g), torch.randn(3, 6, generator=g)
+
+    def body():
+        with torch.no_grad():
+            return F.relu6(x * 4), F.linear(x, w)
+
+    (a, b), st = _run(body)
+    assert torch.equal(a, F.relu6(x * 4)) and torch.allclose(b, x @ w.t())
+    ops = st["fallback_ops"]
+    assert ops.get("aten::hardtanh") == 1 and ops.get("aten::mul.Tensor") == 1
+    assert "aten::relu6" not in ops and "aten::linear" not in ops
+    assert ops.get("aten::t") == 1 and ops.get("aten::mm") == 1
+
+
+def test_enable_resets_the_counters():
+    x = torch.ones(3)
+    _run(lambda: x + x)
+    _, st = _run(lambda: x * x)
+    assert st["fallback_ops"] == {"aten::mul.Tensor": 1}
+
+
+def test_only_the_entering_thread_is_intercepted():
+    x = torch.ones(3)
+    seen = {}
+
+    def other():
+        seen["enabled"] = E.intercept_enabled()
+        seen["out"] = x - x
+
+    def body():
+        t = threading.Thread(target=other)
+        t.start()
+        t.join()
+        return x + x
+
+    out, st = _run(body)
+    assert seen["enabled"] is False and torch.equal(seen["out"], torch.zeros(3))
+    assert torch.equal(out, torch.full((3,), 2.0))
+    assert st["fallback_ops"] == {"aten::add.Tensor": 1}
+
+
+def test_autograd_runs_underneath():
+    """The key sits above autograd; with grad mode on nothing is scheduled and the graph is
+    recorded as usual."""
+    w = torch.tensor([1.0, -2.0, 3.0], requires_grad=True)
+
+    def body():
+        loss = (torch.tanh(w) * 2).sum()
+        loss.backward()
+        return loss.detach()
+
+    loss, st = _run(body)
+    assert torch.allclose(w.grad, 2 * (1 - torch.tanh(w.detach()) ** 2))
+    assert torch.allclose(loss, (torch.tanh(w.detach()) * 2).sum())
+    assert st["scheduled"] == 0 and st["fallback_ops"].get("aten::tanh") == 1
+
+
+def test_errors_of_the_op_reach_the_caller():
+    a, b = torch.ones(3), torch.ones(4)
+
+    def body():
+        try:
+            a + b
+        except RuntimeError as e:
+            return str(e)
+        return ""
+
+    msg, st = _run(body)
+    assert "size of tensor a (3)" in msg
+    assert st["fallback_ops"] == {"aten::add.Tensor": 1}
