@@ -119,7 +119,7 @@ def _torch_flags() -> tuple[list[str], list[str]]:
     libdir = ce.library_paths()[0]
     abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
     cflags = inc + [f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_API_INCLUDE_EXTENSION_H"]
-    lflags = [f"-L{libdir}", "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_python",
+    lflags = [f"-L{libdir}", "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-ltorch_python",
               f"-Wl,-rpath,{libdir}"]
     return cflags, lflags
 

@@ -31,8 +31,7 @@
 #include <ATen/core/Tensor.h>
 #include <ATen/core/dispatch/Dispatcher.h>
 #include <ATen/core/stack.h>
-#include <ATen/ops/empty.h>
-#include <ATen/ops/empty_like.h>
+#include <ATen/cuda/EmptyTensor.h>
 #include <ATen/ops/result_type.h>
 #include <c10/core/GradMode.h>
 #include <c10/core/impl/LocalDispatchKeySet.h>
@@ -218,6 +217,12 @@ bool cpu_scalar(const at::Tensor& t, double* v) {
   }
 }
 
+// A new contiguous CUDA tensor: the allocation at::empty's CUDA kernel makes (the caching
+// allocator on the current stream), without the dispatcher's hops to reach it.
+at::Tensor new_cuda(c10::IntArrayRef sizes, c10::ScalarType dt, c10::Device dev) {
+  return at::Tensor(at::detail::empty_cuda(sizes, dt, dev, at::MemoryFormat::Contiguous));
+}
+
 struct BusyGuard {
   int d;
   explicit BusyGuard(int dev) : d(dev) { busy_add(d, 1); }
@@ -330,11 +335,7 @@ bool try_binary(Route* r, c10::IValue* args, size_t nargs, torch::jit::Stack* st
     if (b.scalar_type() != dt) dt = at::result_type(a, b);
   }
   if (dtype_code(dt) < 0) return false;
-  at::Tensor out;
-  if (same_shape && dt == a.scalar_type() && a.is_contiguous())
-    out = at::empty_like(a, at::MemoryFormat::Contiguous);
-  else
-    out = at::empty(same_shape ? a.sizes() : c10::IntArrayRef(shape), a.options().dtype(dt));
+  at::Tensor out = new_cuda(same_shape ? a.sizes() : c10::IntArrayRef(shape), dt, a.device());
   if (!submit_ew(r, op, a, b_t ? &b : nullptr, !b_t, bv, out, (float)p0, 0.f)) return false;
   finish(stack, nargs, std::move(out));
   return true;
@@ -403,7 +404,7 @@ bool try_unary(Route* r, c10::IValue* args, size_t nargs, torch::jit::Stack* sta
   int op = r->code;
   double p0 = 0.0, p1 = 0.0;
   if (r->kind == K_PARAM && !param_code(r, args, nargs, &op, &p0, &p1)) return false;
-  at::Tensor out = at::empty_like(x, at::MemoryFormat::Contiguous);
+  at::Tensor out = new_cuda(x.sizes(), x.scalar_type(), x.device());
   if (!submit_ew(r, op, x, nullptr, false, 0.0, out, (float)p0, (float)p1)) return false;
   finish(stack, nargs, std::move(out));
   return true;
@@ -444,7 +445,7 @@ bool try_reduce(Route* r, c10::IValue* args, size_t nargs, torch::jit::Stack* st
     if (!reduced) shape.push_back(x.size(d));
     else if (keepdim) shape.push_back(1);
   }
-  at::Tensor out = at::empty(shape, x.options());
+  at::Tensor out = new_cuda(shape, x.scalar_type(), x.device());
   const int dev = x.get_device();
   if (dev < 0 || dev >= kMaxDev) return false;
   GpuosOperand X, O;
@@ -474,8 +475,8 @@ bool try_topk(Route* r, c10::IValue* args, size_t nargs, torch::jit::Stack* stac
   if (dim != x.dim() - 1 || k < 1 || k > std::min<int64_t>(n, 256)) return false;
   std::vector<int64_t> shape(x.sizes().begin(), x.sizes().end());
   shape.back() = k;
-  at::Tensor values = at::empty(shape, x.options());
-  at::Tensor indices = at::empty(shape, x.options().dtype(at::kLong));
+  at::Tensor values = new_cuda(shape, x.scalar_type(), x.device());
+  at::Tensor indices = new_cuda(shape, at::kLong, x.device());
   const int dev = x.get_device();
   if (dev < 0 || dev >= kMaxDev) return false;
   {
