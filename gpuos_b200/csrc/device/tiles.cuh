@@ -686,10 +686,14 @@ __device__ __forceinline__ void ew_2dt(const TileCtx& c) {
 
 // Rows of one item; every row is read by all 32 lanes of a warp on consecutive elements (no
 // bank conflicts on staged rows).  Rows of 128 elements or more: one row per warp step, four
-// partial sums per lane.  Shorter rows: four rows per warp step, one partial sum per lane and
-// row, the four rows' shuffle reductions interleaved.  The order of additions depends only
-// on C, so the result is deterministic.  Inlined in the compute loop (no call through the
-// tile table), loads specialised by dtype.
+// partial sums per lane; when the item has fewer rows than there are compute warps, each row
+// is split over wpr warps (the largest power of two with rows * wpr <= warps): part p of a
+// row takes its 128-element chunks p, p + wpr, ..., and the row's first warp adds the parts'
+// sums in order after a block barrier (items of one or two long rows otherwise left most
+// warps idle).  Shorter rows: four rows per warp step, one partial sum per lane and row, the
+// four rows' shuffle reductions interleaved.  The order of additions depends only on C and
+// the item's row count, so the result is deterministic.  Inlined in the compute loop (no call
+// through the tile table), loads specialised by dtype.
 __device__ __forceinline__ void row_reduce_body(const TileCtx& c) {
   const WorkItem& it = c.m->item;
   const uint32_t rows = it.count;
@@ -705,6 +709,39 @@ __device__ __forceinline__ void row_reduce_body(const TileCtx& c) {
   with_dtype(it.dt_a, [&](auto tag) {
     using T = decltype(tag);
     const T* X = reinterpret_cast<const T*>(base);
+    if (C >= 128 && rows * 2 <= nw) {
+      uint32_t lw = 1;  // log2 of the warps per row
+      while ((rows << (lw + 1)) <= nw && lw < 3) ++lw;
+      const uint32_t wpr = 1u << lw, r = warp >> lw, part = warp & (wpr - 1u);
+      // partial sums of the parts meet in the stage's descriptor extension, which nothing
+      // reads for a row-reduction item until the stage is handed back
+      float* parts = reinterpret_cast<float*>(const_cast<StageMeta*>(c.m)->ext.raw);
+      if (r < rows) {
+        const T* row = X + (int64_t)r * rs;
+        const int64_t step = (int64_t)128 << lw;
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+        int64_t j = (int64_t)part * 128 + lane;
+        for (; j + 96 < C; j += step) {
+          s0 = __fadd_rn(s0, to_f<T>(row[j * is]));
+          s1 = __fadd_rn(s1, to_f<T>(row[(j + 32) * is]));
+          s2 = __fadd_rn(s2, to_f<T>(row[(j + 64) * is]));
+          s3 = __fadd_rn(s3, to_f<T>(row[(j + 96) * is]));
+        }
+        // the rest of this part's last chunk (the next chunk of the part starts beyond C)
+        for (; j < C; j += 32) s0 = __fadd_rn(s0, to_f<T>(row[j * is]));
+        float s = __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+        if (lane == 0) parts[warp] = s;
+      }
+      ptx::named_bar_sync(kBarBlock, c.nt);
+      if (r < rows && part == 0 && lane == 0) {
+        float s = parts[warp];
+        for (uint32_t k = 1; k < wpr; ++k) s = __fadd_rn(s, parts[warp + k]);
+        st_elem(out, dto, r, mean ? __fdiv_rn(s, (float)C) : s);
+      }
+      return;
+    }
     if (C >= 128) {
       for (uint32_t r = warp; r < rows; r += nw) {
         const T* row = X + (int64_t)r * rs;
