@@ -7,6 +7,8 @@
 // copy, and the compute warps run one tile function reached through a device
 // function-pointer table (one indirect call per tile, not per element).
 #pragma once
+#include <type_traits>
+
 #include "ptx.cuh"
 #include "ops.cuh"
 
@@ -684,103 +686,148 @@ __device__ __forceinline__ void ew_2dt(const TileCtx& c) {
 
 // ---- reductions ------------------------------------------------------------------------
 
+// Elements of a row group, as float: staged rows by 32-bit shared-memory addresses (a group
+// never exceeds its stage), rows left in place by global pointers.
+template <typename T>
+struct StagedRows {
+  uint32_t base, rs, is;  // shared address of row 0; row and element strides in bytes
+  __device__ __forceinline__ float operator()(uint32_t r, int64_t j) const {
+    const uint32_t a = base + r * rs + (uint32_t)j * is;
+    if constexpr (sizeof(T) == 4) return ptx::ld_shared_f(a);
+    else if constexpr (std::is_same<T, __half>::value)
+      return __half2float(__ushort_as_half((unsigned short)ptx::ld_shared_u16(a)));
+    else return __uint_as_float(ptx::ld_shared_u16(a) << 16);
+  }
+};
+template <typename T>
+struct GlobalRows {
+  const T* X;
+  int64_t rs, is;  // in elements
+  __device__ __forceinline__ float operator()(uint32_t r, int64_t j) const { return to_f<T>(X[(int64_t)r * rs + j * is]); }
+};
+
+// One lane's sum over the 128-element chunks of row r that start at j - lane, j - lane + step,
+// ... below C: two chunks (eight loads) per step, then a last whole chunk, then the rest of
+// the last chunk (the chunk after it starts beyond C).  Four partial sums, added in an order
+// that depends only on C, step and the first chunk.
+template <typename L>
+__device__ __forceinline__ float chunk_sum(const L& ld, uint32_t r, int64_t j, int64_t C, int64_t step) {
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  for (; j + step + 96 < C; j += 2 * step) {
+    const float v0 = ld(r, j), v1 = ld(r, j + 32), v2 = ld(r, j + 64), v3 = ld(r, j + 96);
+    const float v4 = ld(r, j + step), v5 = ld(r, j + step + 32), v6 = ld(r, j + step + 64),
+                v7 = ld(r, j + step + 96);
+    s0 = __fadd_rn(__fadd_rn(s0, v0), v4);
+    s1 = __fadd_rn(__fadd_rn(s1, v1), v5);
+    s2 = __fadd_rn(__fadd_rn(s2, v2), v6);
+    s3 = __fadd_rn(__fadd_rn(s3, v3), v7);
+  }
+  if (j + 96 < C) {
+    const float v0 = ld(r, j), v1 = ld(r, j + 32), v2 = ld(r, j + 64), v3 = ld(r, j + 96);
+    s0 = __fadd_rn(s0, v0);
+    s1 = __fadd_rn(s1, v1);
+    s2 = __fadd_rn(s2, v2);
+    s3 = __fadd_rn(s3, v3);
+    j += step;
+  }
+  for (; j < C; j += 32) s0 = __fadd_rn(s0, ld(r, j));
+  return __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
+}
+
+__device__ __forceinline__ void row_store(void* out, int dto, uint32_t r, float s, bool mean, int64_t C) {
+  st_elem(out, dto, r, mean ? __fdiv_rn(s, (float)C) : s);
+}
+
 // Rows of one item; every row is read by all 32 lanes of a warp on consecutive elements (no
-// bank conflicts on staged rows).  Rows of 128 elements or more: one row per warp step, four
-// partial sums per lane; when the item has fewer rows than there are compute warps, each row
-// is split over wpr warps (the largest power of two with rows * wpr <= warps): part p of a
-// row takes its 128-element chunks p, p + wpr, ..., and the row's first warp adds the parts'
-// sums in order after a block barrier (items of one or two long rows otherwise left most
-// warps idle).  Shorter rows: four rows per warp step, one partial sum per lane and row, the
-// four rows' shuffle reductions interleaved.  The order of additions depends only on C and
-// the item's row count, so the result is deterministic.  Inlined in the compute loop (no call
-// through the tile table), loads specialised by dtype.
+// bank conflicts on staged rows).  Rows of 128 elements or more: a warp takes two rows per
+// step, eight loads in flight per lane and the two rows' shuffle reductions interleaved; when
+// the item has fewer rows than there are compute warps, each row is split over wpr warps (the
+// largest power of two with rows * wpr <= warps): part p of a row takes its 128-element chunks
+// p, p + wpr, ..., and the row's first warp adds the parts' sums in order after a block
+// barrier.  Shorter rows: four rows per warp step, one partial sum per lane and row, the four
+// rows' shuffle reductions interleaved.  The order of additions depends only on C and the
+// item's row count, so the result is deterministic.  Inlined in the compute loop (no call
+// through the tile table), loads specialised by dtype and by where the rows are.
+template <typename L>
+__device__ __forceinline__ void row_reduce_rows(const TileCtx& c, const L& ld, uint32_t rows, int64_t C, bool mean,
+                                                void* out, int dto) {
+  const uint32_t warp = c.tid >> 5, lane = c.tid & 31, nw = c.nt >> 5;
+  if (C >= 128 && rows * 2 <= nw) {
+    uint32_t lw = 1;  // log2 of the warps per row
+    while ((rows << (lw + 1)) <= nw && lw < 3) ++lw;
+    const uint32_t wpr = 1u << lw, r = warp >> lw, part = warp & (wpr - 1u);
+    // partial sums of the parts meet in the stage's descriptor extension, which nothing
+    // reads for a row-reduction item until the stage is handed back
+    float* parts = reinterpret_cast<float*>(const_cast<StageMeta*>(c.m)->ext.raw);
+    if (r < rows) {
+      float s = chunk_sum(ld, r, (int64_t)part * 128 + lane, C, (int64_t)128 << lw);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+      if (lane == 0) parts[warp] = s;
+    }
+    ptx::named_bar_sync(kBarBlock, c.nt);
+    if (r < rows && part == 0 && lane == 0) {
+      float s = parts[warp];
+      for (uint32_t k = 1; k < wpr; ++k) s = __fadd_rn(s, parts[warp + k]);
+      row_store(out, dto, r, s, mean, C);
+    }
+    return;
+  }
+  if (C >= 128) {
+    for (uint32_t r = warp; r < rows; r += 2 * nw) {
+      const uint32_t r2 = r + nw;
+      float a = chunk_sum(ld, r, lane, C, 128);
+      float b = r2 < rows ? chunk_sum(ld, r2, lane, C, 128) : 0.f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
+        b = __fadd_rn(b, __shfl_xor_sync(0xffffffffu, b, o));
+      }
+      if (lane == 0) row_store(out, dto, r, a, mean, C);
+      if (lane == 1 && r2 < rows) row_store(out, dto, r2, b, mean, C);
+    }
+    return;
+  }
+  const int32_t c32 = (int32_t)C;
+  for (uint32_t rb = warp * 4; rb < rows; rb += nw * 4) {
+    float s[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      s[q] = 0.f;
+      if (rb + q < rows)
+        for (int32_t j = lane; j < c32; j += 32) s[q] = __fadd_rn(s[q], ld(rb + q, j));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) s[q] = __fadd_rn(s[q], __shfl_xor_sync(0xffffffffu, s[q], o));
+    }
+    if (lane < 4 && rb + lane < rows) {
+      const float v = lane == 0 ? s[0] : lane == 1 ? s[1] : lane == 2 ? s[2] : s[3];
+      row_store(out, dto, rb + lane, v, mean, C);
+    }
+  }
+}
+
 __device__ __forceinline__ void row_reduce_body(const TileCtx& c) {
   const WorkItem& it = c.m->item;
   const uint32_t rows = it.count;
   const int64_t C = it.aux;
   const int64_t rs = (int64_t)it.x;
   const int64_t is = (int64_t)it.b;
-  const unsigned char* base =
-      (c.m->staged & 1) ? c.sa + c.m->a_off : reinterpret_cast<const unsigned char*>(it.a);
-  const uint32_t warp = c.tid >> 5, lane = c.tid & 31, nw = c.nt >> 5;
   const bool mean = (it.flags & IF_MEAN) != 0;
   void* out = reinterpret_cast<void*>(it.o);
   const int dto = it.dt_o;
+  const bool staged = (c.m->staged & 1) != 0;
   with_dtype(it.dt_a, [&](auto tag) {
     using T = decltype(tag);
-    const T* X = reinterpret_cast<const T*>(base);
-    if (C >= 128 && rows * 2 <= nw) {
-      uint32_t lw = 1;  // log2 of the warps per row
-      while ((rows << (lw + 1)) <= nw && lw < 3) ++lw;
-      const uint32_t wpr = 1u << lw, r = warp >> lw, part = warp & (wpr - 1u);
-      // partial sums of the parts meet in the stage's descriptor extension, which nothing
-      // reads for a row-reduction item until the stage is handed back
-      float* parts = reinterpret_cast<float*>(const_cast<StageMeta*>(c.m)->ext.raw);
-      if (r < rows) {
-        const T* row = X + (int64_t)r * rs;
-        const int64_t step = (int64_t)128 << lw;
-        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-        int64_t j = (int64_t)part * 128 + lane;
-        for (; j + 96 < C; j += step) {
-          s0 = __fadd_rn(s0, to_f<T>(row[j * is]));
-          s1 = __fadd_rn(s1, to_f<T>(row[(j + 32) * is]));
-          s2 = __fadd_rn(s2, to_f<T>(row[(j + 64) * is]));
-          s3 = __fadd_rn(s3, to_f<T>(row[(j + 96) * is]));
-        }
-        // the rest of this part's last chunk (the next chunk of the part starts beyond C)
-        for (; j < C; j += 32) s0 = __fadd_rn(s0, to_f<T>(row[j * is]));
-        float s = __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
-        if (lane == 0) parts[warp] = s;
-      }
-      ptx::named_bar_sync(kBarBlock, c.nt);
-      if (r < rows && part == 0 && lane == 0) {
-        float s = parts[warp];
-        for (uint32_t k = 1; k < wpr; ++k) s = __fadd_rn(s, parts[warp + k]);
-        st_elem(out, dto, r, mean ? __fdiv_rn(s, (float)C) : s);
-      }
-      return;
-    }
-    if (C >= 128) {
-      for (uint32_t r = warp; r < rows; r += nw) {
-        const T* row = X + (int64_t)r * rs;
-        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-        int64_t j = lane;
-        for (; j + 96 < C; j += 128) {
-          s0 = __fadd_rn(s0, to_f<T>(row[j * is]));
-          s1 = __fadd_rn(s1, to_f<T>(row[(j + 32) * is]));
-          s2 = __fadd_rn(s2, to_f<T>(row[(j + 64) * is]));
-          s3 = __fadd_rn(s3, to_f<T>(row[(j + 96) * is]));
-        }
-        for (; j < C; j += 32) s0 = __fadd_rn(s0, to_f<T>(row[j * is]));
-        float s = __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
-        if (lane == 0) st_elem(out, dto, r, mean ? __fdiv_rn(s, (float)C) : s);
-      }
-      return;
-    }
-    const int32_t c32 = (int32_t)C, is32 = (int32_t)is;
-    for (uint32_t rb = warp * 4; rb < rows; rb += nw * 4) {
-      float s[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        s[q] = 0.f;
-        if (rb + q < rows) {
-          const T* row = X + (int64_t)(rb + q) * rs;
-          for (int32_t j = lane; j < c32; j += 32) s[q] = __fadd_rn(s[q], to_f<T>(row[j * is32]));
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) s[q] = __fadd_rn(s[q], __shfl_xor_sync(0xffffffffu, s[q], o));
-      }
-      if (lane < 4 && rb + lane < rows) {
-        const float v = lane == 0 ? s[0] : lane == 1 ? s[1] : lane == 2 ? s[2] : s[3];
-        st_elem(out, dto, rb + lane, mean ? __fdiv_rn(v, (float)C) : v);
-      }
+    if (staged) {
+      const StagedRows<T> ld{ptx::smem_addr(c.sa) + c.m->a_off, (uint32_t)(rs * (int64_t)sizeof(T)),
+                             (uint32_t)(is * (int64_t)sizeof(T))};
+      row_reduce_rows(c, ld, rows, C, mean, out, dto);
+    } else {
+      const GlobalRows<T> ld{reinterpret_cast<const T*>(it.a), rs, is};
+      row_reduce_rows(c, ld, rows, C, mean, out, dto);
     }
   });
 }
