@@ -79,7 +79,7 @@ std::atomic<int64_t> g_threshold{int64_t(1) << 16};
 torch::Library* g_lib = nullptr;
 
 // Same tables as the Python mode (gpuos_b200/scheduler.py _BINARY/_UNARY/_PARAMETRIC/_REDUCE).
-void classify(Route* r) {
+const std::unordered_map<std::string, std::pair<Kind, int>>& route_table() {
   static const std::unordered_map<std::string, std::pair<Kind, int>> table = {
       {"aten::add.Tensor", {K_BINARY, GPUOS_EW_ADD}},
       {"aten::sub.Tensor", {K_BINARY, GPUOS_EW_SUB}},
@@ -115,6 +115,11 @@ void classify(Route* r) {
       {"aten::mean", {K_REDUCE, GPUOS_RED_MEAN}},
       {"aten::topk", {K_TOPK, 0}},
   };
+  return table;
+}
+
+void classify(Route* r) {
+  const auto& table = route_table();
   // allocations that launch no kernel (views are recognised from the schema)
   static const std::unordered_set<std::string> alloc = {
       "aten::empty.memory_format", "aten::empty_like", "aten::empty_strided", "aten::new_empty",
@@ -634,6 +639,12 @@ InterceptStats intercept_stats() {
     if (kv.second->fallbacks) s.fallback_ops.emplace_back(kv.second->name, kv.second->fallbacks);
   }
   return s;
+}
+
+std::vector<std::pair<std::string, std::pair<int, int>>> intercept_routes() {
+  std::vector<std::pair<std::string, std::pair<int, int>>> v;
+  for (const auto& kv : route_table()) v.emplace_back(kv.first, std::make_pair((int)kv.second.first, kv.second.second));
+  return v;
 }
 
 void intercept_clear_pending() {

@@ -34,6 +34,9 @@ bool intercept_enable(int64_t size_threshold, std::string* err);
 void intercept_disable();
 bool intercept_enabled();
 InterceptStats intercept_stats();
+// The routing table: aten op name -> (kind: 1 binary, 2 unary, 3 parametric unary, 4 reduction,
+// 5 top-k; element-wise or reduction op code).
+std::vector<std::pair<std::string, std::pair<int, int>>> intercept_routes();
 // Forget the storages of pending requests (after a synchronous flush of every device).
 void intercept_clear_pending();
 

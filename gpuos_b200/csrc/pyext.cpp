@@ -697,6 +697,21 @@ PyObject* counts_dict(const std::vector<std::pair<std::string, int64_t>>& v) {
   return d;
 }
 
+PyObject* py_intercept_routes(PyObject*, PyObject*) {
+  PyObject* d = PyDict_New();
+  if (!d) return nullptr;
+  for (const auto& kv : gpuos_py::intercept_routes()) {
+    PyObject* v = Py_BuildValue("(ii)", kv.second.first, kv.second.second);
+    if (!v || PyDict_SetItemString(d, kv.first.c_str(), v) < 0) {
+      Py_XDECREF(v);
+      Py_DECREF(d);
+      return nullptr;
+    }
+    Py_DECREF(v);
+  }
+  return d;
+}
+
 PyObject* py_intercept_stats(PyObject*, PyObject*) {
   const gpuos_py::InterceptStats s = gpuos_py::intercept_stats();
   PyObject* so = counts_dict(s.scheduled_ops);
@@ -1447,6 +1462,8 @@ PyMethodDef kMethods[] = {
     {"intercept_enabled", py_intercept_enabled, METH_NOARGS, "whether this thread's ATen calls are intercepted"},
     {"intercept_stats", py_intercept_stats, METH_NOARGS,
      "intercept counters: scheduled, fallbacks, scheduled_ops, fallback_ops"},
+    {"intercept_routes", py_intercept_routes, METH_NOARGS,
+     "the intercept's routing table: aten op name -> (kind, op code)"},
     {"intercept_clear_pending", py_intercept_clear_pending, METH_NOARGS,
      "forget the intercept's pending storages (after a synchronous flush)"},
     {nullptr, nullptr, 0, nullptr}};

@@ -109,3 +109,20 @@ def test_errors_of_the_op_reach_the_caller():
     msg, st = _run(body)
     assert "size of tensor a (3)" in msg
     assert st["fallback_ops"] == {"aten::add.Tensor": 1}
+
+
+def test_routes_match_the_python_mode():
+    """The C++ intercept routes exactly the ops the Python dispatch mode routes, to the same
+    runtime operators (kinds: 1 binary, 2 unary, 3 parametric unary, 4 reduction, 5 top-k)."""
+    from gpuos_b200 import scheduler as S
+    want = {}
+    for name, op in S._BINARY.items():
+        want[name] = (1, op)
+    for name, op in S._UNARY.items():
+        want[name] = (2, op)
+    for name in S._PARAMETRIC:
+        want[name] = (3, 0)
+    for name in S._REDUCE:
+        want[name] = (4, E.RED_MEAN if "mean" in name else E.RED_SUM)
+    want["aten::topk"] = (5, 0)
+    assert E.intercept_routes() == want
