@@ -126,3 +126,54 @@ def test_routes_match_the_python_mode():
         want[name] = (4, E.RED_MEAN if "mean" in name else E.RED_SUM)
     want["aten::topk"] = (5, 0)
     assert E.intercept_routes() == want
+
+
+def test_models_and_ops_of_every_argument_kind_pass_through():
+    """Tensor lists, optional-tensor lists (indexing), tuple returns, in-place writes, views and
+    a small convolutional model give PyTorch's own results with the intercept on; so does a
+    training step (grad mode on: nothing is scheduled, autograd records as usual)."""
+    import torch.nn as nn
+
+    torch.manual_seed(0)
+    model = nn.Sequential(nn.Conv2d(3, 8, 3, padding=1), nn.BatchNorm2d(8), nn.ReLU(), nn.Flatten(),
+                          nn.Linear(8 * 8 * 8, 16), nn.LayerNorm(16), nn.GELU(), nn.Linear(16, 4)).eval()
+    x = torch.randn(2, 3, 8, 8)
+
+    def work():
+        with torch.no_grad():
+            y = model(x)
+            z = x[torch.tensor([0, 1]), :, None, 1:5]
+            c = torch.cat([y, y * 2], dim=1)
+            s = torch.softmax(c, -1)
+            v, i = torch.sort(s, dim=-1)
+            a = torch.where(s > 0.1, s, torch.zeros_like(s))
+            q = s.clone()
+            q.add_(1.0)
+            q[0, 0] = 5.0
+            u = torch.stack(torch.chunk(c, 2, dim=1))
+            m = torch.einsum("ij,kj->ik", y, y)
+        return [y, z, c, s, v, i, a, q, u, m]
+
+    ref = work()
+    got, st = _run(work)
+    assert all(torch.equal(r, g) for r, g in zip(ref, got))
+    assert st["scheduled"] == 0 and st["fallback_ops"]["aten::index.Tensor"] == 1
+
+    def train(intercept):
+        torch.manual_seed(1)
+        lin = nn.Linear(5, 3)
+        opt = torch.optim.SGD(lin.parameters(), lr=0.1)
+        xb = torch.randn(4, 5)
+
+        def step():
+            loss = F.mse_loss(lin(xb), torch.ones(4, 3))
+            opt.zero_grad()
+            loss.backward()
+            opt.step()
+
+        _run(step) if intercept else step()
+        return lin.weight.detach().clone(), lin.bias.detach().clone()
+
+    w0, b0 = train(False)
+    w1, b1 = train(True)
+    assert torch.equal(w0, w1) and torch.equal(b0, b1)
