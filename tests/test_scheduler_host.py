@@ -73,3 +73,21 @@ def test_cpu_tensors_fall_back_and_are_counted():
     assert m.fallback_ops == {"aten::add.Tensor": 1, "aten::relu": 1}
     assert m.scheduled == 0
     m.close()
+
+
+def test_auto_flusher_runs_and_stops(monkeypatch):
+    """The periodic asynchronous flush shared by both intercepts (scheduler.py:40-51): it calls
+    flush(sync=False) every period and stops within one period of close()."""
+    import time
+    calls = []
+    monkeypatch.setattr(S.gpuos_ext, "flush", lambda sync=False: calls.append(sync))
+    f = S._AutoFlusher(5.0)
+    time.sleep(0.08)
+    t0 = time.perf_counter()
+    f.close()
+    assert time.perf_counter() - t0 < 0.5
+    n = len(calls)
+    assert n >= 3 and not any(calls)
+    time.sleep(0.03)
+    assert len(calls) == n
+    assert S._AutoFlusher(None)._bg is None and S._AutoFlusher(0)._bg is None
