@@ -41,6 +41,7 @@ import math
 import os
 import struct
 import threading
+import warnings
 import weakref
 from typing import Any, Optional, Set
 
@@ -596,7 +597,8 @@ class GPUOSScheduler:
         if self.native:
             try:
                 gpuos_ext.intercept_enable(self.size_threshold)
-            except RuntimeError:
+            except RuntimeError as e:
+                warnings.warn(f"scheduler_context: {e}; using the Python dispatch mode", RuntimeWarning)
                 self.native = False
         if self.native:
             self._flusher = _AutoFlusher(self.auto_flush_ms)

@@ -91,3 +91,25 @@ def test_auto_flusher_runs_and_stops(monkeypatch):
     time.sleep(0.03)
     assert len(calls) == n
     assert S._AutoFlusher(None)._bg is None and S._AutoFlusher(0)._bg is None
+
+
+def test_python_mode_when_the_intercept_is_unavailable(monkeypatch):
+    """If the C++ intercept cannot be enabled, the context warns and routes through the Python
+    dispatch mode (runtime calls stubbed: no device is touched)."""
+    import pytest
+    for name in ("init", "shutdown"):
+        monkeypatch.setattr(S.gpuos_ext, name, lambda *a, **k: None)
+    monkeypatch.setattr(S.gpuos_ext, "flush", lambda sync=False: 0)
+
+    def taken(_):
+        raise RuntimeError("intercept unavailable: the dispatcher key already has a fallback")
+
+    monkeypatch.setattr(S.gpuos_ext, "intercept_enable", taken)
+    x = torch.ones(3)
+    with pytest.warns(RuntimeWarning, match="Python dispatch mode"):
+        with S.scheduler_context(auto_flush_ms=None) as s:
+            assert s.native is False
+            z = x + x
+            st = s.stats
+    assert torch.equal(z, torch.full((3,), 2.0))
+    assert st["fallback_ops"] == {"aten::add.Tensor": 1}
