@@ -113,3 +113,27 @@ def test_python_mode_when_the_intercept_is_unavailable(monkeypatch):
             st = s.stats
     assert torch.equal(z, torch.full((3,), 2.0))
     assert st["fallback_ops"] == {"aten::add.Tensor": 1}
+
+
+def test_native_context_lifecycle(monkeypatch):
+    """The C++ intercept is on exactly inside the context (also when the body raises), its
+    counters are the context's stats, and the runtime calls happen in order (stubbed here)."""
+    import pytest
+    calls = []
+    monkeypatch.setattr(S.gpuos_ext, "init", lambda *a, **k: calls.append("init"))
+    monkeypatch.setattr(S.gpuos_ext, "shutdown", lambda *a, **k: calls.append("shutdown"))
+    monkeypatch.setattr(S.gpuos_ext, "flush", lambda sync=False: calls.append(("flush", sync)) or 0)
+    x = torch.ones(4)
+    with S.scheduler_context(auto_flush_ms=None, native=True) as s:
+        assert s.native is True and E.intercept_enabled()
+        y = torch.relu(x * 2.0)
+        st = s.stats
+    assert not E.intercept_enabled()
+    assert torch.equal(y, torch.full((4,), 2.0))
+    assert st["scheduled"] == 0 and st["fallback_ops"] == {"aten::mul.Tensor": 1, "aten::relu": 1}
+    assert st["fused_chains"] == 0
+    assert calls == ["init", ("flush", True), "shutdown"]
+    with pytest.raises(ValueError, match="boom"):
+        with S.scheduler_context(auto_flush_ms=None, native=True):
+            raise ValueError("boom")
+    assert not E.intercept_enabled()
