@@ -177,3 +177,34 @@ def test_models_and_ops_of_every_argument_kind_pass_through():
     w0, b0 = train(False)
     w1, b1 = train(True)
     assert torch.equal(w0, w1) and torch.equal(b0, b1)
+
+
+def test_other_dispatch_modes_and_autocast_still_work():
+    """A user's TorchDispatchMode (as profilers and tracers use) still sees every op under the
+    intercept, and CPU autocast still changes the dtype: calls with those keys are not plain
+    dense ones, so they pass through unchanged."""
+    from torch.utils._python_dispatch import TorchDispatchMode
+
+    class Count(TorchDispatchMode):
+        def __init__(self):
+            super().__init__()
+            self.names = []
+
+        def __torch_dispatch__(self, func, types, args=(), kwargs=None):
+            self.names.append(func.name())
+            return func(*args, **(kwargs or {}))
+
+    x = torch.randn(8, 8)
+
+    def body():
+        with Count() as m:
+            y = torch.relu(x) + 1.0
+        with torch.autocast("cpu", dtype=torch.bfloat16):
+            z = x @ x
+        return m.names, y, z
+
+    (names, y, z), st = _run(body)
+    assert names == ["aten::relu", "aten::add.Tensor"]
+    assert torch.equal(y, torch.relu(x) + 1.0)
+    assert z.dtype == torch.bfloat16
+    assert st["scheduled"] == 0
