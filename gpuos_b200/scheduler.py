@@ -1,5 +1,6 @@
-"""scheduler_context — TorchDispatchMode plugin that routes small pointwise and reduction
-ops to the persistent runtime (the reference's pytorch_ext/scheduler.py API).
+"""scheduler_context — the PyTorch plugin that routes small pointwise and reduction ops to the
+persistent runtime (the reference's pytorch_ext/scheduler.py API), intercepting ATen calls in
+C++ (default) or in a TorchDispatchMode.
 
 Same public surface as the reference: ``scheduler_context(*, capacity=8192,
 threads_per_block=256, size_threshold=1 << 16, auto_flush_ms=2.0)``, ``GPUOSScheduler`` and
@@ -21,7 +22,9 @@ threads_per_block=256, size_threshold=1 << 16, auto_flush_ms=2.0)``, ``GPUOSSche
   (inside and across flushes), so chains of scheduled ops need no flush.  Any op that is
   not scheduled and touches memory a pending request reads or writes triggers a sync
   flush first (the reference only tracked outputs, and skipped "fusible" ops, so a chain
-  of pending adds never flushed, scheduler.py:53-98).
+  of pending adds never flushed, scheduler.py:53-98).  An op that is not scheduled and launches
+  a kernel on CUDA tensors also stops the resident worker first, which would otherwise hold
+  every SM until its idle stop.
 * Semantics follow PyTorch: alpha of add/sub, positional clamp bounds (scheduler.py:270
   read kwargs only), NaN-propagating maximum/minimum, erf GELU, expm1 ELU, softplus
   threshold.
@@ -577,7 +580,7 @@ class GPUOSScheduler:
     """``native``: True routes ops through the C++ intercept, False through the Python
     ``TorchDispatchMode``; None (default) takes the C++ one unless fusion is requested.  If the
     C++ intercept cannot be enabled (its dispatcher key taken in this process) the Python mode
-    is used."""
+    is used and a RuntimeWarning says so."""
 
     def __init__(self, *, capacity: int = 8192, threads_per_block: int = 256, size_threshold: int = 1 << 16,
                  auto_flush_ms: Optional[float] = 2.0, native: Optional[bool] = None):
